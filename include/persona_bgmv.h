@@ -1,0 +1,119 @@
+/*
+ * persona_bgmv.h -- C ABI of the B200 (sm_100a) multi-LoRA BGMV / SGMV ops.
+ *
+ * Plain pointers, sizes and a cudaStream_t; no torch types.  Every function
+ * returns PERSONA_OK (0) or a PERSONA_ERR_* status synchronously after
+ * validating its arguments on the host and enqueuing its kernels on
+ * `stream`.  Conditions only the device can see (a slot outside [-1, S), a
+ * bounded wait that gave up) are ORed into the caller's device error word
+ * `dev_err` (a device or host-mapped int32; may be NULL to ignore them).
+ *
+ * Layouts (element strides, 16-bit elements unless noted):
+ *   x      [T, K]  row stride ldx          fp16 or bf16
+ *   a_pool [S, R, K] slot stride a_slot_stride, row stride a_row_stride
+ *   b_pool [S, N, R] slot stride b_slot_stride, rows of R contiguous values
+ *   v      [T, R]  fp32, contiguous
+ *   y      [T, N]  row stride ldy, same 16-bit type as x
+ *   slots  [T]     int32; -1 = no adapter for this row
+ * The LoRA scale alpha/r is folded into b_pool by the pool loader; no op
+ * takes a scale.  All base pointers must be 16-byte aligned and K, N, ldx,
+ * ldy and the strides multiples of 8 (the reference's own preconditions,
+ * csrc/bgmv_shrink.cu:100-104, csrc/bgmv_expand.cu:229-233).
+ */
+#ifndef PERSONA_BGMV_H
+#define PERSONA_BGMV_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#include <cuda_runtime_api.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define PERSONA_ABI_VERSION 1
+
+/* 16-bit storage types of x / pools / y. */
+#define PERSONA_DTYPE_F16 0
+#define PERSONA_DTYPE_BF16 1
+
+/* Host-side status codes. */
+#define PERSONA_OK 0
+#define PERSONA_ERR_INVALID_ARG 1 /* null pointer, negative size, bad flag   */
+#define PERSONA_ERR_SHAPE 2       /* inconsistent or unsupported dimensions  */
+#define PERSONA_ERR_DTYPE 3       /* dtype code not F16/BF16                 */
+#define PERSONA_ERR_ALIGNMENT 4   /* pointer or stride not 16-byte aligned   */
+#define PERSONA_ERR_RANK 5        /* LoRA rank this op does not support      */
+#define PERSONA_ERR_WORKSPACE 6   /* workspace missing or too small          */
+#define PERSONA_ERR_CUDA 7        /* CUDA runtime / launch failure           */
+
+/* Device error-word bits (ORed into *dev_err by the kernels). */
+#define PERSONA_DEV_ERR_SLOT 1    /* a slot < -1 or >= S: that row was left alone */
+#define PERSONA_DEV_ERR_TIMEOUT 2 /* a bounded wait gave up                       */
+#define PERSONA_DEV_ERR_SEGMENT 4 /* SGMV segment table out of order or range     */
+
+/* Flags of the BGMV ops. */
+#define PERSONA_REUSE_PLAN 1 /* workspace already holds the plan of these slots */
+
+const char* persona_status_string(int status);
+int persona_abi_version(void);
+
+/* ---- row grouping plan --------------------------------------------------
+ * The BGMV kernels stream each used adapter's A and B once for all rows that
+ * share it.  The plan (built on the device, no host sync) groups the rows of
+ * `slots` by slot into items of at most 16 rows.  One plan serves every
+ * projection of a decode step that shares the slot vector.
+ * No reference counterpart: the reference validates and visits slots row by
+ * row with a host sync per row (csrc/bgmv_shrink.cu:106-109).               */
+size_t persona_bgmv_workspace_size(int64_t T);
+int persona_bgmv_plan(const int32_t* slots, int64_t T, int64_t S, void* workspace,
+                      size_t workspace_bytes, int32_t* dev_err, cudaStream_t stream);
+
+/* ---- BGMV shrink --------------------------------------------------------
+ * v[t, :] = A[slots[t]] @ x[t, :] in fp32; rows with slot -1 get zeros.
+ * Replaces bgmv_shrink_cuda (csrc/bgmv_shrink.cu:81-122) behind
+ * torch.ops.persona.bgmv_shrink (csrc/bindings.cpp:20).  R in {8,16,32,64}
+ * runs the clustered kernel; any other R runs a row-by-row kernel.         */
+int persona_bgmv_shrink(const void* x, int64_t ldx, const void* a_pool, int64_t a_slot_stride,
+                        int64_t a_row_stride, const int32_t* slots, float* v, int64_t T,
+                        int64_t K, int64_t R, int64_t S, int dtype, void* workspace,
+                        size_t workspace_bytes, int flags, int32_t* dev_err,
+                        cudaStream_t stream);
+
+/* ---- BGMV expand --------------------------------------------------------
+ * y[t, :] = round(y[t, :] + B[slots[t]] @ v[t, :]) (fp32 sum, one rounding);
+ * rows with slot -1 are left bit-identical.  R in {8,16,32,64}, as in
+ * the reference.  Replaces bgmv_expand_cuda (csrc/bgmv_expand.cu:88-129)
+ * behind torch.ops.persona.bgmv_expand (csrc/bindings.cpp:21).             */
+int persona_bgmv_expand(const float* v, const void* b_pool, int64_t b_slot_stride,
+                        const int32_t* slots, void* y, int64_t ldy, int64_t T, int64_t N,
+                        int64_t R, int64_t S, int dtype, void* workspace,
+                        size_t workspace_bytes, int flags, int32_t* dev_err,
+                        cudaStream_t stream);
+
+/* ---- fused BGMV shrink -> expand -----------------------------------------
+ * y[t, :] = round(y[t, :] + B[s] @ (A[s] @ x[t, :])) with the rank-R
+ * intermediate kept on chip (distributed shared memory of a thread-block
+ * cluster).  The reference's fused kernel is a stub (docs/BENCHMARKS.md:238);
+ * its result equals bgmv_shrink followed by bgmv_expand
+ * (persona/ops.py:59-68).  R in {8,16,32,64}.                              */
+int persona_bgmv_fused(const void* x, int64_t ldx, const void* a_pool, int64_t a_slot_stride,
+                       int64_t a_row_stride, const void* b_pool, int64_t b_slot_stride,
+                       const int32_t* slots, void* y, int64_t ldy, int64_t T, int64_t K,
+                       int64_t N, int64_t R, int64_t S, int dtype, void* workspace,
+                       size_t workspace_bytes, int flags, int32_t* dev_err,
+                       cudaStream_t stream);
+
+/* ---- warm-up GEMV ---------------------------------------------------------
+ * y[n] = W[n, :] @ x (fp16, fp32 accumulate).  Replaces
+ * persona::gemv_fp16_cuda (csrc/gemv_fp16.cu:33-50), kept so that
+ * torch.ops.persona.gemv_fp16 (csrc/bindings.cpp:22) stays registered.     */
+int persona_gemv_fp16(const void* x, const void* W, void* y, int64_t K, int64_t N,
+                      cudaStream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PERSONA_BGMV_H */

@@ -1,0 +1,353 @@
+// torch.ops.persona registration over the C ABI of libpersona_bgmv.so.
+//
+// The three reference schemas are registered byte-identically on the CUDA
+// dispatch key (reference csrc/bindings.cpp:19-29), with the same C++ host
+// symbols (bgmv_shrink_cuda, bgmv_expand_cuda, persona::gemv_fp16_cuda) and
+// the same TORCH_CHECK messages.  New ops (fused, planned variants, plan)
+// are registered beside them.  Python module persona._C keeps `noop`
+// (reference csrc/bindings.cpp:31-33) and adds the device error word
+// helpers.
+//
+// Slot validation: the reference syncs with the host once per row
+// (csrc/bgmv_shrink.cu:106-109).  Here the device flags an out-of-range
+// slot in a per-device error word held in mapped pinned host memory; every
+// op first reads that word (no sync) and raises RuntimeError if an earlier
+// call flagged it, and PERSONA_STRICT_SLOTS=1 makes each op synchronise and
+// raise on its own call instead.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+#include <torch/library.h>
+
+#include <cstdlib>
+#include <mutex>
+#include <sstream>
+
+#include "persona_bgmv.h"
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+
+struct ErrorWords {
+  std::mutex mu;
+  int32_t* host[kMaxDevices] = {};
+};
+ErrorWords& error_words() {
+  static ErrorWords w;
+  return w;
+}
+
+// Mapped pinned int32 of `device` (allocated on first use), host view.
+int32_t* error_word_host(int device) {
+  TORCH_CHECK(device >= 0 && device < kMaxDevices, "persona: device index out of range");
+  auto& w = error_words();
+  std::lock_guard<std::mutex> lock(w.mu);
+  if (w.host[device] == nullptr) {
+    void* p = nullptr;
+    C10_CUDA_CHECK(cudaHostAlloc(&p, sizeof(int32_t), cudaHostAllocMapped | cudaHostAllocPortable));
+    *static_cast<volatile int32_t*>(p) = 0;
+    w.host[device] = static_cast<int32_t*>(p);
+  }
+  return w.host[device];
+}
+
+int32_t* error_word_device(int device) {
+  static int32_t* dev_ptr[kMaxDevices] = {};
+  if (dev_ptr[device] == nullptr) {
+    int32_t* h = error_word_host(device);
+    void* d = nullptr;
+    C10_CUDA_CHECK(cudaHostGetDevicePointer(&d, h, 0));
+    dev_ptr[device] = static_cast<int32_t*>(d);
+  }
+  return dev_ptr[device];
+}
+
+std::string describe_error(int bits) {
+  std::ostringstream os;
+  os << "persona: a BGMV/SGMV call on this device flagged an error (bits 0x" << std::hex << bits
+     << std::dec << "):";
+  if (bits & PERSONA_DEV_ERR_SLOT) os << " slot out of range;";
+  if (bits & PERSONA_DEV_ERR_TIMEOUT) os << " device wait timed out;";
+  if (bits & PERSONA_DEV_ERR_SEGMENT) os << " invalid segment table;";
+  return os.str();
+}
+
+// Raise (and clear) an error flagged by an earlier call on `device`.
+void raise_pending(int device, const char* op) {
+  volatile int32_t* h = error_word_host(device);
+  const int bits = *h;
+  if (bits != 0) {
+    *h = 0;
+    TORCH_CHECK(false, op, ": ", describe_error(bits));
+  }
+}
+
+bool strict_slots() {
+  static const bool strict = [] {
+    const char* e = std::getenv("PERSONA_STRICT_SLOTS");
+    return e != nullptr && e[0] == '1';
+  }();
+  return strict;
+}
+
+void after_launch(int device, const char* op, cudaStream_t stream) {
+  if (!strict_slots()) return;
+  C10_CUDA_CHECK(cudaStreamSynchronize(stream));
+  volatile int32_t* h = error_word_host(device);
+  const int bits = *h;
+  if (bits & PERSONA_DEV_ERR_SLOT) {
+    *h = 0;
+    TORCH_CHECK(false, op, ": slot out of range");
+  }
+  raise_pending(device, op);
+}
+
+void check_status(int st, const char* op) {
+  TORCH_CHECK(st == PERSONA_OK, op, ": ", persona_status_string(st));
+}
+
+int dtype_code(const at::Tensor& t, const char* op) {
+  if (t.scalar_type() == at::kHalf) return PERSONA_DTYPE_F16;
+  if (t.scalar_type() == at::kBFloat16) return PERSONA_DTYPE_BF16;
+  TORCH_CHECK(false, op, ": only float16 and bfloat16 supported");
+  return -1;
+}
+
+// Row-major [rows, cols] with unit inner stride (a view of a wider buffer is
+// fine); returns the row stride in elements.
+int64_t row_stride(const at::Tensor& t) { return t.size(0) <= 1 ? t.size(1) : t.stride(0); }
+
+at::Tensor workspace_for(int64_t T, const at::Tensor& like) {
+  const size_t bytes = persona_bgmv_workspace_size(T);
+  return at::empty({static_cast<int64_t>(bytes)}, like.options().dtype(at::kByte));
+}
+
+void check_pool_a(const at::Tensor& a_pool, const char* op) {
+  TORCH_CHECK(a_pool.dim() == 3, op, ": a_pool must be [S, R, K]");
+  TORCH_CHECK(a_pool.stride(2) == 1, op, ": tensors must be contiguous");
+}
+
+void check_pool_b(const at::Tensor& b_pool, const char* op) {
+  TORCH_CHECK(b_pool.dim() == 3, op, ": b_pool must be [S, N, R]");
+  TORCH_CHECK(b_pool.stride(2) == 1 && b_pool.stride(1) == b_pool.size(2), op,
+              ": tensors must be contiguous");
+}
+
+void shrink_impl(const at::Tensor& x, const at::Tensor& a_pool, const at::Tensor& slots,
+                 at::Tensor& v, const c10::optional<at::Tensor>& plan) {
+  const char* op = "bgmv_shrink";
+  TORCH_CHECK(x.is_cuda() && a_pool.is_cuda() && slots.is_cuda() && v.is_cuda(),
+              "bgmv_shrink: all tensors must be CUDA");
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1 && slots.is_contiguous() && v.is_contiguous(),
+              "bgmv_shrink: tensors must be contiguous");
+  check_pool_a(a_pool, op);
+  TORCH_CHECK(slots.scalar_type() == at::kInt, "bgmv_shrink: slots must be int32");
+  TORCH_CHECK(v.scalar_type() == at::kFloat, "bgmv_shrink: v must be float32");
+  const int64_t T = x.size(0), K = x.size(1), S = a_pool.size(0), R = a_pool.size(1);
+  TORCH_CHECK(a_pool.size(2) == K, "bgmv_shrink: a_pool shape mismatch");
+  TORCH_CHECK(slots.dim() == 1 && slots.size(0) == T, "bgmv_shrink: slots length must match T");
+  TORCH_CHECK(v.dim() == 2 && v.size(0) == T && v.size(1) == R, "bgmv_shrink: v shape mismatch");
+  TORCH_CHECK(K % 8 == 0, "bgmv_shrink: K must be a multiple of 8");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0, "bgmv_shrink: x must be 16-byte aligned");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(a_pool.data_ptr()) % 16 == 0,
+              "bgmv_shrink: a_pool must be 16-byte aligned");
+  const int dt = dtype_code(x, op);
+  TORCH_CHECK(a_pool.scalar_type() == x.scalar_type(), "bgmv_shrink: dtype mismatch");
+  const at::cuda::OptionalCUDAGuard guard(x.device());
+  const int dev = x.get_device();
+  raise_pending(dev, op);
+  if (T == 0) return;
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  at::Tensor ws = plan.has_value() ? *plan : workspace_for(T, x);
+  const int flags = plan.has_value() ? PERSONA_REUSE_PLAN : 0;
+  TORCH_CHECK(static_cast<size_t>(ws.numel()) >= persona_bgmv_workspace_size(T),
+              "bgmv_shrink: plan was built for fewer rows");
+  const int st = persona_bgmv_shrink(x.data_ptr(), row_stride(x), a_pool.data_ptr(), a_pool.stride(0),
+                                     a_pool.stride(1), slots.data_ptr<int32_t>(), v.data_ptr<float>(), T,
+                                     K, R, S, dt, ws.data_ptr(), ws.numel(), flags,
+                                     error_word_device(dev), stream);
+  check_status(st, op);
+  after_launch(dev, op, stream);
+}
+
+void expand_impl(const at::Tensor& v, const at::Tensor& b_pool, const at::Tensor& slots, at::Tensor& y,
+                 const c10::optional<at::Tensor>& plan) {
+  const char* op = "bgmv_expand";
+  TORCH_CHECK(v.is_cuda() && b_pool.is_cuda() && slots.is_cuda() && y.is_cuda(),
+              "bgmv_expand: all tensors must be CUDA");
+  TORCH_CHECK(v.is_contiguous() && slots.is_contiguous() && y.dim() == 2 && y.stride(1) == 1,
+              "bgmv_expand: tensors must be contiguous");
+  check_pool_b(b_pool, op);
+  TORCH_CHECK(slots.scalar_type() == at::kInt, "bgmv_expand: slots must be int32");
+  TORCH_CHECK(v.scalar_type() == at::kFloat, "bgmv_expand: v must be float32");
+  const int64_t T = v.size(0), R = v.size(1), S = b_pool.size(0), N = b_pool.size(1);
+  TORCH_CHECK(b_pool.size(2) == R, "bgmv_expand: b_pool rank dim mismatch");
+  TORCH_CHECK(slots.dim() == 1 && slots.size(0) == T, "bgmv_expand: slots length must match T");
+  TORCH_CHECK(y.size(0) == T && y.size(1) == N, "bgmv_expand: y shape mismatch");
+  TORCH_CHECK(N % 8 == 0, "bgmv_expand: N must be a multiple of 8");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(b_pool.data_ptr()) % 16 == 0,
+              "bgmv_expand: b_pool must be 16-byte aligned");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(y.data_ptr()) % 16 == 0, "bgmv_expand: y must be 16-byte aligned");
+  TORCH_CHECK(R == 8 || R == 16 || R == 32 || R == 64, "bgmv_expand: R must be 8, 16, 32, or 64");
+  const int dt = dtype_code(y, op);
+  TORCH_CHECK(b_pool.scalar_type() == y.scalar_type(), "bgmv_expand: dtype mismatch");
+  const at::cuda::OptionalCUDAGuard guard(v.device());
+  const int dev = v.get_device();
+  raise_pending(dev, op);
+  if (T == 0) return;
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  at::Tensor ws = plan.has_value() ? *plan : workspace_for(T, v);
+  const int flags = plan.has_value() ? PERSONA_REUSE_PLAN : 0;
+  TORCH_CHECK(static_cast<size_t>(ws.numel()) >= persona_bgmv_workspace_size(T),
+              "bgmv_expand: plan was built for fewer rows");
+  const int st = persona_bgmv_expand(v.data_ptr<float>(), b_pool.data_ptr(), b_pool.stride(0),
+                                     slots.data_ptr<int32_t>(), y.data_ptr(), row_stride(y), T, N, R, S,
+                                     dt, ws.data_ptr(), ws.numel(), flags, error_word_device(dev), stream);
+  check_status(st, op);
+  after_launch(dev, op, stream);
+}
+
+void fused_impl(const at::Tensor& x, const at::Tensor& a_pool, const at::Tensor& b_pool,
+                const at::Tensor& slots, at::Tensor& y, const c10::optional<at::Tensor>& plan) {
+  const char* op = "bgmv_fused";
+  TORCH_CHECK(x.is_cuda() && a_pool.is_cuda() && b_pool.is_cuda() && slots.is_cuda() && y.is_cuda(),
+              "bgmv_fused: all tensors must be CUDA");
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1 && slots.is_contiguous() && y.dim() == 2 &&
+                  y.stride(1) == 1,
+              "bgmv_fused: tensors must be contiguous");
+  check_pool_a(a_pool, op);
+  check_pool_b(b_pool, op);
+  TORCH_CHECK(slots.scalar_type() == at::kInt, "bgmv_fused: slots must be int32");
+  const int64_t T = x.size(0), K = x.size(1), S = a_pool.size(0), R = a_pool.size(1), N = b_pool.size(1);
+  TORCH_CHECK(a_pool.size(2) == K, "bgmv_fused: a_pool shape mismatch");
+  TORCH_CHECK(b_pool.size(0) == S && b_pool.size(2) == R, "bgmv_fused: b_pool shape mismatch");
+  TORCH_CHECK(slots.dim() == 1 && slots.size(0) == T, "bgmv_fused: slots length must match T");
+  TORCH_CHECK(y.size(0) == T && y.size(1) == N, "bgmv_fused: y shape mismatch");
+  const int dt = dtype_code(x, op);
+  TORCH_CHECK(a_pool.scalar_type() == x.scalar_type() && b_pool.scalar_type() == x.scalar_type() &&
+                  y.scalar_type() == x.scalar_type(),
+              "bgmv_fused: dtype mismatch");
+  const at::cuda::OptionalCUDAGuard guard(x.device());
+  const int dev = x.get_device();
+  raise_pending(dev, op);
+  if (T == 0) return;
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  at::Tensor ws = plan.has_value() ? *plan : workspace_for(T, x);
+  const int flags = plan.has_value() ? PERSONA_REUSE_PLAN : 0;
+  TORCH_CHECK(static_cast<size_t>(ws.numel()) >= persona_bgmv_workspace_size(T),
+              "bgmv_fused: plan was built for fewer rows");
+  const int st = persona_bgmv_fused(x.data_ptr(), row_stride(x), a_pool.data_ptr(), a_pool.stride(0),
+                                    a_pool.stride(1), b_pool.data_ptr(), b_pool.stride(0),
+                                    slots.data_ptr<int32_t>(), y.data_ptr(), row_stride(y), T, K, N, R,
+                                    S, dt, ws.data_ptr(), ws.numel(), flags, error_word_device(dev),
+                                    stream);
+  check_status(st, op);
+  after_launch(dev, op, stream);
+}
+
+at::Tensor plan_impl(const at::Tensor& slots, int64_t S) {
+  const char* op = "bgmv_plan";
+  TORCH_CHECK(slots.is_cuda(), "bgmv_plan: all tensors must be CUDA");
+  TORCH_CHECK(slots.is_contiguous() && slots.dim() == 1, "bgmv_plan: tensors must be contiguous");
+  TORCH_CHECK(slots.scalar_type() == at::kInt, "bgmv_plan: slots must be int32");
+  const at::cuda::OptionalCUDAGuard guard(slots.device());
+  const int dev = slots.get_device();
+  raise_pending(dev, op);
+  const int64_t T = slots.size(0);
+  at::Tensor ws = workspace_for(T, slots);
+  if (T == 0) return ws;
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  check_status(persona_bgmv_plan(slots.data_ptr<int32_t>(), T, S, ws.data_ptr(), ws.numel(),
+                                 error_word_device(dev), stream),
+               op);
+  after_launch(dev, op, stream);
+  return ws;
+}
+
+}  // namespace
+
+// Same C++ host symbols as the reference (csrc/bgmv_shrink.cu:81, csrc/bgmv_expand.cu:88).
+void bgmv_shrink_cuda(const at::Tensor& x, const at::Tensor& a_pool, const at::Tensor& slots, at::Tensor& v) {
+  shrink_impl(x, a_pool, slots, v, c10::nullopt);
+}
+
+void bgmv_expand_cuda(const at::Tensor& v, const at::Tensor& b_pool, const at::Tensor& slots, at::Tensor& y) {
+  expand_impl(v, b_pool, slots, y, c10::nullopt);
+}
+
+namespace persona {
+// Reference csrc/gemv_fp16.cu:33-50.
+void gemv_fp16_cuda(const at::Tensor& x, const at::Tensor& W, at::Tensor& y) {
+  TORCH_CHECK(x.is_cuda() && W.is_cuda() && y.is_cuda(), "gemv_fp16: CUDA only");
+  TORCH_CHECK(x.dim() == 1 && W.dim() == 2 && y.dim() == 1, "gemv_fp16: shape");
+  const int64_t K = x.size(0), N = W.size(0);
+  TORCH_CHECK(W.size(1) == K && y.size(0) == N, "gemv_fp16: mismatch");
+  TORCH_CHECK(x.scalar_type() == at::kHalf && W.scalar_type() == at::kHalf && y.scalar_type() == at::kHalf,
+              "gemv_fp16: half only in v1 scaffold");
+  TORCH_CHECK(x.is_contiguous() && W.is_contiguous() && y.is_contiguous(), "gemv_fp16: contiguous only");
+  const at::cuda::OptionalCUDAGuard guard(x.device());
+  check_status(persona_gemv_fp16(x.data_ptr(), W.data_ptr(), y.data_ptr(), K, N,
+                                 at::cuda::getCurrentCUDAStream()),
+               "gemv_fp16");
+}
+}  // namespace persona
+
+namespace {
+void shrink_with_plan(const at::Tensor& x, const at::Tensor& a_pool, const at::Tensor& slots,
+                      const at::Tensor& plan, at::Tensor& v) {
+  shrink_impl(x, a_pool, slots, v, plan);
+}
+void expand_with_plan(const at::Tensor& v, const at::Tensor& b_pool, const at::Tensor& slots,
+                      const at::Tensor& plan, at::Tensor& y) {
+  expand_impl(v, b_pool, slots, y, plan);
+}
+void fused_noplan(const at::Tensor& x, const at::Tensor& a_pool, const at::Tensor& b_pool,
+                  const at::Tensor& slots, at::Tensor& y) {
+  fused_impl(x, a_pool, b_pool, slots, y, c10::nullopt);
+}
+void fused_with_plan(const at::Tensor& x, const at::Tensor& a_pool, const at::Tensor& b_pool,
+                     const at::Tensor& slots, const at::Tensor& plan, at::Tensor& y) {
+  fused_impl(x, a_pool, b_pool, slots, y, plan);
+}
+}  // namespace
+
+TORCH_LIBRARY(persona, m) {
+  // Reference schemas, unchanged (csrc/bindings.cpp:19-23).
+  m.def("bgmv_shrink(Tensor x, Tensor a_pool, Tensor slots, Tensor(a!) v) -> ()");
+  m.def("bgmv_expand(Tensor v, Tensor b_pool, Tensor slots, Tensor(a!) y) -> ()");
+  m.def("gemv_fp16(Tensor x, Tensor W, Tensor(a!) y) -> ()");
+  // New in this build.
+  m.def("bgmv_plan(Tensor slots, int S) -> Tensor");
+  m.def("bgmv_shrink_with_plan(Tensor x, Tensor a_pool, Tensor slots, Tensor plan, Tensor(a!) v) -> ()");
+  m.def("bgmv_expand_with_plan(Tensor v, Tensor b_pool, Tensor slots, Tensor plan, Tensor(a!) y) -> ()");
+  m.def("bgmv_fused(Tensor x, Tensor a_pool, Tensor b_pool, Tensor slots, Tensor(a!) y) -> ()");
+  m.def("bgmv_fused_with_plan(Tensor x, Tensor a_pool, Tensor b_pool, Tensor slots, Tensor plan, "
+        "Tensor(a!) y) -> ()");
+}
+
+TORCH_LIBRARY_IMPL(persona, CUDA, m) {
+  m.impl("bgmv_shrink", &bgmv_shrink_cuda);
+  m.impl("bgmv_expand", &bgmv_expand_cuda);
+  m.impl("gemv_fp16", &persona::gemv_fp16_cuda);
+  m.impl("bgmv_plan", &plan_impl);
+  m.impl("bgmv_shrink_with_plan", &shrink_with_plan);
+  m.impl("bgmv_expand_with_plan", &expand_with_plan);
+  m.impl("bgmv_fused", &fused_noplan);
+  m.impl("bgmv_fused_with_plan", &fused_with_plan);
+}
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.def("noop", []() { return 0; });
+  m.def("abi_version", []() { return persona_abi_version(); });
+  m.def("workspace_size", [](int64_t T) { return persona_bgmv_workspace_size(T); });
+  m.def(
+      "take_device_error",
+      [](int device) {
+        volatile int32_t* h = error_word_host(device);
+        const int bits = *h;
+        *h = 0;
+        return bits;
+      },
+      "Read and clear the device error word of `device` (no synchronisation).");
+}

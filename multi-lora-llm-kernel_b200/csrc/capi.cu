@@ -1,0 +1,292 @@
+// extern "C" entry points of libpersona_bgmv.so (declared in persona_bgmv.h).
+//
+// Host side of every op: validate the arguments (the reference's TORCH_CHECKs,
+// csrc/bgmv_shrink.cu:85-121 and csrc/bgmv_expand.cu:92-128, as status
+// codes), build the TMA tensor maps of the adapter pools, then enqueue the
+// plan kernel (unless the caller reuses a plan) and the clustered kernel.
+// Nothing here synchronises with the device or allocates device memory.
+#include <cudaTypedefs.h>
+
+#include <cstring>
+#include <mutex>
+
+#include "bgmv_args.h"
+#include "common.cuh"
+#include "plan_layout.h"
+
+namespace persona {
+
+
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+bool rank_supported(int64_t R) { return R == 8 || R == 16 || R == 32 || R == 64; }
+constexpr int64_t kI32Max = 2147483647;
+
+int cluster_size_for() {
+  // 8 CTAs per cluster is portable and leaves room for two clusters per GPC.
+  return 8;
+}
+
+// A pool [S, R, K] (k fastest) as a 3-D tensor {K, R, S}; box {64 k, R rows, 1 slot}.
+int encode_a_map(CUtensorMap* m, const void* a_pool, int dtype, int64_t K, int64_t R, int64_t S,
+                 int64_t row_stride, int64_t slot_stride) {
+  auto enc = tensor_map_encoder();
+  if (!enc) return PERSONA_ERR_CUDA;
+  const CUtensorMapDataType dt =
+      dtype == PERSONA_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(R), static_cast<cuuint64_t>(S)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(row_stride * 2), static_cast<cuuint64_t>(slot_stride * 2)};
+  cuuint32_t box[3] = {64u, static_cast<cuuint32_t>(R), 1u};
+  cuuint32_t estr[3] = {1u, 1u, 1u};
+  CUresult r = enc(m, dt, 3, const_cast<void*>(a_pool), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? PERSONA_OK : PERSONA_ERR_CUDA;
+}
+
+// B pool [S, N, R] (r fastest) as {R, N, S}; box {R, n_box rows, 1 slot},
+// swizzled over the 2R-byte rows.
+int encode_b_map(CUtensorMap* m, const void* b_pool, int dtype, int64_t N, int64_t R, int64_t S,
+                 int64_t slot_stride, int n_box) {
+  auto enc = tensor_map_encoder();
+  if (!enc) return PERSONA_ERR_CUDA;
+  const CUtensorMapDataType dt =
+      dtype == PERSONA_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(R), static_cast<cuuint64_t>(N), static_cast<cuuint64_t>(S)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(R * 2), static_cast<cuuint64_t>(slot_stride * 2)};
+  cuuint32_t box[3] = {static_cast<cuuint32_t>(R), static_cast<cuuint32_t>(n_box), 1u};
+  cuuint32_t estr[3] = {1u, 1u, 1u};
+  CUtensorMapSwizzle sw = R == 64   ? CU_TENSOR_MAP_SWIZZLE_128B
+                          : R == 32 ? CU_TENSOR_MAP_SWIZZLE_64B
+                          : R == 16 ? CU_TENSOR_MAP_SWIZZLE_32B
+                                    : CU_TENSOR_MAP_SWIZZLE_NONE;
+  CUresult r = enc(m, dt, 3, const_cast<void*>(b_pool), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? PERSONA_OK : PERSONA_ERR_CUDA;
+}
+
+void split_k(int64_t K, int cs, int* k_per_cta) {
+  const int64_t per = (K + cs - 1) / cs;
+  *k_per_cta = static_cast<int>((per + 63) / 64 * 64);
+}
+
+void split_n(int64_t N, int cs, int* n_per_cta, int* n_box) {
+  const int64_t per = (N + cs - 1) / cs;
+  if (per <= 256) {
+    *n_box = static_cast<int>((per + 7) / 8 * 8);
+    *n_per_cta = *n_box;
+  } else {
+    *n_box = 256;
+    *n_per_cta = static_cast<int>((per + 255) / 256 * 256);
+  }
+}
+
+int check_common(int64_t T, int64_t S, int dtype, const void* workspace, size_t ws_bytes,
+                 const int32_t* slots) {
+  if (T < 0 || S <= 0) return PERSONA_ERR_SHAPE;
+  if (T > kI32Max / 64) return PERSONA_ERR_SHAPE;
+  if (dtype != PERSONA_DTYPE_F16 && dtype != PERSONA_DTYPE_BF16) return PERSONA_ERR_DTYPE;
+  if (T > 0 && slots == nullptr) return PERSONA_ERR_INVALID_ARG;
+  if (T > 0 && (workspace == nullptr || ws_bytes < plan_bytes(T))) return PERSONA_ERR_WORKSPACE;
+  if (T > 0 && !aligned16(workspace)) return PERSONA_ERR_ALIGNMENT;
+  return PERSONA_OK;
+}
+
+int check_a(const void* x, int64_t ldx, const void* a_pool, int64_t a_slot_stride,
+            int64_t a_row_stride, int64_t K, int64_t R, int64_t S) {
+  if (x == nullptr || a_pool == nullptr) return PERSONA_ERR_INVALID_ARG;
+  if (K <= 0 || R <= 0 || K > kI32Max) return PERSONA_ERR_SHAPE;
+  if (K % 8 != 0) return PERSONA_ERR_SHAPE;  // csrc/bgmv_shrink.cu:100
+  if (ldx < K || a_row_stride < K || a_slot_stride < (R - 1) * a_row_stride + K) return PERSONA_ERR_SHAPE;
+  if (!aligned16(x) || !aligned16(a_pool)) return PERSONA_ERR_ALIGNMENT;  // :101-104
+  if (ldx % 8 || a_row_stride % 8 || a_slot_stride % 8) return PERSONA_ERR_ALIGNMENT;
+  (void)S;
+  return PERSONA_OK;
+}
+
+int check_b(const void* b_pool, int64_t b_slot_stride, const void* y, int64_t ldy, int64_t N,
+            int64_t R) {
+  if (b_pool == nullptr || y == nullptr) return PERSONA_ERR_INVALID_ARG;
+  if (N <= 0 || N > kI32Max) return PERSONA_ERR_SHAPE;
+  if (!rank_supported(R)) return PERSONA_ERR_RANK;       // csrc/bgmv_expand.cu:190-205
+  if (N % 8 != 0) return PERSONA_ERR_SHAPE;              // csrc/bgmv_expand.cu:229
+  if (ldy < N || b_slot_stride < N * R) return PERSONA_ERR_SHAPE;
+  if (!aligned16(b_pool) || !aligned16(y)) return PERSONA_ERR_ALIGNMENT;  // :230-233
+  if (ldy % 8 || b_slot_stride % 8) return PERSONA_ERR_ALIGNMENT;
+  return PERSONA_OK;
+}
+
+int plan_if_needed(const int32_t* slots, int64_t T, int64_t S, void* ws, int flags,
+                   int32_t* dev_err, cudaStream_t st) {
+  if (flags & PERSONA_REUSE_PLAN) return PERSONA_OK;
+  return launch_bgmv_plan(slots, static_cast<int>(T), static_cast<int>(S), kRowsPerItem,
+                          static_cast<int32_t*>(ws), dev_err, st) == cudaSuccess
+             ? PERSONA_OK
+             : PERSONA_ERR_CUDA;
+}
+
+}  // namespace
+}  // namespace persona
+
+using namespace persona;
+
+extern "C" {
+
+const char* persona_status_string(int status) {
+  switch (status) {
+    case PERSONA_OK: return "ok";
+    case PERSONA_ERR_INVALID_ARG: return "invalid argument (null pointer, negative size or bad flag)";
+    case PERSONA_ERR_SHAPE: return "inconsistent or unsupported shape";
+    case PERSONA_ERR_DTYPE: return "only float16 and bfloat16 supported";
+    case PERSONA_ERR_ALIGNMENT: return "pointer or stride not 16-byte aligned";
+    case PERSONA_ERR_RANK: return "R must be 8, 16, 32, or 64";
+    case PERSONA_ERR_WORKSPACE: return "workspace missing, misaligned or too small";
+    case PERSONA_ERR_CUDA: return "CUDA runtime or launch failure";
+    default: return "unknown status";
+  }
+}
+
+int persona_abi_version(void) { return PERSONA_ABI_VERSION; }
+
+size_t persona_bgmv_workspace_size(int64_t T) { return T < 0 ? 0 : plan_bytes(T); }
+
+int persona_bgmv_plan(const int32_t* slots, int64_t T, int64_t S, void* workspace,
+                      size_t workspace_bytes, int32_t* dev_err, cudaStream_t stream) {
+  int st = check_common(T, S, PERSONA_DTYPE_F16, workspace, workspace_bytes, slots);
+  if (st != PERSONA_OK) return st;
+  if (T == 0) return PERSONA_OK;
+  return plan_if_needed(slots, T, S, workspace, 0, dev_err, stream);
+}
+
+int persona_bgmv_shrink(const void* x, int64_t ldx, const void* a_pool, int64_t a_slot_stride,
+                        int64_t a_row_stride, const int32_t* slots, float* v, int64_t T,
+                        int64_t K, int64_t R, int64_t S, int dtype, void* workspace,
+                        size_t workspace_bytes, int flags, int32_t* dev_err,
+                        cudaStream_t stream) {
+  if (flags & ~PERSONA_REUSE_PLAN) return PERSONA_ERR_INVALID_ARG;
+  // Ranks 8/16/32/64 with K >= 64 run the clustered kernel over a plan;
+  // any other rank runs row by row and needs no workspace.
+  const bool clustered = rank_supported(R) && K >= 64;
+  int st;
+  if (clustered) {
+    st = check_common(T, S, dtype, workspace, workspace_bytes, slots);
+  } else {
+    st = check_common(T, S, dtype, nullptr, 0, slots);
+    if (st == PERSONA_ERR_WORKSPACE || st == PERSONA_ERR_ALIGNMENT) st = PERSONA_OK;
+  }
+  if (st != PERSONA_OK) return st;
+  if (T == 0) return PERSONA_OK;
+  if ((st = check_a(x, ldx, a_pool, a_slot_stride, a_row_stride, K, R, S)) != PERSONA_OK) return st;
+  if (v == nullptr) return PERSONA_ERR_INVALID_ARG;
+  if (R > 4096 || T * R > kI32Max) return PERSONA_ERR_SHAPE;
+  if (!clustered) {
+    return launch_shrink_rowwise(dtype, x, ldx, a_pool, a_slot_stride, a_row_stride, slots, v,
+                                 static_cast<int>(T), static_cast<int>(K), static_cast<int>(R),
+                                 static_cast<int>(S), dev_err, stream) == cudaSuccess
+               ? PERSONA_OK
+               : PERSONA_ERR_CUDA;
+  }
+  CUtensorMap tmA, tmB;
+  std::memset(&tmB, 0, sizeof(tmB));
+  if ((st = encode_a_map(&tmA, a_pool, dtype, K, R, S, a_row_stride, a_slot_stride)) != PERSONA_OK) return st;
+  if ((st = plan_if_needed(slots, T, S, workspace, flags, dev_err, stream)) != PERSONA_OK) return st;
+  const int cs = cluster_size_for();
+  BgmvArgs a = {};
+  a.x = x; a.ldx = ldx; a.v_out = v; a.slots = slots;
+  a.plan = static_cast<const int32_t*>(workspace); a.err = dev_err;
+  a.T = static_cast<int>(T); a.K = static_cast<int>(K); a.N = 0; a.S = static_cast<int>(S);
+  split_k(K, cs, &a.k_per_cta);
+  a.n_per_cta = 0; a.n_box = 8;
+  return launch_bgmv_cluster(kModeShrink, dtype, static_cast<int>(R), tmA, tmB, a, cs,
+                             static_cast<int>(T), stream) == cudaSuccess
+             ? PERSONA_OK
+             : PERSONA_ERR_CUDA;
+}
+
+int persona_bgmv_expand(const float* v, const void* b_pool, int64_t b_slot_stride,
+                        const int32_t* slots, void* y, int64_t ldy, int64_t T, int64_t N,
+                        int64_t R, int64_t S, int dtype, void* workspace,
+                        size_t workspace_bytes, int flags, int32_t* dev_err,
+                        cudaStream_t stream) {
+  if (flags & ~PERSONA_REUSE_PLAN) return PERSONA_ERR_INVALID_ARG;
+  int st = check_common(T, S, dtype, workspace, workspace_bytes, slots);
+  if (st != PERSONA_OK) return st;
+  if (!rank_supported(R)) return PERSONA_ERR_RANK;
+  if (T == 0) return PERSONA_OK;
+  if ((st = check_b(b_pool, b_slot_stride, y, ldy, N, R)) != PERSONA_OK) return st;
+  if (v == nullptr) return PERSONA_ERR_INVALID_ARG;
+  const int cs = cluster_size_for();
+  BgmvArgs a = {};
+  split_n(N, cs, &a.n_per_cta, &a.n_box);
+  CUtensorMap tmA, tmB;
+  std::memset(&tmA, 0, sizeof(tmA));
+  if ((st = encode_b_map(&tmB, b_pool, dtype, N, R, S, b_slot_stride, a.n_box)) != PERSONA_OK) return st;
+  if ((st = plan_if_needed(slots, T, S, workspace, flags, dev_err, stream)) != PERSONA_OK) return st;
+  a.v_in = v; a.y = y; a.ldy = ldy; a.slots = slots;
+  a.plan = static_cast<const int32_t*>(workspace); a.err = dev_err;
+  a.T = static_cast<int>(T); a.K = 0; a.N = static_cast<int>(N); a.S = static_cast<int>(S);
+  a.k_per_cta = 0;
+  return launch_bgmv_cluster(kModeExpand, dtype, static_cast<int>(R), tmA, tmB, a, cs,
+                             static_cast<int>(T), stream) == cudaSuccess
+             ? PERSONA_OK
+             : PERSONA_ERR_CUDA;
+}
+
+int persona_bgmv_fused(const void* x, int64_t ldx, const void* a_pool, int64_t a_slot_stride,
+                       int64_t a_row_stride, const void* b_pool, int64_t b_slot_stride,
+                       const int32_t* slots, void* y, int64_t ldy, int64_t T, int64_t K,
+                       int64_t N, int64_t R, int64_t S, int dtype, void* workspace,
+                       size_t workspace_bytes, int flags, int32_t* dev_err,
+                       cudaStream_t stream) {
+  if (flags & ~PERSONA_REUSE_PLAN) return PERSONA_ERR_INVALID_ARG;
+  int st = check_common(T, S, dtype, workspace, workspace_bytes, slots);
+  if (st != PERSONA_OK) return st;
+  if (!rank_supported(R)) return PERSONA_ERR_RANK;
+  if (T == 0) return PERSONA_OK;
+  if ((st = check_a(x, ldx, a_pool, a_slot_stride, a_row_stride, K, R, S)) != PERSONA_OK) return st;
+  if ((st = check_b(b_pool, b_slot_stride, y, ldy, N, R)) != PERSONA_OK) return st;
+  if (K < 64) return PERSONA_ERR_SHAPE;
+  const int cs = cluster_size_for();
+  BgmvArgs a = {};
+  split_k(K, cs, &a.k_per_cta);
+  split_n(N, cs, &a.n_per_cta, &a.n_box);
+  CUtensorMap tmA, tmB;
+  if ((st = encode_a_map(&tmA, a_pool, dtype, K, R, S, a_row_stride, a_slot_stride)) != PERSONA_OK) return st;
+  if ((st = encode_b_map(&tmB, b_pool, dtype, N, R, S, b_slot_stride, a.n_box)) != PERSONA_OK) return st;
+  if ((st = plan_if_needed(slots, T, S, workspace, flags, dev_err, stream)) != PERSONA_OK) return st;
+  a.x = x; a.ldx = ldx; a.y = y; a.ldy = ldy; a.slots = slots;
+  a.plan = static_cast<const int32_t*>(workspace); a.err = dev_err;
+  a.T = static_cast<int>(T); a.K = static_cast<int>(K); a.N = static_cast<int>(N);
+  a.S = static_cast<int>(S);
+  return launch_bgmv_cluster(kModeFused, dtype, static_cast<int>(R), tmA, tmB, a, cs,
+                             static_cast<int>(T), stream) == cudaSuccess
+             ? PERSONA_OK
+             : PERSONA_ERR_CUDA;
+}
+
+int persona_gemv_fp16(const void* x, const void* W, void* y, int64_t K, int64_t N,
+                      cudaStream_t stream) {
+  if (K < 0 || N < 0 || K > kI32Max || N > kI32Max) return PERSONA_ERR_SHAPE;
+  if (N == 0) return PERSONA_OK;
+  if (x == nullptr || W == nullptr || y == nullptr) return PERSONA_ERR_INVALID_ARG;
+  return launch_gemv_fp16(x, W, y, static_cast<int>(K), static_cast<int>(N), stream) == cudaSuccess
+             ? PERSONA_OK
+             : PERSONA_ERR_CUDA;
+}
+
+}  // extern "C"

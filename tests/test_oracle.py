@@ -1,0 +1,113 @@
+"""The oracle pinned against the reference's own outputs (golden vectors) and
+its torch-free known-answer test.  CPU only."""
+
+import numpy as np
+import pytest
+
+from oracle import bgmv_oracle as O
+from persona import workloads
+
+
+def _case(golden, name):
+    pre = name + "/"
+    return {k[len(pre):]: golden[k] for k in golden.files if k.startswith(pre)}
+
+
+@pytest.mark.parametrize("dtype", ["f16", "bf16"])
+@pytest.mark.parametrize("R", [8, 16, 32, 64])
+def test_shrink_matches_reference(golden, dtype, R):
+    c = _case(golden, f"shrink_{dtype}_r{R}")
+    v = O.bgmv_shrink_ref(c["x"], c["a"], c["slots"], dtype)
+    # same fp32 math as the reference; only the summation order differs
+    np.testing.assert_allclose(v, c["v"], rtol=1e-5, atol=1e-5)
+    assert np.all(v[c["slots"] < 0] == 0)
+
+
+@pytest.mark.parametrize("dtype", ["f16", "bf16"])
+@pytest.mark.parametrize("R", [8, 16, 32, 64])
+def test_expand_matches_reference(golden, dtype, R):
+    c = _case(golden, f"expand_{dtype}_r{R}")
+    y = c["y_in"].copy()
+    O.bgmv_expand_ref(c["v"], c["b"], c["slots"], y, dtype)
+    got, want = O.to_f32(y, dtype), O.to_f32(c["y_out"], dtype)
+    # one rounding of an fp32 sum: at most one storage ulp apart
+    np.testing.assert_allclose(got, want, rtol=1e-2, atol=1e-2)
+    ulp = 2.0 ** -10 if dtype == "f16" else 2.0 ** -7
+    assert np.all(np.abs(got - want) <= ulp * np.maximum(np.abs(want), 2.0 ** -14) * 1.01)
+    null = c["slots"] < 0
+    assert np.array_equal(y[null].view(np.uint16), c["y_in"][null].view(np.uint16))
+
+
+def test_forward_matches_reference(golden):
+    c = _case(golden, "forward_f16")
+    y = O.bgmv_forward_ref(c["x"], c["a"], c["b"], c["slots"], "f16")
+    np.testing.assert_allclose(y.astype(np.float32), c["y"].astype(np.float32), rtol=1e-3, atol=1e-3)
+
+
+def test_all_null_rows_bit_identical(golden):
+    c = _case(golden, "null_bf16")
+    v = O.bgmv_shrink_ref(c["x"], c["a"], c["slots"], "bf16")
+    assert np.array_equal(v, c["v"]) and not v.any()
+    y = O.from_f32(np.ones(c["y"].shape, np.float32), "bf16")
+    y0 = y.copy()
+    O.bgmv_expand_ref(v, c["b"], c["slots"], y, "bf16")
+    assert np.array_equal(y, y0) and np.array_equal(y, c["y"])
+
+
+@pytest.mark.parametrize("name,maker", [("single_projection", lambda: workloads.single_projection(0)),
+                                        ("mixed_small", lambda: workloads.mixed_batch(
+                                            seed=5, T=64, R=64, S=16, names=["k_proj"]))])
+def test_workload_fixture(golden, name, maker):
+    c = _case(golden, name)
+    wl = maker()
+    p = wl.projections[0]
+    digest = workloads.checksum(p.x, p.a_pool, p.b_pool, wl.slots, p.y)
+    assert digest == bytes(c["checksum"]).decode(), "workload generator drifted"
+    v = O.bgmv_shrink_ref(p.x, p.a_pool, wl.slots)
+    np.testing.assert_allclose(v, c["v"], rtol=1e-4, atol=1e-4)
+    y = p.y.copy()
+    O.bgmv_expand_ref(v, p.b_pool, wl.slots, y)
+    np.testing.assert_allclose(y.astype(np.float32), c["y"].astype(np.float32), rtol=1e-2, atol=1e-2)
+
+
+def test_bf16_rounding_matches_torch(golden):
+    c = _case(golden, "bf16_round")
+    got = O.from_f32(c["f32"], "bf16")
+    want = c["bits"]
+    nan = np.isnan(c["f32"])
+    assert np.array_equal(got[~nan], want[~nan])
+    assert np.all(np.isnan(O.to_f32(got[nan], "bf16")))
+
+
+def test_standalone_known_answer():
+    # standalone/test_bgmv.cu:36-86 -- CPU reference of the deterministic KAT
+    x, a, slots = O.kat_inputs()
+    v = O.bgmv_shrink_ref(x, a, slots)
+    x32, a32 = x.astype(np.float32), a.astype(np.float32)
+    for t in range(4):
+        for r in range(16):
+            want = 0.0 if slots[t] < 0 else float(np.dot(a32[slots[t], r].astype(np.float64),
+                                                       x32[t].astype(np.float64)))
+            assert abs(v[t, r] - want) <= 1e-2
+    assert not v[2].any()
+
+
+def test_plan_ref_contract():
+    rng = np.random.default_rng(0)
+    S = 7
+    slots = rng.integers(-3, S + 2, size=300).astype(np.int32)
+    perm, items, nv, nn, nb = O.plan_ref(slots, S, 5)
+    assert sorted(perm.tolist()) == list(range(300))
+    valid = (slots >= 0) & (slots < S)
+    assert nv == valid.sum() and nn == (slots == -1).sum() and nb == 300 - nv - nn
+    ps = slots[perm[:nv]]
+    assert np.all(np.diff(ps) >= 0)
+    for s in range(S):  # stable within a slot
+        rows = perm[:nv][ps == s]
+        assert np.all(np.diff(rows) > 0)
+    covered = 0
+    for s, b, c in items:
+        assert 1 <= c <= 5 and np.all(slots[perm[b:b + c]] == s)
+        assert b == covered
+        covered += c
+    assert covered == nv
