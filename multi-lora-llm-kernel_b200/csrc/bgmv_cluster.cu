@@ -17,13 +17,22 @@
 //   partial v's are reduced through distributed shared memory: each CTA sums
 //   one share of the entries over the CS CTAs and broadcasts the sum back,
 //   so the rank-R intermediate never leaves the chip in the fused kernel.
-// * One producer warp streams A tiles ({64 k x R rows}, 128-byte swizzle)
-//   and B tiles ({R x n_box rows}) with TMA into a 4-stage ring of 32 KB
-//   stages; eight consumer warps compute with packed fp32x2 FMAs.  The
-//   producer runs ahead across item boundaries, so HBM stays busy while the
-//   consumers reduce.
-// * x rows of an item are gathered by the consumers into a 512-wide fp32
-//   window laid out as row pairs; y is read-modified-written once per row.
+// * A producer warp feeds a 10-slot ring of 20 KB slots with everything the
+//   consumers read: A tiles ({64 k x R rows}, 128-byte swizzle) and B tiles
+//   ({R x n_box rows}) by TMA, the item's x row windows, y tiles and v rows
+//   by 1-D bulk copies (one lane per row), and prefetches the next item's
+//   data into L2.  Item descriptors (slot, row count, row indices) reach the
+//   consumers through a 4-deep item ring.  Consumers never wait on a global
+//   load: they read shared memory and write y / v with plain stores.
+// * The item's 16 rows are one warp-MMA tile (m16n8k16, fp32 accumulate):
+//   x and v fragments are loaded once per warp and reused over every rank /
+//   output column tile, so the inner products cost neither CUDA-core issue
+//   slots nor shared-memory bandwidth (a packed-FMA version was bound by
+//   broadcast shared loads).  The expand multiplies B by v split into two
+//   16-bit halves (v = hi + lo, power-of-two scaled against overflow), which
+//   keeps the fp32 accuracy of v.
+#include <type_traits>
+
 #include "bgmv_args.h"
 #include "common.cuh"
 #include "plan_layout.h"
@@ -33,203 +42,199 @@ namespace persona {
 constexpr int kConsumerWarps = 8;
 constexpr int kConsumers = kConsumerWarps * 32;
 constexpr int kBgmvThreads = kConsumers + 32;  // + one producer warp
-constexpr int kStageBytes = 32768;
-constexpr int kStages = 4;
-constexpr int kXWin = 512;                     // k extent of the staged x window
-constexpr int kPairs = kRowsPerItem / 2;       // row pairs per item
+constexpr int kSlotBytes = 20480;              // one ring slot (multiple of 1024)
+constexpr int kSlots = 10;
+constexpr int kItemRing = 4;
+constexpr int kXWin = 512;                     // k extent of one x window
+constexpr int kXPitch = 2 * kXWin + 16;        // bytes per x row in a window slot (bank-conflict pad)
 constexpr int kMaxR = 64;
 constexpr int kNamedBarConsumers = 1;
 
-constexpr int kRingBytes = kStages * kStageBytes;
-constexpr int kX2Bytes = kPairs * kXWin * 8;            // float2 [pairs][window]
-constexpr int kVBytes = kPairs * kMaxR * 8;             // float2 [pairs][R]
-constexpr int kSmemLayoutBytes = kRingBytes + kX2Bytes + 4 * kVBytes + 64 + 16 * 8;
+struct ItemDesc {
+  int slot;
+  int count;
+  int pad[2];
+  int rows[kRowsPerItem];
+};
+
+constexpr int kRingBytes = kSlots * kSlotBytes;
+constexpr int kVBytes = kRowsPerItem * kMaxR * 4;            // fp32 [16][R]
+constexpr int kRedBytes = kConsumerWarps * kRowsPerItem * 8 * 4;  // fp32 [warp][16][8]
+constexpr int kItemBytes = kItemRing * static_cast<int>(sizeof(ItemDesc));
+constexpr int kBarCount = 2 * kSlots + 2 * kItemRing + 4;
+constexpr int kSmemLayoutBytes = kRingBytes + 4 * kVBytes + kRedBytes + kItemBytes + kBarCount * 8;
 constexpr int kBgmvSmemBytes = kSmemLayoutBytes + 1024;  // slack to align the base
+static_assert(kBgmvSmemBytes <= 227 * 1024, "shared memory budget");
+static_assert(kRowsPerItem * kXPitch <= kSlotBytes, "x window slot");
 
 template <int R>
 struct RankCfg {
   static_assert(R == 8 || R == 16 || R == 32 || R == 64, "rank");
-  static constexpr int kRP = R / 2;  // a thread's rank pair is (rp, rp + R/2)
-  static constexpr int kKC = (kStageBytes / (2 * R)) < kXWin ? (kStageBytes / (2 * R)) : kXWin;
+  static constexpr int kKC = (8192 / R) < kXWin ? (8192 / R) : kXWin;  // k per A stage (<= 16 KB)
   static constexpr int kABoxBytes = 128 * R;  // TMA box {64 k, R rows}
-  static constexpr int kAUnits = kKC / 8;     // 16-byte k units per A stage
-  static constexpr int kKGroups = kConsumers / kRP;
-  static constexpr int kKUPT = kAUnits / kKGroups;
-  static_assert(kKUPT >= 1 && kKUPT * kKGroups == kAUnits, "shrink mapping");
-  static constexpr int kNB = kStageBytes / (2 * R);  // B rows per stage (capacity)
+  static constexpr int kNT = R / 8;           // shrink: 8-wide rank tiles
+  static constexpr int kKS = kConsumerWarps / kNT;  // shrink: warps splitting k per rank tile
+  // B rows per stage: B tile (2R bytes/row) + y tile (16 rows x 2 bytes/col) in one slot.
+  static constexpr int kNBraw = kSlotBytes / (2 * R + 2 * kRowsPerItem) / 8 * 8;
+  static constexpr int kNB = kNBraw < 256 ? kNBraw : 256;
+  static constexpr int kYOff = kNB * 2 * R;  // byte offset of the y tile in a B slot
+  static constexpr int kYStride = kNB * 2;   // bytes per y-tile row
   static constexpr uint32_t kBSwz = (2 * R == 128) ? 7u : (2 * R == 64) ? 3u : (2 * R == 32) ? 1u : 0u;
-  static constexpr int kRU = R / 8;  // 16-byte units per B row
+  static constexpr int kKSteps = R >= 16 ? R / 16 : 1;  // expand: k16 steps over the rank
 };
 
+int bgmv_stage_rows(int R) {
+  switch (R) {
+    case 8: return RankCfg<8>::kNB;
+    case 16: return RankCfg<16>::kNB;
+    case 32: return RankCfg<32>::kNB;
+    default: return RankCfg<64>::kNB;
+  }
+}
 
 struct SmemPtrs {
   uint8_t* ring;
-  float2* x2;
-  float2* pv;      // [2][pairs][R] local partial of v
-  float2* vf;      // [2][pairs][R] full v (row pairs)
-  int* rows;       // [16]
-  uint64_t* full;  // [kStages]
-  uint64_t* empty; // [kStages]
-  uint64_t* red;   // [2]
-  uint64_t* gat;   // [2]
+  float* pv;   // [2][16][R] this CTA's partial v
+  float* vf;   // [2][16][R] full v of the item
+  float* red;  // [warp][16][8] per-warp MMA tiles / maxima
+  ItemDesc* items;
+  uint64_t* full;    // [kSlots]
+  uint64_t* empty;   // [kSlots]
+  uint64_t* ifull;   // [kItemRing]
+  uint64_t* iempty;  // [kItemRing]
+  uint64_t* red_bar; // [2]
+  uint64_t* gat_bar; // [2]
 };
 
 __device__ __forceinline__ SmemPtrs carve_smem(uint8_t* raw) {
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
   SmemPtrs p;
   p.ring = base;
-  p.x2 = reinterpret_cast<float2*>(base + kRingBytes);
-  p.pv = reinterpret_cast<float2*>(base + kRingBytes + kX2Bytes);
-  p.vf = reinterpret_cast<float2*>(base + kRingBytes + kX2Bytes + 2 * kVBytes);
-  p.rows = reinterpret_cast<int*>(base + kRingBytes + kX2Bytes + 4 * kVBytes);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(base + kRingBytes + kX2Bytes + 4 * kVBytes + 64);
+  uint8_t* q = base + kRingBytes;
+  p.pv = reinterpret_cast<float*>(q);
+  p.vf = reinterpret_cast<float*>(q + 2 * kVBytes);
+  p.red = reinterpret_cast<float*>(q + 4 * kVBytes);
+  p.items = reinterpret_cast<ItemDesc*>(q + 4 * kVBytes + kRedBytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(q + 4 * kVBytes + kRedBytes + kItemBytes);
   p.full = bars;
-  p.empty = bars + kStages;
-  p.red = bars + 2 * kStages;
-  p.gat = bars + 2 * kStages + 2;
+  p.empty = bars + kSlots;
+  p.ifull = bars + 2 * kSlots;
+  p.iempty = bars + 2 * kSlots + kItemRing;
+  p.red_bar = bars + 2 * kSlots + 2 * kItemRing;
+  p.gat_bar = p.red_bar + 2;
   return p;
 }
 
 __device__ __forceinline__ float2 f2(float a, float b) { return make_float2(a, b); }
 
+// The j-th item of cluster `cid` out of `ncl`: rounds of ncl items, visited in
+// serpentine order so that clusters that take a heavy (early) item in one
+// round take a light one in the next.  The plan lists items heaviest first.
+__device__ __forceinline__ int item_of(int cid, int ncl, int j) {
+  return (j & 1) ? (j + 1) * ncl - 1 - cid : j * ncl + cid;
+}
+
 // ---------------------------------------------------------------- shrink --
-// acc0/acc1[p] accumulate (v[2p][r], v[2p+1][r]) for r = rp and rp + R/2
-// over the k units this thread owns in one A stage.
-template <typename DT, int R, int P>
-__device__ __forceinline__ void shrink_stage(const uint8_t* stage, const float2* x2, int xoff,
-                                             int units_loaded, int tid, float2 (&acc0)[kPairs],
-                                             float2 (&acc1)[kPairs]) {
+// One A stage: d (this warp's 16 rows x 8 ranks tile) += x[16][k] * A[ranks][k]
+// over the k16 steps of the stage this warp owns (warps sharing a rank tile
+// split the steps).  x16 is the smem address of this lane's ldmatrix row in
+// the x window at the stage's first column.
+template <typename DT, int R>
+__device__ __forceinline__ void shrink_stage(uint32_t abase, uint32_t x16, int ksteps, int warp, int lane,
+                                             float (&d)[4]) {
   using C = RankCfg<R>;
-  const int rp = tid % C::kRP;
-  const int kg = tid / C::kRP;
-  const int r0 = rp, r1 = rp + C::kRP;
-  const uint32_t sbase = smem_u32(stage);
-  const uint32_t xbase = smem_u32(x2);
-#pragma unroll
-  for (int j = 0; j < C::kKUPT; ++j) {
-    const int ku = kg + j * C::kKGroups;
-    if (ku >= units_loaded) break;
+  const int ntile = warp % C::kNT;
+  const int ksplit = warp / C::kNT;
+  const int r = ntile * 8 + (lane & 7);
+  const int uofs = (lane >> 3) & 1;
+  for (int ks = ksplit; ks < ksteps; ks += C::kKS) {
+    uint32_t a[4], b[2];
+    ldsm_x4(x16 + ks * 32, a);
+    const int ku = ks * 2 + uofs;
     const int bx = ku >> 3, u = ku & 7;
-    const uint32_t boff = sbase + bx * C::kABoxBytes;
-    const uint4 a0 = lds128(boff + r0 * 128 + ((u ^ (r0 & 7)) << 4));
-    const uint4 a1 = lds128(boff + r1 * 128 + ((u ^ (r1 & 7)) << 4));
-    float fa0[8], fa1[8];
-    {
-      float2 t;
-      t = Cvt<DT>::to2(a0.x); fa0[0] = t.x; fa0[1] = t.y;
-      t = Cvt<DT>::to2(a0.y); fa0[2] = t.x; fa0[3] = t.y;
-      t = Cvt<DT>::to2(a0.z); fa0[4] = t.x; fa0[5] = t.y;
-      t = Cvt<DT>::to2(a0.w); fa0[6] = t.x; fa0[7] = t.y;
-      t = Cvt<DT>::to2(a1.x); fa1[0] = t.x; fa1[1] = t.y;
-      t = Cvt<DT>::to2(a1.y); fa1[2] = t.x; fa1[3] = t.y;
-      t = Cvt<DT>::to2(a1.z); fa1[4] = t.x; fa1[5] = t.y;
-      t = Cvt<DT>::to2(a1.w); fa1[6] = t.x; fa1[7] = t.y;
-    }
-    const int kx = xoff + ku * 8;
-#pragma unroll
-    for (int p = 0; p < P; ++p) {
-      const uint32_t xa = xbase + static_cast<uint32_t>((p * kXWin + kx) * 8);
-      const float4 q0 = lds128f(xa), q1 = lds128f(xa + 16), q2 = lds128f(xa + 32), q3 = lds128f(xa + 48);
-      acc0[p] = __ffma2_rn(f2(q0.x, q0.y), f2(fa0[0], fa0[0]), acc0[p]);
-      acc1[p] = __ffma2_rn(f2(q0.x, q0.y), f2(fa1[0], fa1[0]), acc1[p]);
-      acc0[p] = __ffma2_rn(f2(q0.z, q0.w), f2(fa0[1], fa0[1]), acc0[p]);
-      acc1[p] = __ffma2_rn(f2(q0.z, q0.w), f2(fa1[1], fa1[1]), acc1[p]);
-      acc0[p] = __ffma2_rn(f2(q1.x, q1.y), f2(fa0[2], fa0[2]), acc0[p]);
-      acc1[p] = __ffma2_rn(f2(q1.x, q1.y), f2(fa1[2], fa1[2]), acc1[p]);
-      acc0[p] = __ffma2_rn(f2(q1.z, q1.w), f2(fa0[3], fa0[3]), acc0[p]);
-      acc1[p] = __ffma2_rn(f2(q1.z, q1.w), f2(fa1[3], fa1[3]), acc1[p]);
-      acc0[p] = __ffma2_rn(f2(q2.x, q2.y), f2(fa0[4], fa0[4]), acc0[p]);
-      acc1[p] = __ffma2_rn(f2(q2.x, q2.y), f2(fa1[4], fa1[4]), acc1[p]);
-      acc0[p] = __ffma2_rn(f2(q2.z, q2.w), f2(fa0[5], fa0[5]), acc0[p]);
-      acc1[p] = __ffma2_rn(f2(q2.z, q2.w), f2(fa1[5], fa1[5]), acc1[p]);
-      acc0[p] = __ffma2_rn(f2(q3.x, q3.y), f2(fa0[6], fa0[6]), acc0[p]);
-      acc1[p] = __ffma2_rn(f2(q3.x, q3.y), f2(fa1[6], fa1[6]), acc1[p]);
-      acc0[p] = __ffma2_rn(f2(q3.z, q3.w), f2(fa0[7], fa0[7]), acc0[p]);
-      acc1[p] = __ffma2_rn(f2(q3.z, q3.w), f2(fa1[7], fa1[7]), acc1[p]);
-    }
+    ldsm_x2(abase + bx * C::kABoxBytes + r * 128 + ((u ^ (r & 7)) << 4), b);
+    Mma<DT>::k16(d, a, b);
   }
 }
 
 // ---------------------------------------------------------------- expand --
-// One stage of B rows: y[rows][n] += sum_r B[n][r] * v[rows][r].
-template <typename DT, int R, int P>
-__device__ __forceinline__ void expand_stage(const uint8_t* stage, const float2* vf, int nboxes,
-                                             int n_box, int n0, int nend, int c, const int* rows,
-                                             uint16_t* y, int64_t ldy, int tid) {
+// One B stage: for each 8-column tile this warp owns,
+// y[row][n] = round(y_tile[row][n] + scale * (v_hi + v_lo)[row] . B[n]).
+template <typename DT, int R>
+__device__ __forceinline__ void expand_stage(const uint8_t* stage, const uint32_t (&vhi)[RankCfg<R>::kKSteps][4],
+                                             const uint32_t (&vlo)[RankCfg<R>::kKSteps][4], int rows_here,
+                                             int n_box, int n0, int c, const int* rows, uint16_t* y, int64_t ldy,
+                                             float scale, int warp, int lane) {
   using C = RankCfg<R>;
   const uint32_t sbase = smem_u32(stage);
-  const uint32_t vbase = smem_u32(vf);
-  for (int bx = 0; bx < nboxes; ++bx) {
-    const int nb0 = n0 + bx * n_box;
-    const int rows_here = min(n_box, nend - nb0);
+  const uint8_t* ytile = stage + C::kYOff;
+  const int g = lane >> 2, t = lane & 3;
+  const int tiles = rows_here >> 3;
+  for (int tile = warp; tile < tiles; tile += kConsumerWarps) {
+    const int nl = tile * 8;
+    const int bx = nl / n_box;
+    const int rib = nl - bx * n_box + (lane & 7);
     const uint32_t boff = sbase + static_cast<uint32_t>(bx * n_box * 2 * R);
-    for (int rib = tid; rib < rows_here; rib += kConsumers) {
-      float2 acc[kPairs];
+    float d[4] = {0.f, 0.f, 0.f, 0.f};
+    if (R >= 16) {
 #pragma unroll
-      for (int p = 0; p < kPairs; ++p) acc[p] = f2(0.f, 0.f);
-#pragma unroll
-      for (int u = 0; u < C::kRU; ++u) {
-        const uint4 bw = lds128(boff + swz(static_cast<uint32_t>(rib * 2 * R + u * 16), C::kBSwz));
-        float fb[8];
-        {
-          float2 t;
-          t = Cvt<DT>::to2(bw.x); fb[0] = t.x; fb[1] = t.y;
-          t = Cvt<DT>::to2(bw.y); fb[2] = t.x; fb[3] = t.y;
-          t = Cvt<DT>::to2(bw.z); fb[4] = t.x; fb[5] = t.y;
-          t = Cvt<DT>::to2(bw.w); fb[6] = t.x; fb[7] = t.y;
-        }
-#pragma unroll
-        for (int p = 0; p < P; ++p) {
-          const uint32_t va = vbase + static_cast<uint32_t>((p * R + u * 8) * 8);
-          const float4 q0 = lds128f(va), q1 = lds128f(va + 16), q2 = lds128f(va + 32), q3 = lds128f(va + 48);
-          acc[p] = __ffma2_rn(f2(q0.x, q0.y), f2(fb[0], fb[0]), acc[p]);
-          acc[p] = __ffma2_rn(f2(q0.z, q0.w), f2(fb[1], fb[1]), acc[p]);
-          acc[p] = __ffma2_rn(f2(q1.x, q1.y), f2(fb[2], fb[2]), acc[p]);
-          acc[p] = __ffma2_rn(f2(q1.z, q1.w), f2(fb[3], fb[3]), acc[p]);
-          acc[p] = __ffma2_rn(f2(q2.x, q2.y), f2(fb[4], fb[4]), acc[p]);
-          acc[p] = __ffma2_rn(f2(q2.z, q2.w), f2(fb[5], fb[5]), acc[p]);
-          acc[p] = __ffma2_rn(f2(q3.x, q3.y), f2(fb[6], fb[6]), acc[p]);
-          acc[p] = __ffma2_rn(f2(q3.z, q3.w), f2(fb[7], fb[7]), acc[p]);
-        }
+      for (int ks = 0; ks < C::kKSteps; ++ks) {
+        uint32_t b[2];
+        const int u = ks * 2 + ((lane >> 3) & 1);
+        ldsm_x2(boff + swz(static_cast<uint32_t>(rib * 2 * R + u * 16), C::kBSwz), b);
+        Mma<DT>::k16(d, vhi[ks], b);
+        Mma<DT>::k16(d, vlo[ks], b);
       }
-      const int n = nb0 + rib;
-      uint16_t yo[2 * kPairs];
+    } else {
+      uint32_t b;
+      ldsm_x1(boff + static_cast<uint32_t>(rib * 2 * R), b);
+      const uint32_t ah[2] = {vhi[0][0], vhi[0][1]};
+      const uint32_t al[2] = {vlo[0][0], vlo[0][1]};
+      Mma<DT>::k8(d, ah, b);
+      Mma<DT>::k8(d, al, b);
+    }
+    // d[0..1]: row g, columns nl+2t, nl+2t+1; d[2..3]: row g+8.
+    const int col = nl + 2 * t;
 #pragma unroll
-      for (int p = 0; p < P; ++p) {
-        if (2 * p < c) yo[2 * p] = y[static_cast<int64_t>(rows[2 * p]) * ldy + n];
-        if (2 * p + 1 < c) yo[2 * p + 1] = y[static_cast<int64_t>(rows[2 * p + 1]) * ldy + n];
-      }
-#pragma unroll
-      for (int p = 0; p < P; ++p) {
-        if (2 * p < c)
-          y[static_cast<int64_t>(rows[2 * p]) * ldy + n] = Cvt<DT>::from1(Cvt<DT>::to1(yo[2 * p]) + acc[p].x);
-        if (2 * p + 1 < c)
-          y[static_cast<int64_t>(rows[2 * p + 1]) * ldy + n] =
-              Cvt<DT>::from1(Cvt<DT>::to1(yo[2 * p + 1]) + acc[p].y);
+    for (int h = 0; h < 2; ++h) {
+      const int row = g + 8 * h;
+      if (row < c) {
+        const uint32_t yw = *reinterpret_cast<const uint32_t*>(ytile + row * C::kYStride + col * 2);
+        const float2 yo = Cvt<DT>::to2(yw);
+        const uint32_t out = Mma<DT>::pack(yo.x + scale * d[2 * h], yo.y + scale * d[2 * h + 1]);
+        *reinterpret_cast<uint32_t*>(y + static_cast<int64_t>(rows[row]) * ldy + n0 + col) = out;
       }
     }
   }
 }
 
-// Gather the item's x rows for k in [w0, w0 + kXWin) into x2 as fp32 row pairs.
-// Columns at or past `klim` (the end of this CTA's K slice) read as zero.
-template <typename DT>
-__device__ __forceinline__ void load_x_window(const uint16_t* x, int64_t ldx, int klim, int w0,
-                                              const int* rows, int c, int P, float2* x2, int tid) {
-#pragma unroll 4
-  for (int idx = tid; idx < P * (kXWin / 2); idx += kConsumers) {
-    const int p = idx / (kXWin / 2);
-    const int kk = (idx % (kXWin / 2)) * 2;
-    const int k = w0 + kk;
-    uint32_t w_lo = 0, w_hi = 0;
-    if (k < klim) {
-      if (2 * p < c) w_lo = *reinterpret_cast<const uint32_t*>(x + static_cast<int64_t>(rows[2 * p]) * ldx + k);
-      if (2 * p + 1 < c)
-        w_hi = *reinterpret_cast<const uint32_t*>(x + static_cast<int64_t>(rows[2 * p + 1]) * ldx + k);
+// A-operand fragments of v (rows x rank, fp32 in smem, row stride R) for the
+// expand MMAs: v * 2^-e split into a 16-bit high part and the 16-bit
+// rounding of the remainder.
+template <typename DT, int R>
+__device__ __forceinline__ void v_fragments(const float* vf, float scale_down, int lane,
+                                            uint32_t (&vhi)[RankCfg<R>::kKSteps][4],
+                                            uint32_t (&vlo)[RankCfg<R>::kKSteps][4]) {
+  using C = RankCfg<R>;
+  const int g = lane >> 2, t = lane & 3;
+#pragma unroll
+  for (int ks = 0; ks < C::kKSteps; ++ks) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      // register i: (row g | g+8) x (k 2t,2t+1 | +8) as in the m16n8k16 A layout
+      const int row = g + 8 * (i & 1);
+      const int k = ks * 16 + 2 * t + 8 * (i >> 1);
+      if (R < 16 && i >= 2) {
+        vhi[ks][i] = 0u;
+        vlo[ks][i] = 0u;
+        continue;
+      }
+      const float2 v = *reinterpret_cast<const float2*>(vf + row * R + k);
+      const float a = v.x * scale_down, b = v.y * scale_down;
+      const float ha = Mma<DT>::round_trip(a), hb = Mma<DT>::round_trip(b);
+      vhi[ks][i] = Mma<DT>::pack(ha, hb);
+      vlo[ks][i] = Mma<DT>::pack(a - ha, b - hb);
     }
-    const float2 lo = Cvt<DT>::to2(w_lo), hi = Cvt<DT>::to2(w_hi);
-    float4* dst = reinterpret_cast<float4*>(x2 + p * kXWin + kk);
-    *dst = make_float4(lo.x, hi.x, lo.y, hi.y);
   }
 }
 
@@ -251,13 +256,17 @@ __global__ void __launch_bounds__(kBgmvThreads, 1)
   const int ncl = static_cast<int>(nclusters_x());
 
   if (tid == 0) {
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < kSlots; ++s) {
       mbar_init(&sm.full[s], 1);
       mbar_init(&sm.empty[s], kConsumerWarps);
     }
+    for (int i = 0; i < kItemRing; ++i) {
+      mbar_init(&sm.ifull[i], 1);
+      mbar_init(&sm.iempty[i], kConsumerWarps);
+    }
     for (int b = 0; b < 2; ++b) {
-      mbar_init(&sm.red[b], CS);
-      mbar_init(&sm.gat[b], CS);
+      mbar_init(&sm.red_bar[b], CS);
+      mbar_init(&sm.gat_bar[b], CS);
     }
     fence_mbar_init_cluster();
   }
@@ -269,45 +278,123 @@ __global__ void __launch_bounds__(kBgmvThreads, 1)
   const int kend = min(args.K, kbeg + args.k_per_cta);
   const int nbeg = static_cast<int>(q) * args.n_per_cta;
   const int nend = min(args.N, nbeg + args.n_per_cta);
-  const int bps = C::kNB / args.n_box;           // B boxes per stage
-  const int stage_rows = bps * args.n_box;
+  const int stage_rows = (C::kNB / args.n_box) * args.n_box;
 
   if (warp == kConsumerWarps) {
     // ------------------------------------------------------- producer --
+    const uint16_t* x = static_cast<const uint16_t*>(args.x);
+    const uint16_t* yg = static_cast<const uint16_t*>(args.y);
     if (lane == 0) {
       if (kDoShrink) tma_prefetch_desc(&tmA);
       if (kDoExpand) tma_prefetch_desc(&tmB);
-      uint32_t g = 0;
-      for (int item = cid; item < n_items; item += ncl) {
-        const int slot = pv.items[item].x;
-        if (kDoShrink) {
-          for (int k0 = kbeg; k0 < kend; k0 += C::kKC, ++g) {
-            const int s = g % kStages;
-            if (g >= kStages) mbar_wait(&sm.empty[s], ((g / kStages) - 1) & 1, args.err);
-            const int nbox = (min(C::kKC, kend - k0) + 63) / 64;
-            mbar_arrive_expect_tx(&sm.full[s], nbox * C::kABoxBytes);
-            for (int b = 0; b < nbox; ++b)
-              tma_load_3d(sm.ring + s * kStageBytes + b * C::kABoxBytes, &tmA, &sm.full[s],
-                          k0 + 64 * b, 0, slot);
-          }
-        }
-        if (kDoExpand) {
-          for (int n0 = nbeg; n0 < nend; n0 += stage_rows, ++g) {
-            const int s = g % kStages;
-            if (g >= kStages) mbar_wait(&sm.empty[s], ((g / kStages) - 1) & 1, args.err);
-            const int nbox = (min(stage_rows, nend - n0) + args.n_box - 1) / args.n_box;
-            mbar_arrive_expect_tx(&sm.full[s], nbox * args.n_box * 2 * R);
-            for (int b = 0; b < nbox; ++b)
-              tma_load_3d(sm.ring + s * kStageBytes + b * args.n_box * 2 * R, &tmB, &sm.full[s], 0,
-                          n0 + b * args.n_box, slot);
+    }
+    uint32_t g = 0;
+    int item = item_of(cid, ncl, 0);
+    int4 it = make_int4(0, 0, 0, 0);
+    int row = 0;
+    if (item < n_items) {
+      it = pv.items[item];
+      row = lane < it.z ? pv.perm[it.y + lane] : 0;
+    }
+    // Claim ring slot g % kSlots (waiting for the consumers to free it) and
+    // post the byte count its copies will deliver.
+    auto claim = [&](uint32_t bytes) -> int {
+      const int s = static_cast<int>(g % kSlots);
+      if (lane == 0) {
+        if (g >= kSlots) mbar_wait(&sm.empty[s], ((g / kSlots) - 1) & 1, args.err);
+        mbar_arrive_expect_tx(&sm.full[s], bytes);
+      }
+      __syncwarp();
+      return s;
+    };
+    for (int j = 0; item < n_items; ++j) {
+      const int slot = it.x, c = it.z;
+      // publish the item descriptor
+      const int iq = j % kItemRing;
+      if (lane == 0 && j >= kItemRing) mbar_wait(&sm.iempty[iq], ((j / kItemRing) - 1) & 1, args.err);
+      __syncwarp();
+      if (lane < kRowsPerItem) sm.items[iq].rows[lane] = row;
+      if (lane == 0) {
+        sm.items[iq].slot = slot;
+        sm.items[iq].count = c;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.ifull[iq]);
+      // prefetch the next item's descriptor while this one streams
+      const int nitem = item_of(cid, ncl, j + 1);
+      int4 nit = make_int4(0, 0, 0, 0);
+      if (nitem < n_items) nit = pv.items[nitem];
+
+      if (kDoShrink) {
+        for (int w0 = kbeg; w0 < kend; w0 += kXWin) {
+          const int wend = min(kend, w0 + kXWin);
+          const uint32_t xb = static_cast<uint32_t>(wend - w0) * 2u;
+          int s = claim(static_cast<uint32_t>(c) * xb);
+          if (lane < c)
+            bulk_load(sm.ring + s * kSlotBytes + lane * kXPitch, x + static_cast<int64_t>(row) * args.ldx + w0,
+                      xb, &sm.full[s]);
+          ++g;
+          for (int k0 = w0; k0 < wend; k0 += C::kKC) {
+            const int nbox = (min(C::kKC, wend - k0) + 63) / 64;
+            s = claim(static_cast<uint32_t>(nbox * C::kABoxBytes));
+            if (lane == 0)
+              for (int b = 0; b < nbox; ++b)
+                tma_load_3d(sm.ring + s * kSlotBytes + b * C::kABoxBytes, &tmA, &sm.full[s], k0 + 64 * b, 0, slot);
+            ++g;
           }
         }
       }
+      // The next item's rows (its descriptor has long arrived by now), then an
+      // L2 prefetch of everything the next item will stream, so that its TMA
+      // and bulk loads hit L2: this keeps far more bytes in flight per SM
+      // than the shared-memory ring alone can hold.
+      int nrow = 0;
+      if (nitem < n_items) {
+        nrow = lane < nit.z ? pv.perm[nit.y + lane] : 0;
+        if (kDoShrink) {
+          for (int k0 = kbeg + 64 * lane; k0 < kend; k0 += 64 * 32) tma_prefetch_3d(&tmA, k0, 0, nit.x);
+          if (lane < nit.z && kend > kbeg)
+            bulk_prefetch_l2(x + static_cast<int64_t>(nrow) * args.ldx + kbeg,
+                             static_cast<uint32_t>(kend - kbeg) * 2u);
+        }
+        if (kDoExpand) {
+          for (int n0 = nbeg + args.n_box * lane; n0 < nend; n0 += args.n_box * 32)
+            tma_prefetch_3d(&tmB, 0, n0, nit.x);
+          if (lane < nit.z && nend > nbeg)
+            bulk_prefetch_l2(yg + static_cast<int64_t>(nrow) * args.ldy + nbeg,
+                             static_cast<uint32_t>(nend - nbeg) * 2u);
+        }
+      }
+      if (MODE == kModeExpand) {
+        const int s = claim(static_cast<uint32_t>(c * R * 4));
+        if (lane < c)
+          bulk_load(sm.ring + s * kSlotBytes + lane * R * 4, args.v_in + static_cast<int64_t>(row) * R, R * 4,
+                    &sm.full[s]);
+        ++g;
+      }
+      if (kDoExpand) {
+        for (int n0 = nbeg; n0 < nend; n0 += stage_rows) {
+          const int rows_here = min(stage_rows, nend - n0);
+          const int nbox = (rows_here + args.n_box - 1) / args.n_box;
+          const uint32_t yb = static_cast<uint32_t>(rows_here) * 2u;
+          const int s = claim(static_cast<uint32_t>(nbox * args.n_box * 2 * R) + static_cast<uint32_t>(c) * yb);
+          if (lane == 0)
+            for (int b = 0; b < nbox; ++b)
+              tma_load_3d(sm.ring + s * kSlotBytes + b * args.n_box * 2 * R, &tmB, &sm.full[s], 0,
+                          n0 + b * args.n_box, slot);
+          if (lane < c)
+            bulk_load(sm.ring + s * kSlotBytes + C::kYOff + lane * C::kYStride,
+                      yg + static_cast<int64_t>(row) * args.ldy + n0, yb, &sm.full[s]);
+          ++g;
+        }
+      }
+      it = nit;
+      row = nrow;
+      item = nitem;
     }
     __syncwarp();
   } else {
     // ------------------------------------------------------ consumers --
-    const uint16_t* x = static_cast<const uint16_t*>(args.x);
     uint16_t* y = static_cast<uint16_t*>(args.y);
     if (MODE == kModeShrink) {
       // Rows without a (valid) adapter get v = 0; the items never touch them.
@@ -320,139 +407,148 @@ __global__ void __launch_bounds__(kBgmvThreads, 1)
     }
     uint32_t g = 0;
     int j = 0;
-    for (int item = cid; item < n_items; item += ncl, ++j) {
-      const int4 it = pv.items[item];
-      const int c = it.z;
-      const int P = (c + 1) >> 1;
+    for (int item = item_of(cid, ncl, 0); item < n_items; ++j, item = item_of(cid, ncl, j)) {
+      const int iq = j % kItemRing;
+      mbar_wait(&sm.ifull[iq], (j / kItemRing) & 1, args.err);
+      const ItemDesc* itd = &sm.items[iq];
+      const int c = itd->count;
+      const int* rows = itd->rows;
       const int b = j & 1;
       const uint32_t red_parity = (j >> 1) & 1;
-      float2* pvb = sm.pv + b * kPairs * kMaxR;
-      float2* vfb = sm.vf + b * kPairs * kMaxR;
-      named_sync(kNamedBarConsumers, kConsumers);  // previous item done with rows / x2
-      if (tid < kRowsPerItem) sm.rows[tid] = tid < c ? pv.perm[it.y + tid] : 0;
-      named_sync(kNamedBarConsumers, kConsumers);
+      float* pvb = sm.pv + b * kRowsPerItem * kMaxR;
+      float* vfb = sm.vf + b * kRowsPerItem * kMaxR;
+      const int E = c * R;  // live entries of v (rows < c)
 
       if (kDoShrink) {
-        float2 acc0[kPairs], acc1[kPairs];
-#pragma unroll
-        for (int p = 0; p < kPairs; ++p) acc0[p] = acc1[p] = f2(0.f, 0.f);
-        int w0 = kbeg;
-        for (int k0 = kbeg; k0 < kend; k0 += C::kKC, ++g) {
-          if (((k0 - kbeg) % kXWin) == 0) {
-            w0 = k0;
-            if (k0 != kbeg) named_sync(kNamedBarConsumers, kConsumers);
-            load_x_window<DT>(x, args.ldx, kend, w0, sm.rows, c, P, sm.x2, tid);
+        float d[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int w0 = kbeg; w0 < kend; w0 += kXWin) {
+          const int wend = min(kend, w0 + kXWin);
+          const int sx = static_cast<int>(g % kSlots);
+          mbar_wait(&sm.full[sx], (g / kSlots) & 1, args.err);
+          ++g;
+          uint8_t* xs = sm.ring + sx * kSlotBytes;
+          const int valid = wend - w0;
+          if (valid & 63) {
+            // The last A tile reads zeros past K; zero the matching x columns so
+            // that stale shared memory cannot inject NaN * 0.
+            const int tail = ((valid + 63) & ~63) - valid;
+            for (int e = tid; e < c * tail; e += kConsumers) {
+              const int rr = e / tail, kk = valid + e % tail;
+              reinterpret_cast<uint16_t*>(xs + rr * kXPitch)[kk] = 0;
+            }
             named_sync(kNamedBarConsumers, kConsumers);
           }
-          const int s = g % kStages;
-          mbar_wait(&sm.full[s], (g / kStages) & 1, args.err);
-          const int units = ((min(C::kKC, kend - k0) + 63) / 64) * 8;
-          const uint8_t* st = sm.ring + s * kStageBytes;
-          switch (P) {
-            case 1: shrink_stage<DT, R, 1>(st, sm.x2, k0 - w0, units, tid, acc0, acc1); break;
-            case 2: shrink_stage<DT, R, 2>(st, sm.x2, k0 - w0, units, tid, acc0, acc1); break;
-            case 3: case 4: shrink_stage<DT, R, 4>(st, sm.x2, k0 - w0, units, tid, acc0, acc1); break;
-            default: shrink_stage<DT, R, 8>(st, sm.x2, k0 - w0, units, tid, acc0, acc1); break;
+          const uint32_t x16 = smem_u32(xs) + (lane & 15) * kXPitch + ((lane >> 4) * 8) * 2;
+          for (int k0 = w0; k0 < wend; k0 += C::kKC, ++g) {
+            const int s = static_cast<int>(g % kSlots);
+            mbar_wait(&sm.full[s], (g / kSlots) & 1, args.err);
+            const int ksteps = ((min(C::kKC, wend - k0) + 63) / 64) * 4;
+            shrink_stage<DT, R>(smem_u32(sm.ring + s * kSlotBytes), x16 + (k0 - w0) * 2, ksteps, warp, lane, d);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sm.empty[s]);
           }
           __syncwarp();
-          if (lane == 0) mbar_arrive(&sm.empty[s]);
+          if (lane == 0) mbar_arrive(&sm.empty[sx]);  // x window no longer read
         }
-        // Reduce the k groups of this CTA: lanes sharing a rank pair, then warps.
-#pragma unroll
-        for (int off = C::kRP; off < 32; off <<= 1) {
-#pragma unroll
-          for (int p = 0; p < kPairs; ++p) {
-            acc0[p].x += __shfl_xor_sync(0xffffffffu, acc0[p].x, off);
-            acc0[p].y += __shfl_xor_sync(0xffffffffu, acc0[p].y, off);
-            acc1[p].x += __shfl_xor_sync(0xffffffffu, acc1[p].x, off);
-            acc1[p].y += __shfl_xor_sync(0xffffffffu, acc1[p].y, off);
-          }
-        }
-        named_sync(kNamedBarConsumers, kConsumers);  // x2 free -> reduction scratch
-        float2* red = sm.x2;                         // [warp][pairs][R]
-        if (lane < C::kRP) {
-          const int rp = lane;
-#pragma unroll
-          for (int p = 0; p < kPairs; ++p) {
-            if (p < P) {
-              red[(warp * kPairs + p) * R + rp] = acc0[p];
-              red[(warp * kPairs + p) * R + rp + C::kRP] = acc1[p];
-            }
-          }
+        // This CTA's partial v: sum the warps that split k for each rank tile.
+        {
+          float* rw = sm.red + warp * (kRowsPerItem * 8);
+          const int gg = lane >> 2, tt = lane & 3;
+          rw[gg * 8 + 2 * tt] = d[0];
+          rw[gg * 8 + 2 * tt + 1] = d[1];
+          rw[(gg + 8) * 8 + 2 * tt] = d[2];
+          rw[(gg + 8) * 8 + 2 * tt + 1] = d[3];
         }
         named_sync(kNamedBarConsumers, kConsumers);
-        for (int e = tid; e < P * R; e += kConsumers) {
-          float2 sum = red[e];
+        for (int e = tid; e < E; e += kConsumers) {
+          const int rr = e / R, r = e - rr * R;
+          const int nt = r >> 3, col = r & 7;
+          float sum = 0.f;
 #pragma unroll
-          for (int w = 1; w < kConsumerWarps; ++w) {
-            const float2 t = red[w * kPairs * R + e];
-            sum.x += t.x;
-            sum.y += t.y;
-          }
+          for (int ks = 0; ks < C::kKS; ++ks) sum += sm.red[(nt + ks * C::kNT) * (kRowsPerItem * 8) + rr * 8 + col];
           pvb[e] = sum;
         }
         // Cluster reduce-scatter of the partial v's through DSMEM.
         named_sync(kNamedBarConsumers, kConsumers);
         if (tid == 0) {
           fence_acq_rel_cluster();
-          for (uint32_t r = 0; r < CS; ++r) mbar_arrive_remote(&sm.red[b], r);
+          for (uint32_t r = 0; r < CS; ++r) mbar_arrive_remote(&sm.red_bar[b], r);
         }
-        mbar_wait<true>(&sm.red[b], red_parity, args.err);
-        const int E = P * R;
-        const int share = (E + CS - 1) / CS;
+        mbar_wait<true>(&sm.red_bar[b], red_parity, args.err);
+        const int E2 = E >> 1;  // float2 entries (R is even)
+        const int share = (E2 + static_cast<int>(CS) - 1) / static_cast<int>(CS);
         const int e_lo = static_cast<int>(q) * share;
-        const int e_hi = min(E, e_lo + share);
+        const int e_hi = min(E2, e_lo + share);
         for (int e = e_lo + tid; e < e_hi; e += kConsumers) {
           float2 sum = f2(0.f, 0.f);
           for (uint32_t r = 0; r < CS; ++r) {
-            const float2 t = ld_dsmem_f2(mapa(pvb + e, r));
-            sum.x += t.x;
-            sum.y += t.y;
+            const float2 t2 = ld_dsmem_f2(mapa(pvb + 2 * e, r));
+            sum.x += t2.x;
+            sum.y += t2.y;
           }
           if (MODE == kModeFused) {
-            for (uint32_t r = 0; r < CS; ++r) st_dsmem_f2(mapa(vfb + e, r), sum);
+            for (uint32_t r = 0; r < CS; ++r) st_dsmem_f2(mapa(vfb + 2 * e, r), sum);
           } else {
-            const int p = e / R, rr = e % R;
-            if (2 * p < c) args.v_out[static_cast<int64_t>(sm.rows[2 * p]) * R + rr] = sum.x;
-            if (2 * p + 1 < c) args.v_out[static_cast<int64_t>(sm.rows[2 * p + 1]) * R + rr] = sum.y;
+            const int rr = (2 * e) / R, r = 2 * e - rr * R;
+            *reinterpret_cast<float2*>(args.v_out + static_cast<int64_t>(rows[rr]) * R + r) = sum;
           }
         }
         if (MODE == kModeFused) {
           named_sync(kNamedBarConsumers, kConsumers);
           if (tid == 0) {
             fence_acq_rel_cluster();
-            for (uint32_t r = 0; r < CS; ++r) mbar_arrive_remote(&sm.gat[b], r);
+            for (uint32_t r = 0; r < CS; ++r) mbar_arrive_remote(&sm.gat_bar[b], r);
           }
-          mbar_wait<true>(&sm.gat[b], red_parity, args.err);
+          mbar_wait<true>(&sm.gat_bar[b], red_parity, args.err);
         }
       }
 
       if (kDoExpand) {
         if (MODE == kModeExpand) {
-          for (int e = tid; e < P * R; e += kConsumers) {
-            const int p = e / R, rr = e % R;
-            float lo = 0.f, hi = 0.f;
-            if (2 * p < c) lo = args.v_in[static_cast<int64_t>(sm.rows[2 * p]) * R + rr];
-            if (2 * p + 1 < c) hi = args.v_in[static_cast<int64_t>(sm.rows[2 * p + 1]) * R + rr];
-            vfb[e] = f2(lo, hi);
-          }
+          const int s = static_cast<int>(g % kSlots);
+          mbar_wait(&sm.full[s], (g / kSlots) & 1, args.err);
+          const float* vs = reinterpret_cast<const float*>(sm.ring + s * kSlotBytes);
+          for (int e = tid; e < E; e += kConsumers) vfb[e] = vs[e];
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&sm.empty[s]);
+          ++g;
           named_sync(kNamedBarConsumers, kConsumers);
         }
-        for (int n0 = nbeg; n0 < nend; n0 += stage_rows, ++g) {
-          const int s = g % kStages;
-          mbar_wait(&sm.full[s], (g / kStages) & 1, args.err);
-          const int nbox = (min(stage_rows, nend - n0) + args.n_box - 1) / args.n_box;
-          const uint8_t* st = sm.ring + s * kStageBytes;
-          switch (P) {
-            case 1: expand_stage<DT, R, 1>(st, vfb, nbox, args.n_box, n0, nend, c, sm.rows, y, args.ldy, tid); break;
-            case 2: expand_stage<DT, R, 2>(st, vfb, nbox, args.n_box, n0, nend, c, sm.rows, y, args.ldy, tid); break;
-            case 3: case 4: expand_stage<DT, R, 4>(st, vfb, nbox, args.n_box, n0, nend, c, sm.rows, y, args.ldy, tid); break;
-            default: expand_stage<DT, R, 8>(st, vfb, nbox, args.n_box, n0, nend, c, sm.rows, y, args.ldy, tid); break;
+        // Power-of-two scale that keeps the 16-bit v halves finite (f16 only).
+        float scale_down = 1.f, scale_up = 1.f;
+        if (sizeof(DT) == 2 && std::is_same<DT, __half>::value) {
+          float m = 0.f;
+          for (int e = tid; e < E; e += kConsumers) m = fmaxf(m, fabsf(vfb[e]));
+#pragma unroll
+          for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+          named_sync(kNamedBarConsumers, kConsumers);  // red[] free (shrink reduction done)
+          if (lane == 0) sm.red[warp] = m;
+          named_sync(kNamedBarConsumers, kConsumers);
+          m = sm.red[0];
+#pragma unroll
+          for (int w = 1; w < kConsumerWarps; ++w) m = fmaxf(m, sm.red[w]);
+          const int ex = static_cast<int>((__float_as_uint(m) >> 23) & 0xff) - 127;
+          const int e2 = ex > 14 ? ex - 14 : 0;
+          if (e2 > 0) {
+            scale_down = __uint_as_float(static_cast<uint32_t>(127 - e2) << 23);
+            scale_up = __uint_as_float(static_cast<uint32_t>(127 + (e2 < 127 ? e2 : 127)) << 23);
           }
+        }
+        uint32_t vhi[C::kKSteps][4], vlo[C::kKSteps][4];
+        v_fragments<DT, R>(vfb, scale_down, lane, vhi, vlo);
+        for (int n0 = nbeg; n0 < nend; n0 += stage_rows, ++g) {
+          const int s = static_cast<int>(g % kSlots);
+          mbar_wait(&sm.full[s], (g / kSlots) & 1, args.err);
+          const int rows_here = min(stage_rows, nend - n0);
+          expand_stage<DT, R>(sm.ring + s * kSlotBytes, vhi, vlo, rows_here, args.n_box, n0, c, rows, y, args.ldy,
+                              scale_up, warp, lane);
           __syncwarp();
           if (lane == 0) mbar_arrive(&sm.empty[s]);
         }
       }
+      // done with this item's descriptor
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.iempty[iq]);
     }
   }
   // No CTA may leave while a peer can still reach its shared memory.
@@ -467,23 +563,23 @@ static cudaError_t launch_one(const CUtensorMap& tmA, const CUtensorMap& tmB, co
                               int cluster_size, int max_clusters, cudaStream_t stream) {
   auto kern = bgmv_cluster_kernel<DT, R, MODE>;
   // Function attributes and occupancy are per device; cache both per device
-  // and per portable (<= 8) / non-portable (16) cluster size.
+  // and per cluster size (1, 2, 4, 8, 16).
   constexpr int kMaxDev = 64;
-  static bool configured[kMaxDev][2] = {};
-  static int occ[kMaxDev][2] = {};
+  static bool configured[kMaxDev] = {};
+  static int occ[kMaxDev][5] = {};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= kMaxDev) return cudaErrorInvalidDevice;
-  const int ci = cluster_size > 8 ? 1 : 0;
-  if (!configured[dev][ci]) {
+  int ci = 0;
+  while ((1 << ci) < cluster_size && ci < 4) ++ci;
+  if ((1 << ci) != cluster_size) return cudaErrorInvalidValue;
+  if (!configured[dev]) {
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kBgmvSmemBytes);
     if (e != cudaSuccess) return e;
-    if (cluster_size > 8) {
-      e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-      if (e != cudaSuccess) return e;
-    }
-    configured[dev][ci] = true;
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e != cudaSuccess) return e;
+    configured[dev] = true;
   }
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
@@ -540,6 +636,5 @@ cudaError_t launch_bgmv_cluster(int mode, int dtype, int R, const CUtensorMap& t
                 : dispatch_rank<__half, kModeFused>(R, tmA, tmB, a, cluster_size, max_clusters, st);
   }
 }
-
 
 }  // namespace persona

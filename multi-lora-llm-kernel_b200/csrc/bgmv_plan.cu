@@ -11,7 +11,9 @@
 //   header  n_items, n_valid, n_null, n_bad, T, S, rows_per_item, magic
 //   perm    row indices; per chunk of kChunk rows: valid rows sorted by slot
 //           (ties in row order), then rows with slot -1, then invalid rows
-//   items   int4 {slot, begin (index into perm), count <= rows_per_item, 0}
+//   items   int4 {slot, begin (index into perm), count <= rows_per_item, 0};
+//           per chunk, the full items (count == rows_per_item) in slot order,
+//           then the partial ones in slot order
 // Items never straddle a chunk; for T <= kChunk there is one chunk and the
 // layout is exactly the oracle's `plan_ref`.
 #include <cub/block/block_radix_sort.cuh>
@@ -97,25 +99,38 @@ __global__ void __launch_bounds__(THREADS)
     }
     ScanI(tmp.scan).InclusiveScan(seg_start, seg_start, cub::Max());
     __syncthreads();
-    int flag[IPT];
+    // Items heaviest first: full items (rows_per_item rows) of every slot in
+    // slot order, then the remainder items in slot order.  The BGMV kernels
+    // deal items to clusters in serpentine rounds, so the heavy items are
+    // spread over the clusters and start first.
+    int full[IPT], part[IPT], cntv[IPT];
 #pragma unroll
     for (int j = 0; j < IPT; ++j) {
       const int pos = tid * IPT + j;
-      const bool valid = skey[pos] < static_cast<uint32_t>(S);
-      flag[j] = (valid && ((pos - seg_start[j]) % rows_per_item) == 0) ? 1 : 0;
+      const uint32_t k = skey[pos];
+      const bool start = k < static_cast<uint32_t>(S) && ((pos - seg_start[j]) % rows_per_item) == 0;
+      int cnt = 0;
+      if (start) {
+        cnt = 1;
+        while (cnt < rows_per_item && pos + cnt < CH && skey[pos + cnt] == k) ++cnt;
+      }
+      cntv[j] = cnt;
+      full[j] = (start && cnt == rows_per_item) ? 1 : 0;
+      part[j] = (start && cnt < rows_per_item) ? 1 : 0;
     }
-    int idx[IPT];
-    int chunk_items = 0;
-    ScanI(tmp.scan).ExclusiveSum(flag, idx, chunk_items);
+    int idx_full[IPT], idx_part[IPT];
+    int n_full = 0, n_part = 0;
+    ScanI(tmp.scan).ExclusiveSum(full, idx_full, n_full);
+    __syncthreads();
+    ScanI(tmp.scan).ExclusiveSum(part, idx_part, n_part);
+    const int chunk_items = n_full + n_part;
     const int item_base = s_counts[3];
 #pragma unroll
     for (int j = 0; j < IPT; ++j) {
-      if (!flag[j]) continue;
+      if (!full[j] && !part[j]) continue;
       const int pos = tid * IPT + j;
-      const uint32_t k = skey[pos];
-      int cnt = 1;
-      while (cnt < rows_per_item && pos + cnt < CH && skey[pos + cnt] == k) ++cnt;
-      pv.items[item_base + idx[j]] = make_int4(static_cast<int>(k), base + pos, cnt, 0);
+      const int at = full[j] ? idx_full[j] : n_full + idx_part[j];
+      pv.items[item_base + at] = make_int4(static_cast<int>(skey[pos]), base + pos, cntv[j], 0);
     }
     __syncthreads();
     if (tid == 0) s_counts[3] = item_base + chunk_items;
@@ -139,6 +154,10 @@ cudaError_t launch_bgmv_plan(const int32_t* slots, int T, int S, int rows_per_it
                              int32_t* plan, int32_t* dev_err, cudaStream_t stream) {
   if (T <= 256) {
     bgmv_plan_kernel<128, 2><<<1, 128, 0, stream>>>(slots, T, S, rows_per_item, plan, dev_err);
+  } else if (T <= 512) {
+    bgmv_plan_kernel<128, 4><<<1, 128, 0, stream>>>(slots, T, S, rows_per_item, plan, dev_err);
+  } else if (T <= 1024) {
+    bgmv_plan_kernel<256, 4><<<1, 256, 0, stream>>>(slots, T, S, rows_per_item, plan, dev_err);
   } else {
     bgmv_plan_kernel<256, 8><<<1, 256, 0, stream>>>(slots, T, S, rows_per_item, plan, dev_err);
   }

@@ -7,6 +7,7 @@
 // Nothing here synchronises with the device or allocates device memory.
 #include <cudaTypedefs.h>
 
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -36,9 +37,17 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 
 bool rank_supported(int64_t R) { return R == 8 || R == 16 || R == 32 || R == 64; }
 constexpr int64_t kI32Max = 2147483647;
 
-int cluster_size_for() {
-  // 8 CTAs per cluster is portable and leaves room for two clusters per GPC.
-  return 8;
+// Cluster size: 8 CTAs when the batch is small (few items, so each is split
+// finely to occupy the GPU), 4 otherwise (more clusters resident, a cheaper
+// reduction per item).  PERSONA_CLUSTER_SIZE (1, 2, 4, 8 or 16) overrides.
+int cluster_size_for(int64_t T) {
+  static const int forced = [] {
+    const char* e = std::getenv("PERSONA_CLUSTER_SIZE");
+    const int v = e ? std::atoi(e) : 0;
+    return (v == 1 || v == 2 || v == 4 || v == 8 || v == 16) ? v : 0;
+  }();
+  if (forced) return forced;
+  return T <= 32 ? 8 : 4;
 }
 
 // A pool [S, R, K] (k fastest) as a 3-D tensor {K, R, S}; box {64 k, R rows, 1 slot}.
@@ -85,15 +94,14 @@ void split_k(int64_t K, int cs, int* k_per_cta) {
   *k_per_cta = static_cast<int>((per + 63) / 64 * 64);
 }
 
-void split_n(int64_t N, int cs, int* n_per_cta, int* n_box) {
+// N slice of each cluster CTA and the rows of one B tile: tiles of at most
+// the rank's stage rows, slices a whole number of tiles.
+void split_n(int64_t N, int cs, int R, int* n_per_cta, int* n_box) {
   const int64_t per = (N + cs - 1) / cs;
-  if (per <= 256) {
-    *n_box = static_cast<int>((per + 7) / 8 * 8);
-    *n_per_cta = *n_box;
-  } else {
-    *n_box = 256;
-    *n_per_cta = static_cast<int>((per + 255) / 256 * 256);
-  }
+  const int64_t nb = bgmv_stage_rows(R);
+  const int64_t per8 = (per + 7) / 8 * 8;
+  *n_box = static_cast<int>(per8 < nb ? per8 : nb);
+  *n_per_cta = static_cast<int>((per + *n_box - 1) / *n_box * *n_box);
 }
 
 int check_common(int64_t T, int64_t S, int dtype, const void* workspace, size_t ws_bytes,
@@ -193,6 +201,7 @@ int persona_bgmv_shrink(const void* x, int64_t ldx, const void* a_pool, int64_t 
   if (T == 0) return PERSONA_OK;
   if ((st = check_a(x, ldx, a_pool, a_slot_stride, a_row_stride, K, R, S)) != PERSONA_OK) return st;
   if (v == nullptr) return PERSONA_ERR_INVALID_ARG;
+  if (!aligned16(v)) return PERSONA_ERR_ALIGNMENT;
   if (R > 4096 || T * R > kI32Max) return PERSONA_ERR_SHAPE;
   if (!clustered) {
     return launch_shrink_rowwise(dtype, x, ldx, a_pool, a_slot_stride, a_row_stride, slots, v,
@@ -205,7 +214,7 @@ int persona_bgmv_shrink(const void* x, int64_t ldx, const void* a_pool, int64_t 
   std::memset(&tmB, 0, sizeof(tmB));
   if ((st = encode_a_map(&tmA, a_pool, dtype, K, R, S, a_row_stride, a_slot_stride)) != PERSONA_OK) return st;
   if ((st = plan_if_needed(slots, T, S, workspace, flags, dev_err, stream)) != PERSONA_OK) return st;
-  const int cs = cluster_size_for();
+  const int cs = cluster_size_for(T);
   BgmvArgs a = {};
   a.x = x; a.ldx = ldx; a.v_out = v; a.slots = slots;
   a.plan = static_cast<const int32_t*>(workspace); a.err = dev_err;
@@ -230,9 +239,10 @@ int persona_bgmv_expand(const float* v, const void* b_pool, int64_t b_slot_strid
   if (T == 0) return PERSONA_OK;
   if ((st = check_b(b_pool, b_slot_stride, y, ldy, N, R)) != PERSONA_OK) return st;
   if (v == nullptr) return PERSONA_ERR_INVALID_ARG;
-  const int cs = cluster_size_for();
+  if (!aligned16(v)) return PERSONA_ERR_ALIGNMENT;
+  const int cs = cluster_size_for(T);
   BgmvArgs a = {};
-  split_n(N, cs, &a.n_per_cta, &a.n_box);
+  split_n(N, cs, static_cast<int>(R), &a.n_per_cta, &a.n_box);
   CUtensorMap tmA, tmB;
   std::memset(&tmA, 0, sizeof(tmA));
   if ((st = encode_b_map(&tmB, b_pool, dtype, N, R, S, b_slot_stride, a.n_box)) != PERSONA_OK) return st;
@@ -261,10 +271,10 @@ int persona_bgmv_fused(const void* x, int64_t ldx, const void* a_pool, int64_t a
   if ((st = check_a(x, ldx, a_pool, a_slot_stride, a_row_stride, K, R, S)) != PERSONA_OK) return st;
   if ((st = check_b(b_pool, b_slot_stride, y, ldy, N, R)) != PERSONA_OK) return st;
   if (K < 64) return PERSONA_ERR_SHAPE;
-  const int cs = cluster_size_for();
+  const int cs = cluster_size_for(T);
   BgmvArgs a = {};
   split_k(K, cs, &a.k_per_cta);
-  split_n(N, cs, &a.n_per_cta, &a.n_box);
+  split_n(N, cs, static_cast<int>(R), &a.n_per_cta, &a.n_box);
   CUtensorMap tmA, tmB;
   if ((st = encode_a_map(&tmA, a_pool, dtype, K, R, S, a_row_stride, a_slot_stride)) != PERSONA_OK) return st;
   if ((st = encode_b_map(&tmB, b_pool, dtype, N, R, S, b_slot_stride, a.n_box)) != PERSONA_OK) return st;

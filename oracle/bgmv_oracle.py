@@ -175,7 +175,9 @@ def plan_ref(slots: np.ndarray, S: int, rows_per_item: int):
       then the rows with slot -1 in row order; then rows with an invalid
       slot (< -1 or >= S) in row order.
     * ``items``: ``(slot, begin, count)`` chunks of at most ``rows_per_item``
-      consecutive entries of ``perm`` that share a slot, in ``perm`` order.
+      consecutive entries of ``perm`` that share a slot; first every full
+      chunk (``count == rows_per_item``) in ``perm`` order, then the partial
+      chunks in ``perm`` order (heaviest work first).
     * counts ``n_valid, n_null, n_bad``.
     """
     slots = np.asarray(slots, dtype=np.int64)
@@ -202,6 +204,8 @@ def plan_ref(slots: np.ndarray, S: int, rows_per_item: int):
             items.append((s, b, c))
             b += c
         i = j
+    items = [it for it in items if it[2] == rows_per_item] + \
+        [it for it in items if it[2] < rows_per_item]
     items = np.array(items, dtype=np.int32).reshape(-1, 3)
     return perm, items, int(nv), int(null.sum()), int(bad.sum())
 

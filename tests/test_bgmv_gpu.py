@@ -329,18 +329,22 @@ def test_fused_is_deterministic():
 
 # ------------------------------------------------------------------- plan --
 
-@pytest.mark.parametrize("T,S", [(1, 1), (8, 8), (255, 7), (256, 300), (257, 3), (2048, 256), (2049, 5)])
+@pytest.mark.parametrize("T,S", [(1, 1), (8, 8), (255, 7), (256, 300), (257, 3), (512, 256), (600, 2),
+                                 (2048, 256), (2049, 5), (5000, 3)])
 def test_plan_matches_oracle(T, S):
     rng = np.random.default_rng(T + S)
     slots = rng.integers(-2, S + 1, size=T).astype(np.int32)
     plan = ops.bgmv_plan(ti(slots), S).cpu().numpy().view(np.int32)
-    ops.check_errors(dev()) if not ((slots < -1) | (slots >= S)).any() else \
-        pytest.raises(RuntimeError, ops.check_errors, dev())
+    if ((slots < -1) | (slots >= S)).any():
+        with pytest.raises(RuntimeError, match="slot out of range"):
+            ops.check_errors(dev())
+    else:
+        ops.check_errors(dev())
     tp = (T + 3) // 4 * 4
     hdr, perm = plan[:8], plan[8:8 + T]
     items = plan[8 + tp:8 + tp + 4 * tp].reshape(-1, 4)
     # chunked like the device planner (2048 rows per chunk above 256 rows)
-    ch = 256 if T <= 256 else 2048
+    ch = 256 if T <= 256 else 512 if T <= 512 else 1024 if T <= 1024 else 2048
     exp_items, nv_tot = [], 0
     for base in range(0, T, ch):
         sl = slots[base:base + ch]
