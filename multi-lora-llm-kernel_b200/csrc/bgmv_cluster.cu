@@ -12,22 +12,29 @@
 // * Work unit = one plan item: one adapter slot and up to 16 rows that use
 //   it.  The adapter's A and B are streamed from HBM once per item, not once
 //   per row.
-// * A thread-block cluster of CS CTAs owns an item.  CTA q shrinks the
-//   K-slice q (partial v over its slice) and expands the N-slice q.  The
-//   partial v's are reduced through distributed shared memory: each CTA sums
-//   one share of the entries over the CS CTAs and broadcasts the sum back,
-//   so the rank-R intermediate never leaves the chip in the fused kernel.
-// * A producer warp feeds a 10-slot ring of 20 KB slots with everything the
-//   consumers read: A tiles ({64 k x R rows}, 128-byte swizzle) and B tiles
-//   ({R x n_box rows}) by TMA, the item's x row windows, y tiles and v rows
-//   by 1-D bulk copies (one lane per row), and prefetches the next item's
-//   data into L2.  Item descriptors (slot, row count, row indices) reach the
-//   consumers through a 4-deep item ring.  Consumers never wait on a global
-//   load: they read shared memory and write y / v with plain stores.
+// * A thread-block cluster of CS (1 or 2) CTAs owns an item.  CTA q shrinks
+//   the K-slice q (partial v over its slice) and expands the N-slice q.  The
+//   partial v's are exchanged through distributed shared memory: each CTA
+//   pushes its partial into the peer's receive buffer with st.async, whose
+//   completion lands on the peer's mbarrier (no release fence), and both sum
+//   the partials in rank order, so the rank-R intermediate never leaves the
+//   chip in the fused kernel.
+// * Each CTA is one producer warp and four consumer warps, and two CTAs share
+//   an SM, so every SM runs two independent pipelines.  The producer feeds a
+//   4-slot ring of 21 KB slots with everything the consumers read: an A
+//   stage holds an A tile ({64 k x R rows} TMA boxes, 128-byte swizzle) plus
+//   the item's x rows for the same k range; a B stage holds a B tile
+//   ({R x n_box rows} TMA boxes) plus the item's y rows for the same columns
+//   (1-D bulk copies, one lane per row); the expand-only kernel adds a v
+//   stage.  The producer also prefetches the next item's data into L2.  Item
+//   descriptors (slot, row count, row indices) reach the consumers through a
+//   4-deep item ring.  Consumers never wait on a global load, release a slot
+//   as soon as its data is in registers (relaxed arrive) and only then issue
+//   their y stores, so no arrive waits on global stores.
 // * The item's 16 rows are one warp-MMA tile (m16n8k16, fp32 accumulate):
-//   x and v fragments are loaded once per warp and reused over every rank /
-//   output column tile, so the inner products cost neither CUDA-core issue
-//   slots nor shared-memory bandwidth (a packed-FMA version was bound by
+//   x and v fragments are loaded once and reused over every rank / output
+//   column tile of the warp, so the inner products cost neither CUDA-core
+//   issue slots nor shared-memory bandwidth (a packed-FMA version was bound by
 //   broadcast shared loads).  The expand multiplies B by v split into two
 //   16-bit halves (v = hi + lo, power-of-two scaled against overflow), which
 //   keeps the fp32 accuracy of v.
@@ -39,15 +46,15 @@
 
 namespace persona {
 
-constexpr int kConsumerWarps = 8;
+constexpr int kConsumerWarps = 4;
 constexpr int kConsumers = kConsumerWarps * 32;
 constexpr int kBgmvThreads = kConsumers + 32;  // + one producer warp
-constexpr int kSlotBytes = 20480;              // one ring slot (multiple of 1024)
-constexpr int kSlots = 10;
+constexpr int kCtasPerSm = 2;
+constexpr int kSlotBytes = 21504;              // one ring slot (multiple of 1024)
+constexpr int kSlots = 4;
 constexpr int kItemRing = 4;
-constexpr int kXWin = 512;                     // k extent of one x window
-constexpr int kXPitch = 2 * kXWin + 16;        // bytes per x row in a window slot (bank-conflict pad)
 constexpr int kMaxR = 64;
+constexpr int kMaxPeers = 1;                   // clusters of at most 2 CTAs
 constexpr int kNamedBarConsumers = 1;
 
 struct ItemDesc {
@@ -58,29 +65,37 @@ struct ItemDesc {
 };
 
 constexpr int kRingBytes = kSlots * kSlotBytes;
-constexpr int kVBytes = kRowsPerItem * kMaxR * 4;            // fp32 [16][R]
-constexpr int kRedBytes = kConsumerWarps * kRowsPerItem * 8 * 4;  // fp32 [warp][16][8]
+constexpr int kVBytes = kRowsPerItem * kMaxR * 4;  // fp32 [16][R]
+constexpr int kVFloats = kRowsPerItem * kMaxR;
+constexpr int kRecvBytes = 2 * kMaxPeers * kVBytes;  // fp32 [2][peers][16][R]
+constexpr int kRedBytes = kRowsPerItem * kMaxR * 4;  // fp32 [warp][tiles][16][8] == [16][R] worth
 constexpr int kItemBytes = kItemRing * static_cast<int>(sizeof(ItemDesc));
-constexpr int kBarCount = 2 * kSlots + 2 * kItemRing + 4;
-constexpr int kSmemLayoutBytes = kRingBytes + 4 * kVBytes + kRedBytes + kItemBytes + kBarCount * 8;
+constexpr int kBarCount = 2 * kSlots + 2 * kItemRing + 2;
+constexpr int kSmemLayoutBytes = kRingBytes + 2 * kVBytes + kRecvBytes + kRedBytes + kItemBytes + kBarCount * 8;
 constexpr int kBgmvSmemBytes = kSmemLayoutBytes + 1024;  // slack to align the base
-static_assert(kBgmvSmemBytes <= 227 * 1024, "shared memory budget");
-static_assert(kRowsPerItem * kXPitch <= kSlotBytes, "x window slot");
+static_assert(kBgmvSmemBytes * kCtasPerSm <= 228 * 1024 - 2048, "two CTAs per SM");
 
 template <int R>
 struct RankCfg {
   static_assert(R == 8 || R == 16 || R == 32 || R == 64, "rank");
-  static constexpr int kKC = (8192 / R) < kXWin ? (8192 / R) : kXWin;  // k per A stage (<= 16 KB)
+  // A stage: A tile (kKC k x R rows) + x chunk (16 rows x kKC, padded pitch).
+  static constexpr int kKC = R >= 32 ? 128 : 256;
   static constexpr int kABoxBytes = 128 * R;  // TMA box {64 k, R rows}
-  static constexpr int kNT = R / 8;           // shrink: 8-wide rank tiles
-  static constexpr int kKS = kConsumerWarps / kNT;  // shrink: warps splitting k per rank tile
-  // B rows per stage: B tile (2R bytes/row) + y tile (16 rows x 2 bytes/col) in one slot.
+  static constexpr int kXOff = kKC * 2 * R;   // byte offset of the x chunk in an A slot
+  static constexpr int kXPitch = kKC * 2 + 16;
+  static_assert(kXOff + kRowsPerItem * kXPitch <= kSlotBytes, "A slot");
+  static constexpr int kNT = R / 8;                                    // 8-wide rank tiles
+  static constexpr int kTPW = kNT >= kConsumerWarps ? kNT / kConsumerWarps : 1;  // rank tiles per warp
+  static constexpr int kKS = kNT >= kConsumerWarps ? 1 : kConsumerWarps / kNT;   // warps splitting k per tile
+  static constexpr int kMaxSteps = kKC / 16 / kKS;                     // k16 steps per warp per stage
+  // B stage: B tile (2R bytes/row) + y tile (16 rows x 2 bytes/col) in one slot.
   static constexpr int kNBraw = kSlotBytes / (2 * R + 2 * kRowsPerItem) / 8 * 8;
   static constexpr int kNB = kNBraw < 256 ? kNBraw : 256;
   static constexpr int kYOff = kNB * 2 * R;  // byte offset of the y tile in a B slot
   static constexpr int kYStride = kNB * 2;   // bytes per y-tile row
   static constexpr uint32_t kBSwz = (2 * R == 128) ? 7u : (2 * R == 64) ? 3u : (2 * R == 32) ? 1u : 0u;
   static constexpr int kKSteps = R >= 16 ? R / 16 : 1;  // expand: k16 steps over the rank
+  static constexpr int kMaxTiles = (kNB / 8 + kConsumerWarps - 1) / kConsumerWarps;  // expand tiles per warp
 };
 
 int bgmv_stage_rows(int R) {
@@ -92,18 +107,20 @@ int bgmv_stage_rows(int R) {
   }
 }
 
+int bgmv_max_cluster() { return kMaxPeers + 1; }
+
 struct SmemPtrs {
   uint8_t* ring;
-  float* pv;   // [2][16][R] this CTA's partial v
-  float* vf;   // [2][16][R] full v of the item
-  float* red;  // [warp][16][8] per-warp MMA tiles / maxima
+  float* pv;    // [16][R] this CTA's partial v of the current item
+  float* vf;    // [16][R] full v of the current item
+  float* recv;  // [2][peers][16][R] partial v pushed here by the cluster peer
+  float* red;   // per-warp MMA tiles / maxima
   ItemDesc* items;
-  uint64_t* full;    // [kSlots]
-  uint64_t* empty;   // [kSlots]
-  uint64_t* ifull;   // [kItemRing]
-  uint64_t* iempty;  // [kItemRing]
-  uint64_t* red_bar; // [2]
-  uint64_t* gat_bar; // [2]
+  uint64_t* full;      // [kSlots]
+  uint64_t* empty;     // [kSlots]
+  uint64_t* ifull;     // [kItemRing]
+  uint64_t* iempty;    // [kItemRing]
+  uint64_t* recv_bar;  // [2] completes when the peer's partial has landed
 };
 
 __device__ __forceinline__ SmemPtrs carve_smem(uint8_t* raw) {
@@ -112,20 +129,18 @@ __device__ __forceinline__ SmemPtrs carve_smem(uint8_t* raw) {
   p.ring = base;
   uint8_t* q = base + kRingBytes;
   p.pv = reinterpret_cast<float*>(q);
-  p.vf = reinterpret_cast<float*>(q + 2 * kVBytes);
-  p.red = reinterpret_cast<float*>(q + 4 * kVBytes);
-  p.items = reinterpret_cast<ItemDesc*>(q + 4 * kVBytes + kRedBytes);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(q + 4 * kVBytes + kRedBytes + kItemBytes);
+  p.vf = reinterpret_cast<float*>(q + kVBytes);
+  p.recv = reinterpret_cast<float*>(q + 2 * kVBytes);
+  p.red = reinterpret_cast<float*>(q + 2 * kVBytes + kRecvBytes);
+  p.items = reinterpret_cast<ItemDesc*>(q + 2 * kVBytes + kRecvBytes + kRedBytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(q + 2 * kVBytes + kRecvBytes + kRedBytes + kItemBytes);
   p.full = bars;
   p.empty = bars + kSlots;
   p.ifull = bars + 2 * kSlots;
   p.iempty = bars + 2 * kSlots + kItemRing;
-  p.red_bar = bars + 2 * kSlots + 2 * kItemRing;
-  p.gat_bar = p.red_bar + 2;
+  p.recv_bar = bars + 2 * kSlots + 2 * kItemRing;
   return p;
 }
-
-__device__ __forceinline__ float2 f2(float a, float b) { return make_float2(a, b); }
 
 // The j-th item of cluster `cid` out of `ncl`: rounds of ncl items, visited in
 // serpentine order so that clusters that take a heavy (early) item in one
@@ -135,75 +150,129 @@ __device__ __forceinline__ int item_of(int cid, int ncl, int j) {
 }
 
 // ---------------------------------------------------------------- shrink --
-// One A stage: d (this warp's 16 rows x 8 ranks tile) += x[16][k] * A[ranks][k]
-// over the k16 steps of the stage this warp owns (warps sharing a rank tile
-// split the steps).  x16 is the smem address of this lane's ldmatrix row in
-// the x window at the stage's first column.
+// One A stage: this warp's rank tiles d[t] (16 rows x 8 ranks) += x * A^T over
+// the k16 steps it owns (warps sharing a rank tile split the steps).  All
+// fragments are loaded before the MMAs, which alternate between two
+// accumulators, so shared-memory and MMA latency overlap.
 template <typename DT, int R>
-__device__ __forceinline__ void shrink_stage(uint32_t abase, uint32_t x16, int ksteps, int warp, int lane,
-                                             float (&d)[4]) {
+__device__ __forceinline__ void shrink_stage(const uint8_t* stage, int ksteps, int warp, int lane,
+                                             float (&d)[RankCfg<R>::kTPW][2][4]) {
   using C = RankCfg<R>;
-  const int ntile = warp % C::kNT;
-  const int ksplit = warp / C::kNT;
-  const int r = ntile * 8 + (lane & 7);
+  const uint32_t abase = smem_u32(stage);
+  const uint32_t x16 = abase + C::kXOff + (lane & 15) * C::kXPitch + ((lane >> 4) * 8) * 2;
+  const int ksplit = warp % C::kKS;
+  const int tile0 = (warp / C::kKS) * C::kTPW;
   const int uofs = (lane >> 3) & 1;
-  for (int ks = ksplit; ks < ksteps; ks += C::kKS) {
-    uint32_t a[4], b[2];
-    ldsm_x4(x16 + ks * 32, a);
-    const int ku = ks * 2 + uofs;
-    const int bx = ku >> 3, u = ku & 7;
-    ldsm_x2(abase + bx * C::kABoxBytes + r * 128 + ((u ^ (r & 7)) << 4), b);
-    Mma<DT>::k16(d, a, b);
+  uint32_t a[C::kMaxSteps][4], b[C::kMaxSteps][C::kTPW][2];
+#pragma unroll
+  for (int i = 0; i < C::kMaxSteps; ++i) {
+    const int ks = ksplit + i * C::kKS;
+    if (ks < ksteps) {
+      ldsm_x4(x16 + ks * 32, a[i]);
+      const int ku = ks * 2 + uofs;
+      const int bx = ku >> 3, u = ku & 7;
+#pragma unroll
+      for (int t = 0; t < C::kTPW; ++t) {
+        const int r = (tile0 + t) * 8 + (lane & 7);
+        ldsm_x2(abase + bx * C::kABoxBytes + r * 128 + ((u ^ (r & 7)) << 4), b[i][t]);
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < C::kMaxSteps; ++i) {
+    if (ksplit + i * C::kKS < ksteps) {
+#pragma unroll
+      for (int t = 0; t < C::kTPW; ++t) Mma<DT>::k16(d[t][i & 1], a[i], b[i][t]);
+    }
   }
 }
 
 // ---------------------------------------------------------------- expand --
 // One B stage: for each 8-column tile this warp owns,
 // y[row][n] = round(y_tile[row][n] + scale * (v_hi + v_lo)[row] . B[n]).
+// The slot is released (relaxed arrive on `empty`) as soon as its data is in
+// registers, before the y stores, so that no arrive waits on global stores.
 template <typename DT, int R>
 __device__ __forceinline__ void expand_stage(const uint8_t* stage, const uint32_t (&vhi)[RankCfg<R>::kKSteps][4],
                                              const uint32_t (&vlo)[RankCfg<R>::kKSteps][4], int rows_here,
                                              int n_box, int n0, int c, const int* rows, uint16_t* y, int64_t ldy,
-                                             float scale, int warp, int lane) {
+                                             float scale, int warp, int lane, uint64_t* empty) {
   using C = RankCfg<R>;
+  constexpr int kMT = C::kMaxTiles;
+  constexpr int KS = C::kKSteps;
   const uint32_t sbase = smem_u32(stage);
   const uint8_t* ytile = stage + C::kYOff;
   const int g = lane >> 2, t = lane & 3;
   const int tiles = rows_here >> 3;
-  for (int tile = warp; tile < tiles; tile += kConsumerWarps) {
-    const int nl = tile * 8;
-    const int bx = nl / n_box;
-    const int rib = nl - bx * n_box + (lane & 7);
-    const uint32_t boff = sbase + static_cast<uint32_t>(bx * n_box * 2 * R);
-    float d[4] = {0.f, 0.f, 0.f, 0.f};
-    if (R >= 16) {
+  uint32_t bf[kMT][KS][2];
 #pragma unroll
-      for (int ks = 0; ks < C::kKSteps; ++ks) {
-        uint32_t b[2];
-        const int u = ks * 2 + ((lane >> 3) & 1);
-        ldsm_x2(boff + swz(static_cast<uint32_t>(rib * 2 * R + u * 16), C::kBSwz), b);
-        Mma<DT>::k16(d, vhi[ks], b);
-        Mma<DT>::k16(d, vlo[ks], b);
+  for (int ti = 0; ti < kMT; ++ti) {
+    const int tile = warp + ti * kConsumerWarps;
+    if (tile < tiles) {
+      const int nl = tile * 8;
+      const int bx = nl / n_box;
+      const int rib = nl - bx * n_box + (lane & 7);
+      const uint32_t boff = sbase + static_cast<uint32_t>(bx * n_box * 2 * R);
+      if (R >= 16) {
+#pragma unroll
+        for (int ks = 0; ks < KS; ++ks) {
+          const int u = ks * 2 + ((lane >> 3) & 1);
+          ldsm_x2(boff + swz(static_cast<uint32_t>(rib * 2 * R + u * 16), C::kBSwz), bf[ti][ks]);
+        }
+      } else {
+        ldsm_x1(boff + static_cast<uint32_t>(rib * 2 * R), bf[ti][0][0]);
       }
-    } else {
-      uint32_t b;
-      ldsm_x1(boff + static_cast<uint32_t>(rib * 2 * R), b);
-      const uint32_t ah[2] = {vhi[0][0], vhi[0][1]};
-      const uint32_t al[2] = {vlo[0][0], vlo[0][1]};
-      Mma<DT>::k8(d, ah, b);
-      Mma<DT>::k8(d, al, b);
     }
-    // d[0..1]: row g, columns nl+2t, nl+2t+1; d[2..3]: row g+8.
-    const int col = nl + 2 * t;
+  }
+  float dh[kMT][4], dl[kMT][4];
+#pragma unroll
+  for (int ti = 0; ti < kMT; ++ti) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) dh[ti][i] = dl[ti][i] = 0.f;
+    if (warp + ti * kConsumerWarps < tiles) {
+      if (R >= 16) {
+#pragma unroll
+        for (int ks = 0; ks < KS; ++ks) {
+          Mma<DT>::k16(dh[ti], vhi[ks], bf[ti][ks]);
+          Mma<DT>::k16(dl[ti], vlo[ks], bf[ti][ks]);
+        }
+      } else {
+        const uint32_t ah[2] = {vhi[0][0], vhi[0][1]};
+        const uint32_t al[2] = {vlo[0][0], vlo[0][1]};
+        Mma<DT>::k8(dh[ti], ah, bf[ti][0][0]);
+        Mma<DT>::k8(dl[ti], al, bf[ti][0][0]);
+      }
+    }
+  }
+  uint32_t out[kMT][2];
+#pragma unroll
+  for (int ti = 0; ti < kMT; ++ti) {
+    const int tile = warp + ti * kConsumerWarps;
+    // dh/dl[0..1]: row g, columns nl+2t, nl+2t+1; [2..3]: row g+8.
+    const int col = tile * 8 + 2 * t;
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       const int row = g + 8 * h;
-      if (row < c) {
+      out[ti][h] = 0u;
+      if (tile < tiles && row < c) {
         const uint32_t yw = *reinterpret_cast<const uint32_t*>(ytile + row * C::kYStride + col * 2);
         const float2 yo = Cvt<DT>::to2(yw);
-        const uint32_t out = Mma<DT>::pack(yo.x + scale * d[2 * h], yo.y + scale * d[2 * h + 1]);
-        *reinterpret_cast<uint32_t*>(y + static_cast<int64_t>(rows[row]) * ldy + n0 + col) = out;
+        const float s0 = dh[ti][2 * h] + dl[ti][2 * h], s1 = dh[ti][2 * h + 1] + dl[ti][2 * h + 1];
+        out[ti][h] = Mma<DT>::pack(yo.x + scale * s0, yo.y + scale * s1);
       }
+    }
+  }
+  __syncwarp();
+  if (lane == 0) mbar_arrive_relaxed(empty);
+#pragma unroll
+  for (int ti = 0; ti < kMT; ++ti) {
+    const int tile = warp + ti * kConsumerWarps;
+    const int col = tile * 8 + 2 * t;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int row = g + 8 * h;
+      if (tile < tiles && row < c)
+        *reinterpret_cast<uint32_t*>(y + static_cast<int64_t>(rows[row]) * ldy + n0 + col) = out[ti][h];
     }
   }
 }
@@ -239,7 +308,7 @@ __device__ __forceinline__ void v_fragments(const float* vf, float scale_down, i
 }
 
 template <typename DT, int R, int MODE>
-__global__ void __launch_bounds__(kBgmvThreads, 1)
+__global__ void __launch_bounds__(kBgmvThreads, kCtasPerSm)
     bgmv_cluster_kernel(const __grid_constant__ CUtensorMap tmA,
                         const __grid_constant__ CUtensorMap tmB, const BgmvArgs args) {
   using C = RankCfg<R>;
@@ -264,10 +333,7 @@ __global__ void __launch_bounds__(kBgmvThreads, 1)
       mbar_init(&sm.ifull[i], 1);
       mbar_init(&sm.iempty[i], kConsumerWarps);
     }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&sm.red_bar[b], CS);
-      mbar_init(&sm.gat_bar[b], CS);
-    }
+    for (int b = 0; b < 2; ++b) mbar_init(&sm.recv_bar[b], 1);
     fence_mbar_init_cluster();
   }
   cluster_sync_all();
@@ -326,22 +392,18 @@ __global__ void __launch_bounds__(kBgmvThreads, 1)
       if (nitem < n_items) nit = pv.items[nitem];
 
       if (kDoShrink) {
-        for (int w0 = kbeg; w0 < kend; w0 += kXWin) {
-          const int wend = min(kend, w0 + kXWin);
-          const uint32_t xb = static_cast<uint32_t>(wend - w0) * 2u;
-          int s = claim(static_cast<uint32_t>(c) * xb);
+        for (int k0 = kbeg; k0 < kend; k0 += C::kKC) {
+          const int valid = min(C::kKC, kend - k0);
+          const int nbox = (valid + 63) / 64;
+          const uint32_t xb = static_cast<uint32_t>(valid) * 2u;
+          const int s = claim(static_cast<uint32_t>(nbox * C::kABoxBytes) + static_cast<uint32_t>(c) * xb);
+          uint8_t* st = sm.ring + s * kSlotBytes;
+          if (lane == 0)
+            for (int b = 0; b < nbox; ++b) tma_load_3d(st + b * C::kABoxBytes, &tmA, &sm.full[s], k0 + 64 * b, 0, slot);
           if (lane < c)
-            bulk_load(sm.ring + s * kSlotBytes + lane * kXPitch, x + static_cast<int64_t>(row) * args.ldx + w0,
-                      xb, &sm.full[s]);
+            bulk_load(st + C::kXOff + lane * C::kXPitch, x + static_cast<int64_t>(row) * args.ldx + k0, xb,
+                      &sm.full[s]);
           ++g;
-          for (int k0 = w0; k0 < wend; k0 += C::kKC) {
-            const int nbox = (min(C::kKC, wend - k0) + 63) / 64;
-            s = claim(static_cast<uint32_t>(nbox * C::kABoxBytes));
-            if (lane == 0)
-              for (int b = 0; b < nbox; ++b)
-                tma_load_3d(sm.ring + s * kSlotBytes + b * C::kABoxBytes, &tmA, &sm.full[s], k0 + 64 * b, 0, slot);
-            ++g;
-          }
         }
       }
       // The next item's rows (its descriptor has long arrived by now), then an
@@ -378,13 +440,13 @@ __global__ void __launch_bounds__(kBgmvThreads, 1)
           const int nbox = (rows_here + args.n_box - 1) / args.n_box;
           const uint32_t yb = static_cast<uint32_t>(rows_here) * 2u;
           const int s = claim(static_cast<uint32_t>(nbox * args.n_box * 2 * R) + static_cast<uint32_t>(c) * yb);
+          uint8_t* st = sm.ring + s * kSlotBytes;
           if (lane == 0)
             for (int b = 0; b < nbox; ++b)
-              tma_load_3d(sm.ring + s * kSlotBytes + b * args.n_box * 2 * R, &tmB, &sm.full[s], 0,
-                          n0 + b * args.n_box, slot);
+              tma_load_3d(st + b * args.n_box * 2 * R, &tmB, &sm.full[s], 0, n0 + b * args.n_box, slot);
           if (lane < c)
-            bulk_load(sm.ring + s * kSlotBytes + C::kYOff + lane * C::kYStride,
-                      yg + static_cast<int64_t>(row) * args.ldy + n0, yb, &sm.full[s]);
+            bulk_load(st + C::kYOff + lane * C::kYStride, yg + static_cast<int64_t>(row) * args.ldy + n0, yb,
+                      &sm.full[s]);
           ++g;
         }
       }
@@ -414,93 +476,88 @@ __global__ void __launch_bounds__(kBgmvThreads, 1)
       const int c = itd->count;
       const int* rows = itd->rows;
       const int b = j & 1;
-      const uint32_t red_parity = (j >> 1) & 1;
-      float* pvb = sm.pv + b * kRowsPerItem * kMaxR;
-      float* vfb = sm.vf + b * kRowsPerItem * kMaxR;
+      const uint32_t recv_parity = (j >> 1) & 1;
+      float* pvb = sm.pv;
+      float* vfb = sm.vf;
       const int E = c * R;  // live entries of v (rows < c)
+      // Bytes the peer will push into recv[b] for this item (its partial v).
+      if (kDoShrink && tid == 0)
+        mbar_arrive_expect_tx(&sm.recv_bar[b], (CS - 1) * static_cast<uint32_t>(E) * 4u);
 
       if (kDoShrink) {
-        float d[4] = {0.f, 0.f, 0.f, 0.f};
-        for (int w0 = kbeg; w0 < kend; w0 += kXWin) {
-          const int wend = min(kend, w0 + kXWin);
-          const int sx = static_cast<int>(g % kSlots);
-          mbar_wait(&sm.full[sx], (g / kSlots) & 1, args.err);
-          ++g;
-          uint8_t* xs = sm.ring + sx * kSlotBytes;
-          const int valid = wend - w0;
+        float d[C::kTPW][2][4];
+#pragma unroll
+        for (int t = 0; t < C::kTPW; ++t)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) d[t][0][i] = d[t][1][i] = 0.f;
+        for (int k0 = kbeg; k0 < kend; k0 += C::kKC, ++g) {
+          const int s = static_cast<int>(g % kSlots);
+          mbar_wait(&sm.full[s], (g / kSlots) & 1, args.err);
+          uint8_t* st = sm.ring + s * kSlotBytes;
+          const int valid = min(C::kKC, kend - k0);
           if (valid & 63) {
             // The last A tile reads zeros past K; zero the matching x columns so
             // that stale shared memory cannot inject NaN * 0.
             const int tail = ((valid + 63) & ~63) - valid;
             for (int e = tid; e < c * tail; e += kConsumers) {
               const int rr = e / tail, kk = valid + e % tail;
-              reinterpret_cast<uint16_t*>(xs + rr * kXPitch)[kk] = 0;
+              reinterpret_cast<uint16_t*>(st + C::kXOff + rr * C::kXPitch)[kk] = 0;
             }
             named_sync(kNamedBarConsumers, kConsumers);
           }
-          const uint32_t x16 = smem_u32(xs) + (lane & 15) * kXPitch + ((lane >> 4) * 8) * 2;
-          for (int k0 = w0; k0 < wend; k0 += C::kKC, ++g) {
-            const int s = static_cast<int>(g % kSlots);
-            mbar_wait(&sm.full[s], (g / kSlots) & 1, args.err);
-            const int ksteps = ((min(C::kKC, wend - k0) + 63) / 64) * 4;
-            shrink_stage<DT, R>(smem_u32(sm.ring + s * kSlotBytes), x16 + (k0 - w0) * 2, ksteps, warp, lane, d);
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&sm.empty[s]);
-          }
+          shrink_stage<DT, R>(st, ((valid + 63) / 64) * 4, warp, lane, d);
           __syncwarp();
-          if (lane == 0) mbar_arrive(&sm.empty[sx]);  // x window no longer read
+          if (lane == 0) mbar_arrive_relaxed(&sm.empty[s]);
         }
-        // This CTA's partial v: sum the warps that split k for each rank tile.
-        {
-          float* rw = sm.red + warp * (kRowsPerItem * 8);
+        // This CTA's partial v: sum the two accumulators and the warps that
+        // split k for each rank tile.
+#pragma unroll
+        for (int t = 0; t < C::kTPW; ++t) {
+          float* rw = sm.red + (warp * C::kTPW + t) * (kRowsPerItem * 8);
           const int gg = lane >> 2, tt = lane & 3;
-          rw[gg * 8 + 2 * tt] = d[0];
-          rw[gg * 8 + 2 * tt + 1] = d[1];
-          rw[(gg + 8) * 8 + 2 * tt] = d[2];
-          rw[(gg + 8) * 8 + 2 * tt + 1] = d[3];
+          rw[gg * 8 + 2 * tt] = d[t][0][0] + d[t][1][0];
+          rw[gg * 8 + 2 * tt + 1] = d[t][0][1] + d[t][1][1];
+          rw[(gg + 8) * 8 + 2 * tt] = d[t][0][2] + d[t][1][2];
+          rw[(gg + 8) * 8 + 2 * tt + 1] = d[t][0][3] + d[t][1][3];
         }
         named_sync(kNamedBarConsumers, kConsumers);
         for (int e = tid; e < E; e += kConsumers) {
           const int rr = e / R, r = e - rr * R;
-          const int nt = r >> 3, col = r & 7;
+          const int T = r >> 3, col = r & 7;
           float sum = 0.f;
 #pragma unroll
-          for (int ks = 0; ks < C::kKS; ++ks) sum += sm.red[(nt + ks * C::kNT) * (kRowsPerItem * 8) + rr * 8 + col];
+          for (int ks = 0; ks < C::kKS; ++ks)
+            sum += sm.red[(((T / C::kTPW) * C::kKS + ks) * C::kTPW + (T % C::kTPW)) * (kRowsPerItem * 8) +
+                          rr * 8 + col];
           pvb[e] = sum;
         }
-        // Cluster reduce-scatter of the partial v's through DSMEM.
+        // Exchange through DSMEM: push this CTA's partial to the peer with
+        // st.async (completing on the peer's recv barrier), then sum the
+        // partials in rank order, so both CTAs hold the bit-identical full v.
         named_sync(kNamedBarConsumers, kConsumers);
-        if (tid == 0) {
-          fence_acq_rel_cluster();
-          for (uint32_t r = 0; r < CS; ++r) mbar_arrive_remote(&sm.red_bar[b], r);
-        }
-        mbar_wait<true>(&sm.red_bar[b], red_parity, args.err);
-        const int E2 = E >> 1;  // float2 entries (R is even)
-        const int share = (E2 + static_cast<int>(CS) - 1) / static_cast<int>(CS);
-        const int e_lo = static_cast<int>(q) * share;
-        const int e_hi = min(E2, e_lo + share);
-        for (int e = e_lo + tid; e < e_hi; e += kConsumers) {
-          float2 sum = f2(0.f, 0.f);
-          for (uint32_t r = 0; r < CS; ++r) {
-            const float2 t2 = ld_dsmem_f2(mapa(pvb + 2 * e, r));
-            sum.x += t2.x;
-            sum.y += t2.y;
-          }
-          if (MODE == kModeFused) {
-            for (uint32_t r = 0; r < CS; ++r) st_dsmem_f2(mapa(vfb + 2 * e, r), sum);
-          } else {
-            const int rr = (2 * e) / R, r = 2 * e - rr * R;
-            *reinterpret_cast<float2*>(args.v_out + static_cast<int64_t>(rows[rr]) * R + r) = sum;
+        if (CS > 1) {
+          for (int e4 = tid; e4 < (E >> 2); e4 += kConsumers) {
+            const float4 val = *reinterpret_cast<const float4*>(pvb + 4 * e4);
+            for (uint32_t r = 0; r < CS; ++r) {
+              if (r == q) continue;
+              const int pslot = q < r ? static_cast<int>(q) : static_cast<int>(q) - 1;  // my slot at peer r
+              st_async_v4(sm.recv + (b * kMaxPeers + pslot) * kVFloats + 4 * e4, &sm.recv_bar[b], r, val);
+            }
           }
         }
-        if (MODE == kModeFused) {
-          named_sync(kNamedBarConsumers, kConsumers);
-          if (tid == 0) {
-            fence_acq_rel_cluster();
-            for (uint32_t r = 0; r < CS; ++r) mbar_arrive_remote(&sm.gat_bar[b], r);
+        mbar_wait<true>(&sm.recv_bar[b], recv_parity, args.err);
+        const float* rb = sm.recv + b * kMaxPeers * kVFloats;
+        const int share = (E + static_cast<int>(CS) - 1) / static_cast<int>(CS);
+        for (int e = tid; e < E; e += kConsumers) {
+          float sum = 0.f;
+          for (uint32_t r = 0; r < CS; ++r) sum += r == q ? pvb[e] : rb[(r < q ? r : r - 1) * kVFloats + e];
+          vfb[e] = sum;
+          if (MODE == kModeShrink && e / share == static_cast<int>(q)) {
+            const int rr = e / R, rk = e - rr * R;  // CTA q writes the entries of share q
+            args.v_out[static_cast<int64_t>(rows[rr]) * R + rk] = sum;
           }
-          mbar_wait<true>(&sm.gat_bar[b], red_parity, args.err);
         }
+        named_sync(kNamedBarConsumers, kConsumers);
       }
 
       if (kDoExpand) {
@@ -510,19 +567,18 @@ __global__ void __launch_bounds__(kBgmvThreads, 1)
           const float* vs = reinterpret_cast<const float*>(sm.ring + s * kSlotBytes);
           for (int e = tid; e < E; e += kConsumers) vfb[e] = vs[e];
           __syncwarp();
-          if (lane == 0) mbar_arrive(&sm.empty[s]);
+          if (lane == 0) mbar_arrive_relaxed(&sm.empty[s]);
           ++g;
           named_sync(kNamedBarConsumers, kConsumers);
         }
         // Power-of-two scale that keeps the 16-bit v halves finite (f16 only).
         float scale_down = 1.f, scale_up = 1.f;
-        if (sizeof(DT) == 2 && std::is_same<DT, __half>::value) {
+        if (std::is_same<DT, __half>::value) {
           float m = 0.f;
           for (int e = tid; e < E; e += kConsumers) m = fmaxf(m, fabsf(vfb[e]));
 #pragma unroll
           for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
-          named_sync(kNamedBarConsumers, kConsumers);  // red[] free (shrink reduction done)
-          if (lane == 0) sm.red[warp] = m;
+          if (lane == 0) sm.red[warp] = m;  // red[] is free: the shrink reduction is done
           named_sync(kNamedBarConsumers, kConsumers);
           m = sm.red[0];
 #pragma unroll
@@ -541,14 +597,14 @@ __global__ void __launch_bounds__(kBgmvThreads, 1)
           mbar_wait(&sm.full[s], (g / kSlots) & 1, args.err);
           const int rows_here = min(stage_rows, nend - n0);
           expand_stage<DT, R>(sm.ring + s * kSlotBytes, vhi, vlo, rows_here, args.n_box, n0, c, rows, y, args.ldy,
-                              scale_up, warp, lane);
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&sm.empty[s]);
+                              scale_up, warp, lane, &sm.empty[s]);
         }
+        // the next item overwrites red[] / vf only after named syncs
+        named_sync(kNamedBarConsumers, kConsumers);
       }
       // done with this item's descriptor
       __syncwarp();
-      if (lane == 0) mbar_arrive(&sm.iempty[iq]);
+      if (lane == 0) mbar_arrive_relaxed(&sm.iempty[iq]);
     }
   }
   // No CTA may leave while a peer can still reach its shared memory.
@@ -563,21 +619,18 @@ static cudaError_t launch_one(const CUtensorMap& tmA, const CUtensorMap& tmB, co
                               int cluster_size, int max_clusters, cudaStream_t stream) {
   auto kern = bgmv_cluster_kernel<DT, R, MODE>;
   // Function attributes and occupancy are per device; cache both per device
-  // and per cluster size (1, 2, 4, 8, 16).
+  // and per cluster size (1, 2).
   constexpr int kMaxDev = 64;
   static bool configured[kMaxDev] = {};
-  static int occ[kMaxDev][5] = {};
+  static int occ[kMaxDev][2] = {};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= kMaxDev) return cudaErrorInvalidDevice;
-  int ci = 0;
-  while ((1 << ci) < cluster_size && ci < 4) ++ci;
-  if ((1 << ci) != cluster_size) return cudaErrorInvalidValue;
+  if (cluster_size != 1 && cluster_size != 2) return cudaErrorInvalidValue;
+  const int ci = cluster_size - 1;
   if (!configured[dev]) {
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kBgmvSmemBytes);
-    if (e != cudaSuccess) return e;
-    e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     if (e != cudaSuccess) return e;
     configured[dev] = true;
   }

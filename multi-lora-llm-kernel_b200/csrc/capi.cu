@@ -37,17 +37,18 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 
 bool rank_supported(int64_t R) { return R == 8 || R == 16 || R == 32 || R == 64; }
 constexpr int64_t kI32Max = 2147483647;
 
-// Cluster size: 8 CTAs when the batch is small (few items, so each is split
-// finely to occupy the GPU), 4 otherwise (more clusters resident, a cheaper
-// reduction per item).  PERSONA_CLUSTER_SIZE (1, 2, 4, 8 or 16) overrides.
+// Cluster size: 2 CTAs (each shrinks half of K and expands half of N of an
+// item, so twice as many CTAs share the work of the batch's items).  The
+// kernel holds one peer receive buffer, so 2 is the maximum.
+// PERSONA_CLUSTER_SIZE (1 or 2) overrides.
 int cluster_size_for(int64_t T) {
   static const int forced = [] {
     const char* e = std::getenv("PERSONA_CLUSTER_SIZE");
     const int v = e ? std::atoi(e) : 0;
-    return (v == 1 || v == 2 || v == 4 || v == 8 || v == 16) ? v : 0;
+    return (v == 1 || v == 2) ? v : 0;
   }();
-  if (forced) return forced;
-  return T <= 32 ? 8 : 4;
+  (void)T;
+  return forced ? forced : 2;
 }
 
 // A pool [S, R, K] (k fastest) as a 3-D tensor {K, R, S}; box {64 k, R rows, 1 slot}.

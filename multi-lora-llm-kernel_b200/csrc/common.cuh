@@ -93,6 +93,29 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
       : "memory");
 }
 
+// Relaxed arrive: no release fence, so it never waits for the thread's earlier
+// global stores.  Used where the only ordering that matters is that the
+// caller's shared-memory reads are done, which holds because their values
+// have already been consumed.
+__device__ __forceinline__ void mbar_arrive_relaxed(uint64_t* bar) {
+  asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.relaxed.cta.shared::cta.b64 st, [%0];\n\t}" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+
+// 16-byte asynchronous store into CTA `rank`'s shared memory (same offset as
+// `dst` here) that completes `bytes` of the transaction count of the mbarrier
+// at `bar`'s offset in that CTA: the receiver learns the data has landed by
+// waiting on its own barrier, with no release fence on the sender.
+__device__ __forceinline__ void st_async_v4(const void* dst, const uint64_t* bar, uint32_t rank, float4 v) {
+  asm volatile(
+      "{\n\t.reg .b32 ra, rb;\n\tmapa.shared::cluster.u32 ra, %0, %1;\n\tmapa.shared::cluster.u32 rb, %2, %1;\n\t"
+      "st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [ra], {%3, %4, %5, %6}, [rb];\n\t}" ::"r"(
+          smem_u32(dst)),
+      "r"(rank), "r"(smem_u32(bar)), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
+      : "memory");
+}
+
 // Arrive (release, cluster scope) on the mbarrier at the same smem offset in
 // CTA `cta_rank` of this cluster.
 __device__ __forceinline__ void mbar_arrive_remote(uint64_t* bar, uint32_t cta_rank) {
@@ -275,14 +298,14 @@ __device__ __forceinline__ void ldsm_x1(uint32_t addr, uint32_t& r) {
 template <typename DT> struct Mma;
 template <> struct Mma<__half> {
   static __device__ __forceinline__ void k16(float (&d)[4], const uint32_t (&a)[4], const uint32_t (&b)[2]) {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
         "{%0, %1, %2, %3};"
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
   }
   static __device__ __forceinline__ void k8(float (&d)[4], const uint32_t (&a)[2], uint32_t b) {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k8.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5}, {%6}, {%0, %1, %2, %3};"
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
         : "r"(a[0]), "r"(a[1]), "r"(b));
@@ -296,14 +319,14 @@ template <> struct Mma<__half> {
 };
 template <> struct Mma<__nv_bfloat16> {
   static __device__ __forceinline__ void k16(float (&d)[4], const uint32_t (&a)[4], const uint32_t (&b)[2]) {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
         "{%0, %1, %2, %3};"
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
   }
   static __device__ __forceinline__ void k8(float (&d)[4], const uint32_t (&a)[2], uint32_t b) {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k8.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5}, {%6}, {%0, %1, %2, %3};"
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
         : "r"(a[0]), "r"(a[1]), "r"(b));
