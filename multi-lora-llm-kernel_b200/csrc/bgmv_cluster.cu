@@ -89,10 +89,11 @@ struct RankCfg {
   static constexpr int kKS = kNT >= kConsumerWarps ? 1 : kConsumerWarps / kNT;   // warps splitting k per tile
   static constexpr int kMaxSteps = kKC / 16 / kKS;                     // k16 steps per warp per stage
   // B stage: B tile (2R bytes/row) + y tile (16 rows x 2 bytes/col) in one slot.
-  static constexpr int kNBraw = kSlotBytes / (2 * R + 2 * kRowsPerItem) / 8 * 8;
+  static constexpr int kNBraw = (kSlotBytes - 16 * kRowsPerItem) / (2 * R + 2 * kRowsPerItem) / 8 * 8;
   static constexpr int kNB = kNBraw < 256 ? kNBraw : 256;
-  static constexpr int kYOff = kNB * 2 * R;  // byte offset of the y tile in a B slot
-  static constexpr int kYStride = kNB * 2;   // bytes per y-tile row
+  static constexpr int kYOff = kNB * 2 * R;     // byte offset of the y tile in a B slot
+  static constexpr int kYStride = kNB * 2 + 16;  // bytes per y-tile row (padded: rows land on distinct banks)
+  static_assert(kYOff + kRowsPerItem * kYStride <= kSlotBytes, "B slot");
   static constexpr uint32_t kBSwz = (2 * R == 128) ? 7u : (2 * R == 64) ? 3u : (2 * R == 32) ? 1u : 0u;
   static constexpr int kKSteps = R >= 16 ? R / 16 : 1;  // expand: k16 steps over the rank
   static constexpr int kMaxTiles = (kNB / 8 + kConsumerWarps - 1) / kConsumerWarps;  // expand tiles per warp
@@ -201,7 +202,7 @@ __device__ __forceinline__ void expand_stage(const uint8_t* stage, const uint32_
   constexpr int kMT = C::kMaxTiles;
   constexpr int KS = C::kKSteps;
   const uint32_t sbase = smem_u32(stage);
-  const uint8_t* ytile = stage + C::kYOff;
+  const uint32_t ytile = sbase + C::kYOff;
   const int g = lane >> 2, t = lane & 3;
   const int tiles = rows_here >> 3;
   uint32_t bf[kMT][KS][2];
@@ -255,13 +256,15 @@ __device__ __forceinline__ void expand_stage(const uint8_t* stage, const uint32_
       const int row = g + 8 * h;
       out[ti][h] = 0u;
       if (tile < tiles && row < c) {
-        const uint32_t yw = *reinterpret_cast<const uint32_t*>(ytile + row * C::kYStride + col * 2);
+        const uint32_t yw = lds32(ytile + row * C::kYStride + col * 2);
         const float2 yo = Cvt<DT>::to2(yw);
         const float s0 = dh[ti][2 * h] + dl[ti][2 * h], s1 = dh[ti][2 * h + 1] + dl[ti][2 * h + 1];
         out[ti][h] = Mma<DT>::pack(yo.x + scale * s0, yo.y + scale * s1);
       }
     }
   }
+  const int row0 = g < c ? static_cast<int>(lds32(smem_u32(rows + g))) : 0;
+  const int row1 = g + 8 < c ? static_cast<int>(lds32(smem_u32(rows + g + 8))) : 0;
   __syncwarp();
   if (lane == 0) mbar_arrive_relaxed(empty);
 #pragma unroll
@@ -272,7 +275,7 @@ __device__ __forceinline__ void expand_stage(const uint8_t* stage, const uint32_
     for (int h = 0; h < 2; ++h) {
       const int row = g + 8 * h;
       if (tile < tiles && row < c)
-        *reinterpret_cast<uint32_t*>(y + static_cast<int64_t>(rows[row]) * ldy + n0 + col) = out[ti][h];
+        *reinterpret_cast<uint32_t*>(y + static_cast<int64_t>(h ? row1 : row0) * ldy + n0 + col) = out[ti][h];
     }
   }
 }
