@@ -105,6 +105,33 @@ int persona_bgmv_fused(const void* x, int64_t ldx, const void* a_pool, int64_t a
                        size_t workspace_bytes, int flags, int32_t* dev_err,
                        cudaStream_t stream);
 
+/* ---- segmented (SGMV) ------------------------------------------------------
+ * A prefill batch whose rows are grouped contiguously by adapter: segment i
+ * covers rows [seg_indptr[i], seg_indptr[i+1]) and uses slot seg_slots[i]
+ * (-1 = no adapter).  Rows outside every segment behave like slot -1.  The
+ * results equal the BGMV ops on the per-row slots the segments imply, which
+ * is how the reference's callers express a prefill (LoRAContext.set_batch_slots,
+ * persona/lora_layer.py:21-28); the reference itself has no segmented op.
+ * seg_indptr [num_segments + 1] and seg_slots [num_segments] are int32 device
+ * arrays; a decreasing or out-of-range seg_indptr sets PERSONA_DEV_ERR_SEGMENT
+ * and the offending segment is skipped.  Workspace: persona_sgmv_workspace_size(T). */
+size_t persona_sgmv_workspace_size(int64_t T);
+int persona_sgmv_shrink(const void* x, int64_t ldx, const void* a_pool, int64_t a_slot_stride,
+                        int64_t a_row_stride, const int32_t* seg_indptr, const int32_t* seg_slots,
+                        int64_t num_segments, float* v, int64_t T, int64_t K, int64_t R, int64_t S,
+                        int dtype, void* workspace, size_t workspace_bytes, int32_t* dev_err,
+                        cudaStream_t stream);
+int persona_sgmv_expand(const float* v, const void* b_pool, int64_t b_slot_stride,
+                        const int32_t* seg_indptr, const int32_t* seg_slots, int64_t num_segments,
+                        void* y, int64_t ldy, int64_t T, int64_t N, int64_t R, int64_t S, int dtype,
+                        void* workspace, size_t workspace_bytes, int32_t* dev_err, cudaStream_t stream);
+int persona_sgmv_fused(const void* x, int64_t ldx, const void* a_pool, int64_t a_slot_stride,
+                       int64_t a_row_stride, const void* b_pool, int64_t b_slot_stride,
+                       const int32_t* seg_indptr, const int32_t* seg_slots, int64_t num_segments,
+                       void* y, int64_t ldy, int64_t T, int64_t K, int64_t N, int64_t R, int64_t S,
+                       int dtype, void* workspace, size_t workspace_bytes, int32_t* dev_err,
+                       cudaStream_t stream);
+
 /* ---- warm-up GEMV ---------------------------------------------------------
  * y[n] = W[n, :] @ x (fp16, fp32 accumulate).  Replaces
  * persona::gemv_fp16_cuda (csrc/gemv_fp16.cu:33-50), kept so that

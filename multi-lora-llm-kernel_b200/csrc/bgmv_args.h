@@ -36,6 +36,9 @@ cudaError_t launch_shrink_rowwise(int dtype, const void* x, int64_t ldx, const v
                                   int64_t a_slot_stride, int64_t a_row_stride,
                                   const int32_t* slots, float* v, int T, int K, int R, int S,
                                   int32_t* err, cudaStream_t st);
+cudaError_t launch_sgmv_plan(const int32_t* indptr, const int32_t* seg_slots, int nseg, int T, int S,
+                             int rows_per_item, int32_t* plan, int32_t* row_slots, int32_t* dev_err,
+                             cudaStream_t stream);
 int bgmv_stage_rows(int R);
 cudaError_t launch_gemv_fp16(const void* x, const void* W, void* y, int K, int N, cudaStream_t st);
 

@@ -165,3 +165,110 @@ cudaError_t launch_bgmv_plan(const int32_t* slots, int T, int S, int rows_per_it
 }
 
 }  // namespace persona
+
+namespace persona {
+
+// Plan of a segmented batch (rows grouped contiguously by adapter, as in a
+// prefill): segment i covers rows [indptr[i], indptr[i+1]) and uses slot
+// seg_slots[i].  No sort is needed: perm is the identity, items are the
+// segments cut into chunks of rows_per_item rows (full chunks first, then the
+// remainders, each in segment order), and row_slots[t] receives every row's
+// slot (-1 outside the segments) for the kernels that zero rows without an
+// adapter.  A decreasing or out-of-range indptr raises
+// PERSONA_DEV_ERR_SEGMENT (the offending segment is skipped); a slot outside
+// [-1, S) raises PERSONA_DEV_ERR_SLOT (its rows are skipped).
+template <int THREADS>
+__global__ void __launch_bounds__(THREADS)
+    sgmv_plan_kernel(const int32_t* __restrict__ indptr, const int32_t* __restrict__ seg_slots, int nseg,
+                     int T, int S, int rows_per_item, int32_t* __restrict__ plan, int32_t* __restrict__ row_slots,
+                     int32_t* dev_err) {
+  using ScanI = cub::BlockScan<int, THREADS>;
+  __shared__ typename ScanI::TempStorage scan;
+  __shared__ int s_base[2];  // running full / partial item counts
+  __shared__ int s_total_full;
+  __shared__ int s_err;
+  const int tid = threadIdx.x;
+  PlanView pv = plan_view(plan, T);
+  for (int t = tid; t < T; t += THREADS) {
+    row_slots[t] = -1;
+    pv.perm[t] = t;
+  }
+  if (tid == 0) {
+    s_base[0] = s_base[1] = 0;
+    s_total_full = 0;
+    s_err = 0;
+  }
+  __syncthreads();
+  // pass 0 counts the full items of all segments; pass 1 writes the items
+  for (int pass = 0; pass < 2; ++pass) {
+    for (int base = 0; base < nseg; base += THREADS) {
+      const int i = base + tid;
+      int lo = 0, hi = 0, slot = -1;
+      if (i < nseg) {
+        lo = indptr[i];
+        hi = indptr[i + 1];
+        slot = seg_slots[i];
+        if (lo < 0 || hi < lo || hi > T) {
+          if (pass == 0) atomicOr(&s_err, PERSONA_DEV_ERR_SEGMENT);
+          lo = hi = 0;
+        } else if (slot < -1 || slot >= S) {
+          if (pass == 0) atomicOr(&s_err, PERSONA_DEV_ERR_SLOT);
+          slot = -1;
+        }
+      }
+      const int len = slot >= 0 ? hi - lo : 0;
+      const int nfull = len / rows_per_item;
+      const int npart = (len % rows_per_item) ? 1 : 0;
+      int off_full, off_part, agg_full, agg_part;
+      ScanI(scan).ExclusiveSum(nfull, off_full, agg_full);
+      __syncthreads();
+      ScanI(scan).ExclusiveSum(npart, off_part, agg_part);
+      __syncthreads();
+      if (pass == 1) {
+        for (int f = 0; f < nfull; ++f)
+          pv.items[s_base[0] + off_full + f] = make_int4(slot, lo + f * rows_per_item, rows_per_item, 0);
+        if (npart)
+          pv.items[s_total_full + s_base[1] + off_part] =
+              make_int4(slot, lo + nfull * rows_per_item, len - nfull * rows_per_item, 0);
+      }
+      __syncthreads();
+      if (tid == 0) {
+        s_base[0] += agg_full;
+        s_base[1] += agg_part;
+      }
+      __syncthreads();
+    }
+    if (pass == 0 && tid == 0) {
+      s_total_full = s_base[0];
+      s_base[0] = s_base[1] = 0;
+    }
+    __syncthreads();
+  }
+  // row slots: segments fill their rows (valid ones only), one warp per segment
+  for (int i = tid >> 5; i < nseg; i += THREADS / 32) {
+    const int lo = indptr[i], hi = indptr[i + 1], slot = seg_slots[i];
+    if (lo < 0 || hi < lo || hi > T || slot < 0 || slot >= S) continue;
+    for (int t = lo + (tid & 31); t < hi; t += 32) row_slots[t] = slot;
+  }
+  if (tid == 0) {
+    pv.hdr[kHdrItems] = s_total_full + s_base[1];
+    pv.hdr[kHdrValid] = 0;
+    pv.hdr[kHdrNull] = 0;
+    pv.hdr[kHdrBad] = 0;
+    pv.hdr[kHdrT] = T;
+    pv.hdr[kHdrS] = S;
+    pv.hdr[kHdrRowsPerItem] = rows_per_item;
+    pv.hdr[kHdrMagic] = kPlanMagic;
+    if (s_err) raise_error(dev_err, s_err);
+  }
+}
+
+cudaError_t launch_sgmv_plan(const int32_t* indptr, const int32_t* seg_slots, int nseg, int T, int S,
+                             int rows_per_item, int32_t* plan, int32_t* row_slots, int32_t* dev_err,
+                             cudaStream_t stream) {
+  sgmv_plan_kernel<512><<<1, 512, 0, stream>>>(indptr, seg_slots, nseg, T, S, rows_per_item, plan, row_slots,
+                                               dev_err);
+  return cudaGetLastError();
+}
+
+}  // namespace persona

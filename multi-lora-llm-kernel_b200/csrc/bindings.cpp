@@ -312,6 +312,106 @@ void fused_with_plan(const at::Tensor& x, const at::Tensor& a_pool, const at::Te
 }
 }  // namespace
 
+namespace {
+void check_segments(const at::Tensor& indptr, const at::Tensor& seg_slots, const char* op) {
+  TORCH_CHECK(indptr.is_cuda() && seg_slots.is_cuda(), op, ": all tensors must be CUDA");
+  TORCH_CHECK(indptr.dim() == 1 && seg_slots.dim() == 1 && indptr.size(0) == seg_slots.size(0) + 1, op,
+              ": seg_indptr must have one more entry than seg_slots");
+  TORCH_CHECK(indptr.is_contiguous() && seg_slots.is_contiguous(), op, ": tensors must be contiguous");
+  TORCH_CHECK(indptr.scalar_type() == at::kInt && seg_slots.scalar_type() == at::kInt, op,
+              ": seg_indptr and seg_slots must be int32");
+}
+
+at::Tensor sgmv_workspace(int64_t T, const at::Tensor& like) {
+  return at::empty({static_cast<int64_t>(persona_sgmv_workspace_size(T))}, like.options().dtype(at::kByte));
+}
+
+void sgmv_shrink_op(const at::Tensor& x, const at::Tensor& a_pool, const at::Tensor& indptr,
+                    const at::Tensor& seg_slots, at::Tensor& v) {
+  const char* op = "sgmv_shrink";
+  check_segments(indptr, seg_slots, op);
+  TORCH_CHECK(x.is_cuda() && a_pool.is_cuda() && v.is_cuda(), "sgmv_shrink: all tensors must be CUDA");
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1 && v.is_contiguous(), "sgmv_shrink: tensors must be contiguous");
+  check_pool_a(a_pool, op);
+  TORCH_CHECK(v.scalar_type() == at::kFloat, "sgmv_shrink: v must be float32");
+  const int64_t T = x.size(0), K = x.size(1), S = a_pool.size(0), R = a_pool.size(1);
+  TORCH_CHECK(a_pool.size(2) == K, "sgmv_shrink: a_pool shape mismatch");
+  TORCH_CHECK(v.dim() == 2 && v.size(0) == T && v.size(1) == R, "sgmv_shrink: v shape mismatch");
+  const int dt = dtype_code(x, op);
+  TORCH_CHECK(a_pool.scalar_type() == x.scalar_type(), "sgmv_shrink: dtype mismatch");
+  const at::cuda::OptionalCUDAGuard guard(x.device());
+  const int dev = x.get_device();
+  raise_pending(dev, op);
+  if (T == 0) return;
+  at::Tensor ws = sgmv_workspace(T, x);
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  check_status(persona_sgmv_shrink(x.data_ptr(), row_stride(x), a_pool.data_ptr(), a_pool.stride(0),
+                                   a_pool.stride(1), indptr.data_ptr<int32_t>(), seg_slots.data_ptr<int32_t>(),
+                                   seg_slots.size(0), v.data_ptr<float>(), T, K, R, S, dt, ws.data_ptr(),
+                                   ws.numel(), error_word_device(dev), stream),
+               op);
+  after_launch(dev, op, stream);
+}
+
+void sgmv_expand_op(const at::Tensor& v, const at::Tensor& b_pool, const at::Tensor& indptr,
+                    const at::Tensor& seg_slots, at::Tensor& y) {
+  const char* op = "sgmv_expand";
+  check_segments(indptr, seg_slots, op);
+  TORCH_CHECK(v.is_cuda() && b_pool.is_cuda() && y.is_cuda(), "sgmv_expand: all tensors must be CUDA");
+  TORCH_CHECK(v.is_contiguous() && y.dim() == 2 && y.stride(1) == 1, "sgmv_expand: tensors must be contiguous");
+  check_pool_b(b_pool, op);
+  TORCH_CHECK(v.scalar_type() == at::kFloat, "sgmv_expand: v must be float32");
+  const int64_t T = v.size(0), R = v.size(1), S = b_pool.size(0), N = b_pool.size(1);
+  TORCH_CHECK(b_pool.size(2) == R, "sgmv_expand: b_pool rank dim mismatch");
+  TORCH_CHECK(y.size(0) == T && y.size(1) == N, "sgmv_expand: y shape mismatch");
+  const int dt = dtype_code(y, op);
+  TORCH_CHECK(b_pool.scalar_type() == y.scalar_type(), "sgmv_expand: dtype mismatch");
+  const at::cuda::OptionalCUDAGuard guard(v.device());
+  const int dev = v.get_device();
+  raise_pending(dev, op);
+  if (T == 0) return;
+  at::Tensor ws = sgmv_workspace(T, v);
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  check_status(persona_sgmv_expand(v.data_ptr<float>(), b_pool.data_ptr(), b_pool.stride(0),
+                                   indptr.data_ptr<int32_t>(), seg_slots.data_ptr<int32_t>(), seg_slots.size(0),
+                                   y.data_ptr(), row_stride(y), T, N, R, S, dt, ws.data_ptr(), ws.numel(),
+                                   error_word_device(dev), stream),
+               op);
+  after_launch(dev, op, stream);
+}
+
+void sgmv_fused_op(const at::Tensor& x, const at::Tensor& a_pool, const at::Tensor& b_pool,
+                   const at::Tensor& indptr, const at::Tensor& seg_slots, at::Tensor& y) {
+  const char* op = "sgmv_fused";
+  check_segments(indptr, seg_slots, op);
+  TORCH_CHECK(x.is_cuda() && a_pool.is_cuda() && b_pool.is_cuda() && y.is_cuda(),
+              "sgmv_fused: all tensors must be CUDA");
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1 && y.dim() == 2 && y.stride(1) == 1,
+              "sgmv_fused: tensors must be contiguous");
+  check_pool_a(a_pool, op);
+  check_pool_b(b_pool, op);
+  const int64_t T = x.size(0), K = x.size(1), S = a_pool.size(0), R = a_pool.size(1), N = b_pool.size(1);
+  TORCH_CHECK(a_pool.size(2) == K && b_pool.size(0) == S && b_pool.size(2) == R, "sgmv_fused: pool shape mismatch");
+  TORCH_CHECK(y.size(0) == T && y.size(1) == N, "sgmv_fused: y shape mismatch");
+  const int dt = dtype_code(x, op);
+  TORCH_CHECK(a_pool.scalar_type() == x.scalar_type() && b_pool.scalar_type() == x.scalar_type() &&
+                  y.scalar_type() == x.scalar_type(),
+              "sgmv_fused: dtype mismatch");
+  const at::cuda::OptionalCUDAGuard guard(x.device());
+  const int dev = x.get_device();
+  raise_pending(dev, op);
+  if (T == 0) return;
+  at::Tensor ws = sgmv_workspace(T, x);
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  check_status(persona_sgmv_fused(x.data_ptr(), row_stride(x), a_pool.data_ptr(), a_pool.stride(0),
+                                  a_pool.stride(1), b_pool.data_ptr(), b_pool.stride(0), indptr.data_ptr<int32_t>(),
+                                  seg_slots.data_ptr<int32_t>(), seg_slots.size(0), y.data_ptr(), row_stride(y), T,
+                                  K, N, R, S, dt, ws.data_ptr(), ws.numel(), error_word_device(dev), stream),
+               op);
+  after_launch(dev, op, stream);
+}
+}  // namespace
+
 TORCH_LIBRARY(persona, m) {
   // Reference schemas, unchanged (csrc/bindings.cpp:19-23).
   m.def("bgmv_shrink(Tensor x, Tensor a_pool, Tensor slots, Tensor(a!) v) -> ()");
@@ -324,6 +424,10 @@ TORCH_LIBRARY(persona, m) {
   m.def("bgmv_fused(Tensor x, Tensor a_pool, Tensor b_pool, Tensor slots, Tensor(a!) y) -> ()");
   m.def("bgmv_fused_with_plan(Tensor x, Tensor a_pool, Tensor b_pool, Tensor slots, Tensor plan, "
         "Tensor(a!) y) -> ()");
+  m.def("sgmv_shrink(Tensor x, Tensor a_pool, Tensor seg_indptr, Tensor seg_slots, Tensor(a!) v) -> ()");
+  m.def("sgmv_expand(Tensor v, Tensor b_pool, Tensor seg_indptr, Tensor seg_slots, Tensor(a!) y) -> ()");
+  m.def("sgmv_fused(Tensor x, Tensor a_pool, Tensor b_pool, Tensor seg_indptr, Tensor seg_slots, "
+        "Tensor(a!) y) -> ()");
 }
 
 TORCH_LIBRARY_IMPL(persona, CUDA, m) {
@@ -335,6 +439,9 @@ TORCH_LIBRARY_IMPL(persona, CUDA, m) {
   m.impl("bgmv_expand_with_plan", &expand_with_plan);
   m.impl("bgmv_fused", &fused_noplan);
   m.impl("bgmv_fused_with_plan", &fused_with_plan);
+  m.impl("sgmv_shrink", &sgmv_shrink_op);
+  m.impl("sgmv_expand", &sgmv_expand_op);
+  m.impl("sgmv_fused", &sgmv_fused_op);
 }
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {

@@ -301,3 +301,73 @@ int persona_gemv_fp16(const void* x, const void* W, void* y, int64_t K, int64_t 
 }
 
 }  // extern "C"
+
+// ----------------------------------------------------------------- SGMV ---
+namespace {
+size_t sgmv_ws_bytes(int64_t T) { return persona::plan_bytes(T) + 4 * static_cast<size_t>(persona::plan_tpad(T)); }
+
+int sgmv_prepare(const int32_t* seg_indptr, const int32_t* seg_slots, int64_t nseg, int64_t T, int64_t S,
+                 void* workspace, size_t workspace_bytes, int32_t* dev_err, cudaStream_t stream,
+                 int32_t** row_slots) {
+  if (T < 0 || S <= 0 || nseg < 0 || T > (int64_t{1} << 30) || nseg > (int64_t{1} << 30)) return PERSONA_ERR_SHAPE;
+  if (T == 0) return PERSONA_OK;
+  if (seg_indptr == nullptr || (nseg > 0 && seg_slots == nullptr)) return PERSONA_ERR_INVALID_ARG;
+  if (workspace == nullptr || workspace_bytes < sgmv_ws_bytes(T)) return PERSONA_ERR_WORKSPACE;
+  if ((reinterpret_cast<uintptr_t>(workspace) & 15) != 0) return PERSONA_ERR_ALIGNMENT;
+  *row_slots = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(workspace) + persona::plan_bytes(T));
+  return persona::launch_sgmv_plan(seg_indptr, seg_slots, static_cast<int>(nseg), static_cast<int>(T),
+                                   static_cast<int>(S), persona::kRowsPerItem, static_cast<int32_t*>(workspace),
+                                   *row_slots, dev_err, stream) == cudaSuccess
+             ? PERSONA_OK
+             : PERSONA_ERR_CUDA;
+}
+}  // namespace
+
+extern "C" {
+
+size_t persona_sgmv_workspace_size(int64_t T) { return T < 0 ? 0 : sgmv_ws_bytes(T); }
+
+int persona_sgmv_shrink(const void* x, int64_t ldx, const void* a_pool, int64_t a_slot_stride, int64_t a_row_stride,
+                        const int32_t* seg_indptr, const int32_t* seg_slots, int64_t num_segments, float* v,
+                        int64_t T, int64_t K, int64_t R, int64_t S, int dtype, void* workspace,
+                        size_t workspace_bytes, int32_t* dev_err, cudaStream_t stream) {
+  if (dtype != PERSONA_DTYPE_F16 && dtype != PERSONA_DTYPE_BF16) return PERSONA_ERR_DTYPE;
+  int32_t* row_slots = nullptr;
+  int st = sgmv_prepare(seg_indptr, seg_slots, num_segments, T, S, workspace, workspace_bytes, dev_err, stream,
+                        &row_slots);
+  if (st != PERSONA_OK || T == 0) return st;
+  return persona_bgmv_shrink(x, ldx, a_pool, a_slot_stride, a_row_stride, row_slots, v, T, K, R, S, dtype,
+                             workspace, persona::plan_bytes(T), PERSONA_REUSE_PLAN, dev_err, stream);
+}
+
+int persona_sgmv_expand(const float* v, const void* b_pool, int64_t b_slot_stride, const int32_t* seg_indptr,
+                        const int32_t* seg_slots, int64_t num_segments, void* y, int64_t ldy, int64_t T, int64_t N,
+                        int64_t R, int64_t S, int dtype, void* workspace, size_t workspace_bytes,
+                        int32_t* dev_err, cudaStream_t stream) {
+  if (dtype != PERSONA_DTYPE_F16 && dtype != PERSONA_DTYPE_BF16) return PERSONA_ERR_DTYPE;
+  if (!rank_supported(R)) return PERSONA_ERR_RANK;
+  int32_t* row_slots = nullptr;
+  int st = sgmv_prepare(seg_indptr, seg_slots, num_segments, T, S, workspace, workspace_bytes, dev_err, stream,
+                        &row_slots);
+  if (st != PERSONA_OK || T == 0) return st;
+  return persona_bgmv_expand(v, b_pool, b_slot_stride, row_slots, y, ldy, T, N, R, S, dtype, workspace,
+                             persona::plan_bytes(T), PERSONA_REUSE_PLAN, dev_err, stream);
+}
+
+int persona_sgmv_fused(const void* x, int64_t ldx, const void* a_pool, int64_t a_slot_stride, int64_t a_row_stride,
+                       const void* b_pool, int64_t b_slot_stride, const int32_t* seg_indptr,
+                       const int32_t* seg_slots, int64_t num_segments, void* y, int64_t ldy, int64_t T, int64_t K,
+                       int64_t N, int64_t R, int64_t S, int dtype, void* workspace, size_t workspace_bytes,
+                       int32_t* dev_err, cudaStream_t stream) {
+  if (dtype != PERSONA_DTYPE_F16 && dtype != PERSONA_DTYPE_BF16) return PERSONA_ERR_DTYPE;
+  if (!rank_supported(R)) return PERSONA_ERR_RANK;
+  int32_t* row_slots = nullptr;
+  int st = sgmv_prepare(seg_indptr, seg_slots, num_segments, T, S, workspace, workspace_bytes, dev_err, stream,
+                        &row_slots);
+  if (st != PERSONA_OK || T == 0) return st;
+  return persona_bgmv_fused(x, ldx, a_pool, a_slot_stride, a_row_stride, b_pool, b_slot_stride, row_slots, y, ldy,
+                            T, K, N, R, S, dtype, workspace, persona::plan_bytes(T), PERSONA_REUSE_PLAN, dev_err,
+                            stream);
+}
+
+}  // extern "C"

@@ -107,6 +107,33 @@ def bgmv_fused(x: torch.Tensor, a_pool: torch.Tensor, b_pool: torch.Tensor, slot
     return y
 
 
+def sgmv_shrink(x: torch.Tensor, a_pool: torch.Tensor, seg_indptr: torch.Tensor,
+                seg_slots: torch.Tensor) -> torch.Tensor:
+    """Segmented shrink: rows ``[seg_indptr[i], seg_indptr[i+1])`` use slot
+    ``seg_slots[i]``; rows outside every segment get zeros.  Equals
+    ``bgmv_shrink`` on the per-row slots the segments imply."""
+    _require_cuda("sgmv_shrink", x, a_pool, seg_indptr, seg_slots)
+    v = torch.empty((x.shape[0], a_pool.shape[1]), dtype=torch.float32, device=x.device)
+    torch.ops.persona.sgmv_shrink(x.contiguous(), a_pool, seg_indptr, seg_slots, v)
+    return v
+
+
+def sgmv_expand(v: torch.Tensor, b_pool: torch.Tensor, seg_indptr: torch.Tensor,
+                seg_slots: torch.Tensor, y: torch.Tensor) -> torch.Tensor:
+    """Segmented expand, in place on ``y``; rows outside the segments untouched."""
+    _require_cuda("sgmv_expand", v, b_pool, seg_indptr, seg_slots, y)
+    torch.ops.persona.sgmv_expand(v, b_pool, seg_indptr, seg_slots, y)
+    return y
+
+
+def sgmv_fused(x: torch.Tensor, a_pool: torch.Tensor, b_pool: torch.Tensor, seg_indptr: torch.Tensor,
+               seg_slots: torch.Tensor, y: torch.Tensor) -> torch.Tensor:
+    """Segmented shrink->expand in place on ``y``."""
+    _require_cuda("sgmv_fused", x, a_pool, b_pool, seg_indptr, seg_slots, y)
+    torch.ops.persona.sgmv_fused(x, a_pool, b_pool, seg_indptr, seg_slots, y)
+    return y
+
+
 def gemv_fp16(x: torch.Tensor, W: torch.Tensor, y: torch.Tensor) -> torch.Tensor:
     """Warm-up GEMV kept from the reference (``csrc/gemv_fp16.cu``)."""
     _require_cuda("gemv_fp16", x, W, y)

@@ -402,3 +402,65 @@ def test_gemv_fp16():
     ops.gemv_fp16(t16(x, "f16"), t16(W, "f16"), y)
     want = W.astype(np.float32) @ x.astype(np.float32)
     np.testing.assert_allclose(y.float().cpu().numpy(), want, rtol=1e-2, atol=5e-2)
+
+
+# ------------------------------------------------------------------- SGMV --
+
+def _sgmv_case(requests, rows, names, dtype="bf16", seed=3, holes=False):
+    wl = workloads.segmented_prefill(seed=seed, requests=requests, rows_per_request=rows, names=names, dtype=dtype)
+    indptr, seg = wl.indptr.copy(), wl.seg_slots.copy()
+    if holes:  # drop a segment (rows without adapter) and mark one as -1
+        seg[1] = -1
+    return wl, indptr, seg
+
+
+@pytest.mark.parametrize("holes", [False, True])
+def test_sgmv_matches_oracle_small(holes):
+    wl, indptr, seg = _sgmv_case(6, 37, ["gate_proj"], holes=holes)
+    p = wl.projections[0]
+    x, a, b = t16(p.x, "bf16"), t16(p.a_pool, "bf16"), t16(p.b_pool, "bf16")
+    ip, ss = ti(indptr), ti(seg)
+    slots = O.sgmv_slots(indptr, seg, wl.T)
+    v_ref = O.bgmv_shrink_ref(p.x, p.a_pool, slots, "bf16")
+    v = ops.sgmv_shrink(x, a, ip, ss)
+    np.testing.assert_allclose(v.cpu().numpy(), v_ref, **TOL)
+    y_ref = p.y.copy()
+    O.bgmv_expand_ref(v_ref, p.b_pool, slots, y_ref, "bf16")
+    y = t16(p.y, "bf16")
+    ops.sgmv_expand(v, b, ip, ss, y)
+    np.testing.assert_allclose(f32(n16(y, "bf16"), "bf16"), f32(y_ref, "bf16"), **TOL)
+    y2 = t16(p.y, "bf16")
+    ops.sgmv_fused(x, a, b, ip, ss, y2)
+    got = n16(y2, "bf16")
+    np.testing.assert_allclose(f32(got, "bf16"), f32(y_ref, "bf16"), **TOL)
+    assert np.array_equal(got[slots < 0], p.y[slots < 0])
+    no_device_error()
+
+
+def test_sgmv_bad_segment_table_is_reported():
+    wl, indptr, seg = _sgmv_case(4, 16, ["down_proj"])
+    p = wl.projections[0]
+    bad = indptr.copy()
+    bad[2] = bad[1] - 3  # decreasing
+    y = t16(p.y, "bf16")
+    ops.sgmv_fused(t16(p.x, "bf16"), t16(p.a_pool, "bf16"), t16(p.b_pool, "bf16"), ti(bad), ti(seg), y)
+    with pytest.raises(RuntimeError, match="invalid segment table"):
+        ops.check_errors(dev())
+
+
+def test_sgmv_prefill_full_size_down_proj_sampled():
+    """32 requests x 512 rows, rank 16, bf16, 14336 -> 4096: full-size run,
+    oracle on a sample of rows (every 97th row) to bound CPU time."""
+    wl = workloads.segmented_prefill(names=["down_proj"])
+    p = wl.projections[0]
+    x, a, b = t16(p.x, "bf16"), t16(p.a_pool, "bf16"), t16(p.b_pool, "bf16")
+    ip, ss = ti(wl.indptr), ti(wl.seg_slots)
+    y = t16(p.y, "bf16")
+    ops.sgmv_fused(x, a, b, ip, ss, y)
+    got = n16(y, "bf16")
+    rows = np.arange(0, wl.T, 97)
+    sl = wl.slots[rows]
+    y_ref = p.y[rows].copy()
+    O.bgmv_forward_ref(p.x[rows], p.a_pool, p.b_pool, sl, "bf16", y=y_ref)
+    np.testing.assert_allclose(f32(got[rows], "bf16"), f32(y_ref, "bf16"), **TOL)
+    no_device_error()
