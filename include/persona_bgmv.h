@@ -113,8 +113,13 @@ int persona_bgmv_fused(const void* x, int64_t ldx, const void* a_pool, int64_t a
  * is how the reference's callers express a prefill (LoRAContext.set_batch_slots,
  * persona/lora_layer.py:21-28); the reference itself has no segmented op.
  * seg_indptr [num_segments + 1] and seg_slots [num_segments] are int32 device
- * arrays; a decreasing or out-of-range seg_indptr sets PERSONA_DEV_ERR_SEGMENT
- * and the offending segment is skipped.  Workspace: persona_sgmv_workspace_size(T). */
+ * arrays.  A segment is used only if 0 <= lo <= hi <= T and no earlier
+ * seg_indptr entry exceeds lo (used segments never overlap); any other
+ * segment sets PERSONA_DEV_ERR_SEGMENT and is skipped.
+ * Ranks 16 and 32 with K % 64 == 0 (shrink) and N % 128 == 0 (expand) run on
+ * the tensor cores (tcgen05, accumulators in TMEM, 128-row tiles); other
+ * shapes run the clustered BGMV kernels over the segments' rows.
+ * Workspace: persona_sgmv_workspace_size(T). */
 size_t persona_sgmv_workspace_size(int64_t T);
 int persona_sgmv_shrink(const void* x, int64_t ldx, const void* a_pool, int64_t a_slot_stride,
                         int64_t a_row_stride, const int32_t* seg_indptr, const int32_t* seg_slots,

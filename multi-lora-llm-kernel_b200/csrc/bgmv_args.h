@@ -40,6 +40,20 @@ cudaError_t launch_sgmv_plan(const int32_t* indptr, const int32_t* seg_slots, in
                              int rows_per_item, int32_t* plan, int32_t* row_slots, int32_t* dev_err,
                              cudaStream_t stream);
 int bgmv_stage_rows(int R);
+
+// Segmented tensor-core kernels (sgmv_tcgen05.cu).
+struct SgmvTcArgs {
+  const int32_t* plan;  // segment plan, 128-row items, identity perm
+  const float* v_in;    // expand only: [T, R]
+  float* v_out;         // shrink only: [T, R]
+  uint16_t* y;          // [T, N] row stride ldy (plain stores of short items)
+  int64_t ldy;
+  int32_t* err;
+  int T, K, N;
+};
+cudaError_t launch_sgmv_tc(int mode, int dtype, int R, const CUtensorMap& tx, const CUtensorMap& ta,
+                           const CUtensorMap& tb, const CUtensorMap& ty, const SgmvTcArgs& a, int max_items,
+                           cudaStream_t st);
 cudaError_t launch_gemv_fp16(const void* x, const void* W, void* y, int K, int N, cudaStream_t st);
 
 }  // namespace persona

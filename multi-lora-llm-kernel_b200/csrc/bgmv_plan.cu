@@ -16,6 +16,8 @@
 //           then the partial ones in slot order
 // Items never straddle a chunk; for T <= kChunk there is one chunk and the
 // layout is exactly the oracle's `plan_ref`.
+#include <climits>
+
 #include <cub/block/block_radix_sort.cuh>
 #include <cub/block/block_scan.cuh>
 
@@ -174,9 +176,11 @@ namespace persona {
 // segments cut into chunks of rows_per_item rows (full chunks first, then the
 // remainders, each in segment order), and row_slots[t] receives every row's
 // slot (-1 outside the segments) for the kernels that zero rows without an
-// adapter.  A decreasing or out-of-range indptr raises
-// PERSONA_DEV_ERR_SEGMENT (the offending segment is skipped); a slot outside
-// [-1, S) raises PERSONA_DEV_ERR_SLOT (its rows are skipped).
+// adapter.  A segment is used only if 0 <= lo <= hi <= T and no earlier
+// indptr entry exceeds lo, so the used segments never overlap and the items
+// never outnumber the rows; any other segment raises PERSONA_DEV_ERR_SEGMENT
+// and is skipped.  A slot outside [-1, S) raises PERSONA_DEV_ERR_SLOT (its
+// rows are skipped).
 template <int THREADS>
 __global__ void __launch_bounds__(THREADS)
     sgmv_plan_kernel(const int32_t* __restrict__ indptr, const int32_t* __restrict__ seg_slots, int nseg,
@@ -187,6 +191,8 @@ __global__ void __launch_bounds__(THREADS)
   __shared__ int s_base[2];  // running full / partial item counts
   __shared__ int s_total_full;
   __shared__ int s_err;
+  __shared__ int s_carry;    // max indptr entry of the previous chunks
+  __shared__ int s_lo[THREADS], s_hi[THREADS], s_slot[THREADS];
   const int tid = threadIdx.x;
   PlanView pv = plan_view(plan, T);
   for (int t = tid; t < T; t += THREADS) {
@@ -200,7 +206,10 @@ __global__ void __launch_bounds__(THREADS)
   }
   __syncthreads();
   // pass 0 counts the full items of all segments; pass 1 writes the items
+  // and the row slots
   for (int pass = 0; pass < 2; ++pass) {
+    if (tid == 0) s_carry = 0;
+    __syncthreads();
     for (int base = 0; base < nseg; base += THREADS) {
       const int i = base + tid;
       int lo = 0, hi = 0, slot = -1;
@@ -208,9 +217,16 @@ __global__ void __launch_bounds__(THREADS)
         lo = indptr[i];
         hi = indptr[i + 1];
         slot = seg_slots[i];
-        if (lo < 0 || hi < lo || hi > T) {
+      }
+      int run_max;
+      ScanI(scan).InclusiveScan(i < nseg ? lo : INT_MIN, run_max, cub::Max());
+      __syncthreads();
+      run_max = max(run_max, s_carry);
+      if (i < nseg) {
+        if (lo < 0 || hi < lo || hi > T || run_max > lo) {
           if (pass == 0) atomicOr(&s_err, PERSONA_DEV_ERR_SEGMENT);
           lo = hi = 0;
+          slot = -1;
         } else if (slot < -1 || slot >= S) {
           if (pass == 0) atomicOr(&s_err, PERSONA_DEV_ERR_SLOT);
           slot = -1;
@@ -230,8 +246,17 @@ __global__ void __launch_bounds__(THREADS)
         if (npart)
           pv.items[s_total_full + s_base[1] + off_part] =
               make_int4(slot, lo + nfull * rows_per_item, len - nfull * rows_per_item, 0);
+        s_lo[tid] = lo;
+        s_hi[tid] = slot >= 0 ? hi : lo;
+        s_slot[tid] = slot;
       }
       __syncthreads();
+      if (pass == 1) {  // row slots of this chunk's segments, one warp per segment
+        const int n = min(THREADS, nseg - base);
+        for (int q = tid >> 5; q < n; q += THREADS / 32)
+          for (int t = s_lo[q] + (tid & 31); t < s_hi[q]; t += 32) row_slots[t] = s_slot[q];
+      }
+      if (tid == THREADS - 1) s_carry = run_max;  // inclusive max up to the chunk's last entry
       if (tid == 0) {
         s_base[0] += agg_full;
         s_base[1] += agg_part;
@@ -243,12 +268,6 @@ __global__ void __launch_bounds__(THREADS)
       s_base[0] = s_base[1] = 0;
     }
     __syncthreads();
-  }
-  // row slots: segments fill their rows (valid ones only), one warp per segment
-  for (int i = tid >> 5; i < nseg; i += THREADS / 32) {
-    const int lo = indptr[i], hi = indptr[i + 1], slot = seg_slots[i];
-    if (lo < 0 || hi < lo || hi > T || slot < 0 || slot >= S) continue;
-    for (int t = lo + (tid & 31); t < hi; t += 32) row_slots[t] = slot;
   }
   if (tid == 0) {
     pv.hdr[kHdrItems] = s_total_full + s_base[1];

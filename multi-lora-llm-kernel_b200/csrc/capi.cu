@@ -90,6 +90,23 @@ int encode_b_map(CUtensorMap* m, const void* b_pool, int dtype, int64_t N, int64
   return r == CUDA_SUCCESS ? PERSONA_OK : PERSONA_ERR_CUDA;
 }
 
+// Row-major [rows, cols] 16-bit matrix as a 2-D tensor {cols, rows}; box
+// {box_cols, box_rows}, 128-byte swizzle (box_cols * 2 == 128).
+int encode_2d_map(CUtensorMap* m, const void* base, int dtype, int64_t cols, int64_t rows, int64_t row_stride,
+                  int box_cols, int box_rows) {
+  auto enc = tensor_map_encoder();
+  if (!enc) return PERSONA_ERR_CUDA;
+  const CUtensorMapDataType dt =
+      dtype == PERSONA_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_stride * 2)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1u, 1u};
+  CUresult r = enc(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? PERSONA_OK : PERSONA_ERR_CUDA;
+}
+
 void split_k(int64_t K, int cs, int* k_per_cta) {
   const int64_t per = (K + cs - 1) / cs;
   *k_per_cta = static_cast<int>((per + 63) / 64 * 64);
@@ -323,6 +340,76 @@ int sgmv_prepare(const int32_t* seg_indptr, const int32_t* seg_slots, int64_t ns
 }
 }  // namespace
 
+namespace {
+// Tensor-core path: ranks 16 / 32, K a multiple of 64, N a multiple of 128.
+// PERSONA_SGMV_TENSOR_CORES=0 selects the clustered path instead.
+bool sgmv_tc_eligible(int64_t R, int64_t K, int64_t N, bool need_k, bool need_n) {
+  static const bool enabled = [] {
+    const char* e = std::getenv("PERSONA_SGMV_TENSOR_CORES");
+    return !(e != nullptr && e[0] == '0');
+  }();
+  if (!enabled || !(R == 16 || R == 32)) return false;
+  if (need_k && (K % 64 != 0 || K <= 0)) return false;
+  if (need_n && (N % 128 != 0 || N <= 0)) return false;
+  return true;
+}
+
+int sgmv_tc_run(int mode, const void* x, int64_t ldx, const void* a_pool, int64_t a_slot_stride,
+                int64_t a_row_stride, const void* b_pool, int64_t b_slot_stride, const int32_t* seg_indptr,
+                const int32_t* seg_slots, int64_t nseg, const float* v_in, float* v_out, void* y, int64_t ldy,
+                int64_t T, int64_t K, int64_t N, int64_t R, int64_t S, int dtype, void* workspace,
+                size_t workspace_bytes, int32_t* dev_err, cudaStream_t stream) {
+  using namespace persona;
+  if (T < 0 || S <= 0 || nseg < 0 || T > (int64_t{1} << 30)) return PERSONA_ERR_SHAPE;
+  if (T == 0) return PERSONA_OK;
+  if (seg_indptr == nullptr || (nseg > 0 && seg_slots == nullptr)) return PERSONA_ERR_INVALID_ARG;
+  if (workspace == nullptr || workspace_bytes < sgmv_ws_bytes(T)) return PERSONA_ERR_WORKSPACE;
+  if (!aligned16(workspace)) return PERSONA_ERR_ALIGNMENT;
+  int st;
+  CUtensorMap tx, ta, tb, ty;
+  std::memset(&tx, 0, sizeof(tx));
+  std::memset(&ta, 0, sizeof(ta));
+  std::memset(&tb, 0, sizeof(tb));
+  std::memset(&ty, 0, sizeof(ty));
+  if (mode & kModeShrink) {
+    if ((st = check_a(x, ldx, a_pool, a_slot_stride, a_row_stride, K, R, S)) != PERSONA_OK) return st;
+    if ((st = encode_2d_map(&tx, x, dtype, K, T, ldx, 64, 128)) != PERSONA_OK) return st;
+    if ((st = encode_a_map(&ta, a_pool, dtype, K, R, S, a_row_stride, a_slot_stride)) != PERSONA_OK) return st;
+  }
+  if (mode & kModeExpand) {
+    if ((st = check_b(b_pool, b_slot_stride, y, ldy, N, R)) != PERSONA_OK) return st;
+    if ((st = encode_2d_map(&ty, y, dtype, N, T, ldy, 64, 128)) != PERSONA_OK) return st;
+    if ((st = encode_b_map(&tb, b_pool, dtype, N, R, S, b_slot_stride, 128)) != PERSONA_OK) return st;
+  }
+  if (mode == kModeShrink && (v_out == nullptr || !aligned16(v_out))) return PERSONA_ERR_ALIGNMENT;
+  if (mode == kModeExpand && (v_in == nullptr || !aligned16(v_in))) return PERSONA_ERR_ALIGNMENT;
+  int32_t* row_slots = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(workspace) + plan_bytes(T));
+  if (launch_sgmv_plan(seg_indptr, seg_slots, static_cast<int>(nseg), static_cast<int>(T), static_cast<int>(S),
+                       128, static_cast<int32_t*>(workspace), row_slots, dev_err, stream) != cudaSuccess)
+    return PERSONA_ERR_CUDA;
+  if (mode == kModeShrink) {
+    // rows outside every segment (or with slot -1) get v = 0 first
+    if (cudaMemsetAsync(v_out, 0, static_cast<size_t>(T * R) * sizeof(float), stream) != cudaSuccess)
+      return PERSONA_ERR_CUDA;
+  }
+  SgmvTcArgs a = {};
+  a.plan = static_cast<const int32_t*>(workspace);
+  a.v_in = v_in;
+  a.v_out = v_out;
+  a.y = static_cast<uint16_t*>(y);
+  a.ldy = ldy;
+  a.err = dev_err;
+  a.T = static_cast<int>(T);
+  a.K = static_cast<int>(K);
+  a.N = static_cast<int>(N);
+  const int64_t max_items = (T + 127) / 128 + nseg;
+  return launch_sgmv_tc(mode, dtype, static_cast<int>(R), tx, ta, tb, ty, a,
+                        static_cast<int>(max_items < (1 << 30) ? max_items : (1 << 30)), stream) == cudaSuccess
+             ? PERSONA_OK
+             : PERSONA_ERR_CUDA;
+}
+}  // namespace
+
 extern "C" {
 
 size_t persona_sgmv_workspace_size(int64_t T) { return T < 0 ? 0 : sgmv_ws_bytes(T); }
@@ -332,6 +419,10 @@ int persona_sgmv_shrink(const void* x, int64_t ldx, const void* a_pool, int64_t 
                         int64_t T, int64_t K, int64_t R, int64_t S, int dtype, void* workspace,
                         size_t workspace_bytes, int32_t* dev_err, cudaStream_t stream) {
   if (dtype != PERSONA_DTYPE_F16 && dtype != PERSONA_DTYPE_BF16) return PERSONA_ERR_DTYPE;
+  if (sgmv_tc_eligible(R, K, 0, true, false))
+    return sgmv_tc_run(persona::kModeShrink, x, ldx, a_pool, a_slot_stride, a_row_stride, nullptr, 0, seg_indptr,
+                       seg_slots, num_segments, nullptr, v, nullptr, 0, T, K, 0, R, S, dtype, workspace,
+                       workspace_bytes, dev_err, stream);
   int32_t* row_slots = nullptr;
   int st = sgmv_prepare(seg_indptr, seg_slots, num_segments, T, S, workspace, workspace_bytes, dev_err, stream,
                         &row_slots);
@@ -346,6 +437,10 @@ int persona_sgmv_expand(const float* v, const void* b_pool, int64_t b_slot_strid
                         int32_t* dev_err, cudaStream_t stream) {
   if (dtype != PERSONA_DTYPE_F16 && dtype != PERSONA_DTYPE_BF16) return PERSONA_ERR_DTYPE;
   if (!rank_supported(R)) return PERSONA_ERR_RANK;
+  if (sgmv_tc_eligible(R, 0, N, false, true))
+    return sgmv_tc_run(persona::kModeExpand, nullptr, 0, nullptr, 0, 0, b_pool, b_slot_stride, seg_indptr,
+                       seg_slots, num_segments, v, nullptr, y, ldy, T, 0, N, R, S, dtype, workspace,
+                       workspace_bytes, dev_err, stream);
   int32_t* row_slots = nullptr;
   int st = sgmv_prepare(seg_indptr, seg_slots, num_segments, T, S, workspace, workspace_bytes, dev_err, stream,
                         &row_slots);
@@ -361,6 +456,10 @@ int persona_sgmv_fused(const void* x, int64_t ldx, const void* a_pool, int64_t a
                        int32_t* dev_err, cudaStream_t stream) {
   if (dtype != PERSONA_DTYPE_F16 && dtype != PERSONA_DTYPE_BF16) return PERSONA_ERR_DTYPE;
   if (!rank_supported(R)) return PERSONA_ERR_RANK;
+  if (sgmv_tc_eligible(R, K, N, true, true))
+    return sgmv_tc_run(persona::kModeFused, x, ldx, a_pool, a_slot_stride, a_row_stride, b_pool, b_slot_stride,
+                       seg_indptr, seg_slots, num_segments, nullptr, nullptr, y, ldy, T, K, N, R, S, dtype,
+                       workspace, workspace_bytes, dev_err, stream);
   int32_t* row_slots = nullptr;
   int st = sgmv_prepare(seg_indptr, seg_slots, num_segments, T, S, workspace, workspace_bytes, dev_err, stream,
                         &row_slots);

@@ -145,11 +145,19 @@ def sgmv_slots(indptr: np.ndarray, seg_slots: np.ndarray, T: int) -> np.ndarray:
     contiguous same-adapter rows as per-token slots
     (``LoRAContext.set_batch_slots``, ``persona/lora_layer.py:21-28``).  SGMV
     is therefore checked against BGMV on the expanded slots.  Rows outside
-    every segment carry slot -1.
+    every segment carry slot -1.  A segment is used only if
+    ``0 <= lo <= hi <= T`` and no earlier ``indptr`` entry exceeds ``lo`` (so
+    used segments never overlap); other segments, and slots outside
+    ``[-1, S)``, leave their rows at -1 (the device reports them).
     """
     slots = np.full((T,), -1, dtype=np.int32)
+    run_max = None
     for i in range(len(seg_slots)):
-        slots[int(indptr[i]):int(indptr[i + 1])] = int(seg_slots[i])
+        lo, hi = int(indptr[i]), int(indptr[i + 1])
+        run_max = lo if run_max is None else max(run_max, lo)
+        if lo < 0 or hi < lo or hi > T or run_max > lo:
+            continue
+        slots[lo:hi] = int(seg_slots[i])
     return slots
 
 

@@ -114,3 +114,15 @@ def test_plan_ref_contract():
         seen_partial |= c < 5
         assert c < 5 or not seen_partial, "full items come first"
     assert covered.sum() == nv and covered[:nv].all()
+
+
+def test_sgmv_slots_expand_segments_and_skip_bad_ones():
+    indptr = np.array([0, 3, 3, 7, 9], dtype=np.int32)
+    seg = np.array([2, 5, -1, 1], dtype=np.int32)
+    assert O.sgmv_slots(indptr, seg, 10).tolist() == [2, 2, 2, -1, -1, -1, -1, 1, 1, -1]
+    # a step back: segment 1 is decreasing, segment 2 overlaps segment 0 -> both skipped
+    bad = np.array([0, 5, 2, 8, 9], dtype=np.int32)
+    assert O.sgmv_slots(bad, seg, 10).tolist() == [2] * 5 + [-1] * 3 + [1, -1]
+    # past the end
+    assert O.sgmv_slots(np.array([0, 4, 12], np.int32), np.array([0, 1], np.int32), 10).tolist() == \
+        [0] * 4 + [-1] * 6
