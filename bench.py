@@ -50,8 +50,8 @@ SEED = 2
 def parse_args():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=400)
-    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=3000)
+    ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
@@ -112,9 +112,11 @@ class ClockSampler:
 
     def _read(self):
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            self.lines.append((time.monotonic(), line.strip()))
 
-    def stop(self):
+    def stop(self, window=None):
+        """Summarise the samples that arrived inside ``window`` (host
+        monotonic seconds bracketing the timed region)."""
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         self.proc.terminate()
@@ -123,26 +125,25 @@ class ClockSampler:
         except subprocess.TimeoutExpired:
             self.proc.kill()
         self.thread.join(timeout=2)
-        sm, busy, mx, reasons = [], [], None, set()
+        sm, inside, mx, reasons = [], [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        for t, ln in self.lines:
             f = [c.strip() for c in ln.split(",")]
             if len(f) < 10:
                 continue
             try:
-                mhz, mxv, util = float(f[1]), float(f[2]), float(f[3])
+                mhz, mxv = float(f[1]), float(f[2])
             except ValueError:
                 continue
             mx = mxv
             sm.append(mhz)
-            if util >= 50:
-                busy.append(mhz)
+            if window is None or window[0] <= t <= window[1]:
+                inside.append(mhz)
                 for nm, val in zip(names, f[6:10]):
                     if val.lower() == "active":
                         reasons.add(nm)
-        pick = busy or sm
-        return {"sm_mhz": statistics.median(pick) if pick else None, "sm_max_mhz": mx,
-                "reasons": sorted(reasons), "samples": len(sm), "samples_under_load": len(busy)}
+        return {"sm_mhz": statistics.median(inside) if inside else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm), "samples_in_timed_region": len(inside)}
 
 
 # -------------------------------------------------------------- CPU legs --
@@ -195,6 +196,18 @@ def cpu_baseline(seconds: float = 12.0, min_reps: int = 2):
                       f"(pool widening single-threaded); host cpus={os.cpu_count()}"}
 
 
+def workload_config(world: int) -> dict:
+    return {
+        "workload": "mixed-adapter decode batch: 7 Mistral-7B LoRA projections, 512 rows/GPU, "
+                    "rank 64, 256-slot pool, Zipf(1.1) slots + 5% rows without adapter",
+        "rows_per_gpu": ROWS_PER_GPU, "global_rows": ROWS_PER_GPU * world, "rank": RANK,
+        "pool_slots": POOL_SLOTS, "projections": [n for n, _, _ in projections()],
+        "parallelism": f"row-sharded x{world} (adapter affinity), pool replicated",
+        "l2": "inputs larger than L2: ~1.4 GB of adapter/x/y traffic per step vs 126 MB L2",
+        "launches_per_step": 1 + len(projections()),
+    }
+
+
 def run_reference(args):
     """The reference arm: the reference's CPU implementation of the path (its
     fp32 torch BGMV, restated by the oracle port) on the host cores.  Under
@@ -203,15 +216,17 @@ def run_reference(args):
     if rank != 0:
         return 0
     t0 = time.perf_counter()
-    # Per-step sample sized so that warm-up + steps stay within ~2 minutes.
-    full = CpuSample(rows=64, slots=32)
-    t1 = full.call()
+    # Per-step sample: the largest of these whose warm-up + steps fit in ~2 minutes.
     budget = 120.0
     steps = max(1, args.steps)
     warm = max(0, args.warmup)
-    smp = full
-    if (steps + warm) * t1 > budget:
-        smp = CpuSample(rows=16, slots=8)
+    smp = None
+    for rows, slots in ((64, 32), (16, 8), (4, 2), (1, 1)):
+        smp = CpuSample(rows=rows, slots=slots)
+        smp.call()
+        t1 = min(smp.call() for _ in range(2))
+        if (steps + warm) * t1 <= budget:
+            break
     for _ in range(warm):
         smp.call()
     times = [smp.call() for _ in range(steps)]
@@ -223,8 +238,7 @@ def run_reference(args):
         "steps": steps, "warmup": warm, "ms_per_step": med * 1e3,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded Zipf slots, random-init rank-64 adapters)",
-        "config": {"workload": "mixed-adapter decode batch, q_proj sample on the host CPU",
-                   "rank": RANK, "h_in": 4096, "h_out": 4096},
+        "config": workload_config(args.gpus),
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": th, "kind": "port",
                          "sample": f"{smp.desc}; median of {steps} steps; BLAS threads={th}"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -321,11 +335,13 @@ def run_ours(args):
     barrier()
     torch.cuda.synchronize()
     t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    host_t0 = time.monotonic()
     t_start.record(stream)
     for s in range(K_steps):
         step(evs[s])
     t_end.record(stream)
     torch.cuda.synchronize()
+    host_t1 = time.monotonic()
     barrier()
     ms_local = t_start.elapsed_time(t_end) / K_steps
     fused_ms = sum(evs[s][i][0].elapsed_time(evs[s][i][1]) for s in range(K_steps) for i in range(len(projs)))
@@ -363,7 +379,7 @@ def run_ours(args):
     torch.cuda.synchronize()
     barrier()
     e2e_ms_local = e_start.elapsed_time(e_end) / e_steps
-    clk = clocks.stop()
+    clk = clocks.stop(window=(host_t0, host_t1))
     ops.check_errors(dev)
 
     ms = max_over_ranks(ms_local)
@@ -392,15 +408,7 @@ def run_ours(args):
             "vs_baseline": None,
             "dtype": "f16",
             "data": "synthetic (seeded Zipf slots, random-init rank-64 adapters)",
-            "config": {
-                "workload": "mixed-adapter decode batch: 7 Mistral-7B LoRA projections, 512 rows/GPU, "
-                            "rank 64, 256-slot pool, Zipf(1.1) slots + 5% rows without adapter",
-                "rows_per_gpu": ROWS_PER_GPU, "global_rows": ROWS_PER_GPU * world, "rank": RANK,
-                "pool_slots": POOL_SLOTS, "projections": [p["name"] for p in projs],
-                "parallelism": f"row-sharded x{world} (adapter affinity), pool replicated",
-                "l2": "inputs larger than L2: ~1.4 GB of adapter/x/y traffic per step vs 126 MB L2",
-                "launches_per_step": 1 + len(projs),
-            },
+            "config": workload_config(world),
             "rows_per_s": total_rows / (ms * 1e-3),
             "roofline": {
                 "bound": "hbm",
