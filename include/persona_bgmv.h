@@ -47,6 +47,7 @@ extern "C" {
 #define PERSONA_ERR_RANK 5        /* LoRA rank this op does not support      */
 #define PERSONA_ERR_WORKSPACE 6   /* workspace missing or too small          */
 #define PERSONA_ERR_CUDA 7        /* CUDA runtime / launch failure           */
+#define PERSONA_ERR_NOALLOC_ROWS 8 /* T above PERSONA_NOALLOC_MAX_ROWS          */
 
 /* Device error-word bits (ORed into *dev_err by the kernels). */
 #define PERSONA_DEV_ERR_SLOT 1    /* a slot < -1 or >= S: that row was left alone */
@@ -136,6 +137,32 @@ int persona_sgmv_fused(const void* x, int64_t ldx, const void* a_pool, int64_t a
                        void* y, int64_t ldy, int64_t T, int64_t K, int64_t N, int64_t R, int64_t S,
                        int dtype, void* workspace, size_t workspace_bytes, int32_t* dev_err,
                        cudaStream_t stream);
+
+/* ---- fused BGMV without any allocation -----------------------------------
+ * No reference counterpart.  Same operation, arguments and results as
+ * persona_bgmv_fused, minus the workspace: the row-grouping plan lives in a
+ * fixed device array inside this library (one per device), so the call
+ * needs no buffer from the caller and allocates nothing itself.  It serves
+ * callers that cannot hand out device memory per call: an engine that has
+ * already carved all of HBM into its own pools (KV cache, adapter pool), or
+ * a host binding with no device allocator of its own.
+ * Limits and rules:
+ *  - T <= PERSONA_NOALLOC_MAX_ROWS; a larger T returns
+ *    PERSONA_ERR_NOALLOC_ROWS and enqueues nothing.
+ *  - The first call on a device looks the array's device address up
+ *    (cudaGetSymbolAddress, with that device current); make that first call
+ *    before any stream capture begins.
+ *  - Nothing in the array has to start at zero: each call rewrites the plan
+ *    before the kernel reads it.
+ *  - All calls on one device share the array: calls whose device work can
+ *    overlap (different streams, unsynchronised threads) race and must be
+ *    serialised, e.g. on one stream.                                        */
+#define PERSONA_NOALLOC_MAX_ROWS 8192
+int persona_bgmv_fused_noalloc(const void* x, int64_t ldx, const void* a_pool, int64_t a_slot_stride,
+                               int64_t a_row_stride, const void* b_pool, int64_t b_slot_stride,
+                               const int32_t* slots, void* y, int64_t ldy, int64_t T, int64_t K,
+                               int64_t N, int64_t R, int64_t S, int dtype, int32_t* dev_err,
+                               cudaStream_t stream);
 
 /* ---- warm-up GEMV ---------------------------------------------------------
  * y[n] = W[n, :] @ x (fp16, fp32 accumulate).  Replaces

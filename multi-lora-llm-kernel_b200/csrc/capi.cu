@@ -183,6 +183,7 @@ const char* persona_status_string(int status) {
     case PERSONA_ERR_RANK: return "R must be 8, 16, 32, or 64";
     case PERSONA_ERR_WORKSPACE: return "workspace missing, misaligned or too small";
     case PERSONA_ERR_CUDA: return "CUDA runtime or launch failure";
+    case PERSONA_ERR_NOALLOC_ROWS: return "T above PERSONA_NOALLOC_MAX_ROWS, the fixed plan scratch of persona_bgmv_fused_noalloc";
     default: return "unknown status";
   }
 }

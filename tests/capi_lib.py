@@ -27,6 +27,8 @@ SIGNATURES = {
     "persona_bgmv_fused": (_i32, [_p, _i64, _p, _i64, _i64, _p, _i64, _p, _p, _i64, _i64, _i64, _i64,
                                   _i64, _i64, _i32, _p, _sz, _i32, _p, _p]),
     "persona_gemv_fp16": (_i32, [_p, _p, _p, _i64, _i64, _p]),
+    "persona_bgmv_fused_noalloc": (_i32, [_p, _i64, _p, _i64, _i64, _p, _i64, _p, _p, _i64, _i64, _i64, _i64,
+                                          _i64, _i64, _i32, _p, _p]),
     "persona_sgmv_workspace_size": (_sz, [_i64]),
     "persona_sgmv_shrink": (_i32, [_p, _i64, _p, _i64, _i64, _p, _p, _i64, _p, _i64, _i64, _i64, _i64, _i32,
                                    _p, _sz, _p, _p]),
