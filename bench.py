@@ -54,6 +54,11 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", choices=["mixed_decode", "sgmv_prefill", "decode_set"],
+                    default="mixed_decode",
+                    help="mixed_decode is the headline; the others print their own line (1 GPU)")
+    ap.add_argument("--only", default=None,
+                    help="restrict to one projection (e.g. gate_proj), for profiling a small case")
     return ap.parse_args()
 
 
@@ -65,10 +70,13 @@ def load_peaks():
     return 6650.0, "fallback"
 
 
+ONLY = None
+
+
 def projections():
     from persona.workloads import PROJECTIONS
 
-    return [(n, k, nn) for n, (k, nn) in PROJECTIONS.items()]
+    return [(n, k, nn) for n, (k, nn) in PROJECTIONS.items() if ONLY is None or n == ONLY]
 
 
 def adapter_and_row_bytes():
@@ -441,10 +449,196 @@ def run_ours(args):
     return 0
 
 
+# ------------------------------------------------------ other workloads --
+
+def _timed(fn, steps, stream):
+    import torch
+
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(steps):
+        fn()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / steps
+
+
+def run_extra(args):
+    """Single-GPU lines for the segmented prefill (SGMV on the tensor cores)
+    and the small decode set (launch-latency bound; eager and CUDA graph)."""
+    import torch
+
+    from persona import ops
+    from persona.workloads import bgmv_bytes
+
+    if args.gpus != 1:
+        raise SystemExit(f"--workload {args.workload} runs on one GPU")
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    stream = torch.cuda.current_stream()
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(SEED * 1000 + 29)
+    steps, warm = max(1, args.steps), max(3, args.warmup)
+
+    def pools(K, N, R, S, dt):
+        lim = 1.0 / np.sqrt(K)
+        a = (torch.rand(S, R, K, generator=gen, device=dev) * (2 * lim) - lim).to(dt)
+        b = (torch.randn(S, N, R, generator=gen, device=dev) * 0.04).to(dt)
+        return a, b
+
+    if args.workload == "sgmv_prefill":
+        # 32 requests x 512 rows, rank 16, 32 adapters, bf16; gate/up/down.
+        req, rows, R, S = 32, 512, 16, 32
+        T = req * rows
+        rng = np.random.Generator(np.random.PCG64(SEED + 1))
+        seg = rng.permutation(req).astype(np.int32)
+        indptr = (np.arange(req + 1) * rows).astype(np.int32)
+        slots = np.repeat(seg, rows)
+        ip, ss = torch.from_numpy(indptr).to(dev), torch.from_numpy(seg).to(dev)
+        names = [n for n in ("gate_proj", "up_proj", "down_proj") if ONLY is None or n == ONLY]
+        from persona.workloads import PROJECTIONS
+
+        projs = []
+        for n in names:
+            K, N = PROJECTIONS[n]
+            a, b = pools(K, N, R, S, torch.bfloat16)
+            x = torch.randn(T, K, generator=gen, device=dev).to(torch.bfloat16)
+            y = torch.zeros(T, N, device=dev, dtype=torch.bfloat16)
+            projs.append(dict(name=n, K=K, N=N, a=a, b=b, x=x, y=y, bytes=bgmv_bytes(K, N, R, slots),
+                              flops=2 * T * R * (K + N)))
+        evs = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in projs]
+               for _ in range(steps)]
+
+        def step(ev=None):
+            for i, p in enumerate(projs):
+                if ev is not None:
+                    ev[i][0].record(stream)
+                ops.sgmv_fused(p["x"], p["a"], p["b"], ip, ss, p["y"])
+                if ev is not None:
+                    ev[i][1].record(stream)
+
+        for _ in range(warm):
+            step()
+        torch.cuda.synchronize()
+        ops.check_errors(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for k in range(steps):
+            step(evs[k])
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ops.check_errors(dev)
+        ms = e0.elapsed_time(e1) / steps
+        per = {p["name"]: sum(evs[k][i][0].elapsed_time(evs[k][i][1]) for k in range(steps)) / steps
+               for i, p in enumerate(projs)}
+        tot_b = sum(p["bytes"] for p in projs)
+        tot_f = sum(p["flops"] for p in projs)
+        peak, _ = load_peaks()
+        tpk = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()).get("bf16_tflops") \
+            if (ROOT / "MEASURED_PEAKS.json").exists() else 1590.0
+        line = {
+            "workload": "sgmv_prefill", "metric": "SGMV fused shrink+expand GB/s (algorithmic)",
+            "value": tot_b / (ms * 1e-3) / 1e9, "unit": "GB/s", "n_gpus": 1, "steps": steps, "warmup": warm,
+            "ms_per_step": ms, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "segmented prefill: 32 requests x 512 rows contiguous by adapter, rank 16, "
+                                   "32-slot pool, bf16", "projections": names,
+                       "l2": "inputs larger than L2 (~2.9 GB per step)"},
+            "per_projection": {n: {"ms": t, "GB/s": p["bytes"] / (t * 1e-3) / 1e9,
+                                   "TFLOP/s": p["flops"] / (t * 1e-3) / 1e12,
+                                   "hbm_frac": p["bytes"] / (t * 1e-3) / 1e9 / peak}
+                               for (n, t), p in zip(per.items(), projs)},
+            "tensor": {"TFLOP/s": tot_f / (ms * 1e-3) / 1e12, "peak_bf16_tflops": tpk,
+                       "frac": tot_f / (ms * 1e-3) / 1e12 / tpk},
+            "roofline": {"bound": "hbm", "achieved": tot_b / (ms * 1e-3) / 1e9, "peak": peak, "unit": "GB/s",
+                         "frac": tot_b / (ms * 1e-3) / 1e9 / peak},
+            "gpu_launches": steps * len(projs) * 2,
+        }
+        print(json.dumps(line), flush=True)
+        return 0
+
+    # decode_set: 7 projections, T=8, rank 16, 8 adapters (slots = a permutation), fp16.
+    from persona.workloads import PROJECTIONS
+
+    T, R, S = 8, 16, 8
+    copies = 8  # rotate through 8 independent sets (~184 MB > L2) so no step hits in L2
+    rng = np.random.Generator(np.random.PCG64(SEED + 2))
+    sets = []
+    for c in range(copies):
+        slots = rng.permutation(S).astype(np.int32)
+        sd = torch.from_numpy(slots).to(dev)
+        projs = []
+        for n, (K, N) in PROJECTIONS.items():
+            if ONLY is not None and n != ONLY:
+                continue
+            a, b = pools(K, N, R, S, torch.float16)
+            projs.append(dict(K=K, N=N, a=a, b=b, x=torch.randn(T, K, generator=gen, device=dev).half(),
+                              y=torch.zeros(T, N, device=dev, dtype=torch.float16),
+                              bytes=bgmv_bytes(K, N, R, slots)))
+        sets.append(dict(slots=sd, projs=projs))
+    step_bytes = sum(p["bytes"] for p in sets[0]["projs"])
+
+    def fused_all():
+        for st in sets:
+            plan = ops.bgmv_plan(st["slots"], S)
+            for p in st["projs"]:
+                ops.bgmv_fused(p["x"], p["a"], p["b"], st["slots"], p["y"], plan=plan)
+
+    def separate_all():
+        for st in sets:
+            plan = ops.bgmv_plan(st["slots"], S)
+            for p in st["projs"]:
+                v = ops.bgmv_shrink(p["x"], p["a"], st["slots"], plan=plan)
+                ops.bgmv_expand(v, p["b"], st["slots"], p["y"], plan=plan)
+
+    for _ in range(warm):
+        fused_all()
+        separate_all()
+    ops.check_errors(dev)
+    reps = max(1, steps // copies)
+    eager_f = _timed(fused_all, reps, stream) / copies
+    eager_s = _timed(separate_all, reps, stream) / copies
+    g = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream()
+    side.wait_stream(stream)
+    with torch.cuda.stream(side):
+        fused_all()
+    stream.wait_stream(side)
+    torch.cuda.synchronize()
+    with torch.cuda.graph(g):
+        fused_all()
+    for _ in range(warm):
+        g.replay()
+    graph_f = _timed(g.replay, reps, stream) / copies
+    ops.check_errors(dev)
+    peak, _ = load_peaks()
+    line = {
+        "workload": "decode_set", "metric": "decode step of 7 fused LoRA projections, us per step",
+        "value": graph_f * 1e3, "unit": "us", "higher_is_better": False, "n_gpus": 1,
+        "steps": reps * copies, "warmup": warm, "dtype": "f16", "data": "synthetic",
+        "config": {"workload": "7 Mistral-7B projections, 8 rows, rank 16, 8 adapters (one per row), fp16",
+                   "l2": f"{copies} independent input sets rotated (~{copies * step_bytes / 1e6:.0f} MB > L2)"},
+        "us_per_step": {"fused_graph": graph_f * 1e3, "fused_eager": eager_f * 1e3,
+                        "separate_eager": eager_s * 1e3},
+        "algorithmic_bytes_per_step": step_bytes,
+        "GB/s": {"fused_graph": step_bytes / (graph_f * 1e-3) / 1e9,
+                 "fused_eager": step_bytes / (eager_f * 1e-3) / 1e9},
+        "hbm_frac_fused_graph": step_bytes / (graph_f * 1e-3) / 1e9 / peak,
+        "launches_per_step": 1 + len(sets[0]["projs"]),
+    }
+    g.reset()
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
+    global ONLY
     args = parse_args()
+    ONLY = args.only
     if args.impl == "reference":
         return run_reference(args)
+    if args.workload != "mixed_decode":
+        return run_extra(args)
     return run_ours(args)
 
 

@@ -22,6 +22,7 @@ struct BgmvArgs {
   const int32_t* plan;
   int32_t* err;
   int T, K, N, S;
+  int units_per_cta;  // split kernels: target work units per CTA (0 = default)
   int k_per_cta;       // K slice of one cluster CTA, multiple of 64
   int n_per_cta;       // N slice of one cluster CTA, multiple of n_box
   int n_box;           // rows of one B tile, multiple of 8, <= 256
@@ -40,6 +41,10 @@ cudaError_t launch_sgmv_plan(const int32_t* indptr, const int32_t* seg_slots, in
                              int rows_per_item, int32_t* plan, int32_t* row_slots, int32_t* dev_err,
                              cudaStream_t stream);
 int bgmv_stage_rows(int R);
+// Split kernels (bgmv_split.cu): every item cut into K / N slices claimed by
+// all CTAs; workspace = bgmv_ws_bytes(T) (plan_layout.h).
+cudaError_t launch_bgmv_split(int mode, int dtype, int R, const CUtensorMap& tmA, const CUtensorMap& tmB,
+                              const BgmvArgs& a, int max_ctas, cudaStream_t st);
 
 // Segmented tensor-core kernels (sgmv_tcgen05.cu).
 struct SgmvTcArgs {

@@ -27,6 +27,15 @@
 
 namespace persona {
 
+// Zero the split kernels' shared state (claim counter, per-item counters and
+// ready words) and start the epoch at 1; run by every thread of a plan kernel.
+__device__ __forceinline__ void init_work_state(int32_t* ws, int T, int tid, int nthreads) {
+  WorkView w = work_view(ws, T);
+  const int words = kSyncWords + 2 * static_cast<int>(plan_tpad(T));
+  for (int i = tid; i < words; i += nthreads) w.sync[i] = (i == kSyncEpoch) ? 1 : 0;
+}
+
+
 template <int THREADS, int IPT>
 __global__ void __launch_bounds__(THREADS)
     bgmv_plan_kernel(const int32_t* __restrict__ slots, int T, int S, int rows_per_item,
@@ -44,6 +53,7 @@ __global__ void __launch_bounds__(THREADS)
   const int tid = threadIdx.x;
   PlanView pv = plan_view(plan, T);
   if (tid < 4) s_counts[tid] = 0;
+  init_work_state(plan, T, tid, THREADS);
 
   const uint32_t key_null = static_cast<uint32_t>(S);
   const uint32_t key_bad = static_cast<uint32_t>(S) + 1u;
@@ -195,6 +205,7 @@ __global__ void __launch_bounds__(THREADS)
   __shared__ int s_lo[THREADS], s_hi[THREADS], s_slot[THREADS];
   const int tid = threadIdx.x;
   PlanView pv = plan_view(plan, T);
+  init_work_state(plan, T, tid, THREADS);
   for (int t = tid; t < T; t += THREADS) {
     row_slots[t] = -1;
     pv.perm[t] = t;

@@ -1,0 +1,757 @@
+// Split BGMV kernels for B200 (sm_100a): shrink, expand and fused
+// shrink->expand over a row-grouping plan, with each item's work cut into
+// slices that every CTA of the GPU can take.
+//
+// Work units.  A plan item is one adapter slot and up to 16 rows that use it.
+// Its shrink is cut into nks K-slices and its expand into nes N-slices; the
+// unit list is [all shrink slices, item by item] then [all expand slices].
+// Slice counts are chosen on the device from the item count so that the GPU
+// gets about 8 units per CTA: a decode batch of 8 adapters is spread over the
+// whole GPU, and a batch of ~150 adapters no longer leaves most CTAs idle
+// while a few stream a second whole adapter.
+//
+// Scheduling.  Persistent CTAs (two per SM) claim units in list order from a
+// device-wide counter.  Because every shrink unit precedes every expand unit
+// in claim order, a CTA that waits for an item's v only waits on shrink units
+// that running CTAs have already claimed, so the kernel always makes progress
+// even when not all CTAs are resident.
+//
+// Partial v.  A shrink slice writes its partial v (16 rows x R, fp32) to the
+// workspace (L2-resident).  The CTA that completes an item's last slice
+// (per-item counter) sums the partials in slice order -- so the result does
+// not depend on which CTA ran what -- writes v, and releases the item by
+// storing the call's epoch into its ready word.  Expand slices wait for that
+// word (bounded), read v, and stream B and y.  The epoch (bumped by the last
+// CTA of every launch) makes stale ready words from earlier calls harmless,
+// and the last CTA also resets the claim counter for the next launch.
+//
+// Inside a CTA (six warps): one producer warp (TMA boxes of A / B, 1-D bulk
+// copies of the x / y / v rows, L2 prefetch of the next unit) feeds a 4-slot
+// ring.  Four consumer warps run the shrink stages on the 16-row warp-MMA
+// tiles of bgmv_stages.cuh.  For ranks 16 / 32 / 64 the expand runs on the
+// tensor cores: the item's rows are the N = 16 side of a tcgen05 MMA whose
+// M = 128 side is a TMA-loaded B tile, so one MMA warp turns a stage into
+// D[128 output columns][16 rows] in tensor memory with 2 * R / 16
+// instructions (v split into 16-bit hi and lo halves, both as small swizzled
+// shared-memory operands), and a consumer thread per output column only
+// reads its 16 accumulators, adds y and stores.  Rank 8 keeps the warp-MMA
+// expand.
+#include "bgmv_stages.cuh"
+#include "tcgen05.cuh"
+
+namespace persona {
+
+namespace {
+
+constexpr int kUnitRing = 4;
+constexpr int kUnitsPerCta = 8;
+// One CTA per SM (kernels that allocate tensor memory are scheduled one per
+// SM) running kGroups independent pipelines of six warps: 4 consumers, a
+// producer and an MMA warp, each group with its own ring and unit queue.
+constexpr int kGroups = 2;
+constexpr int kGroupThreads = kBgmvThreads + 32;  // + one MMA warp
+constexpr int kSplitThreads = kGroups * kGroupThreads;
+constexpr int kMmaWarp = kConsumerWarps + 1;
+constexpr uint32_t kGroupTmemCols = 128;  // one 16-column accumulator per (ring slot, 128-row box)
+constexpr uint32_t kTmemCols = kGroups * kGroupTmemCols;
+enum : int { kUnitEnd = 0, kUnitShrink = 1, kUnitExpand = 2 };
+
+struct UnitDesc {
+  int kind;
+  int item;
+  int slice;
+  int slot;
+  int count;
+  int pos;  // plan position of the item's first row
+  int pad[2];
+  int rows[kRowsPerItem];
+};
+
+constexpr int kSRingBytes = kSlots * kSlotBytes;
+constexpr int kSVBytes = kRowsPerItem * kMaxR * 4;
+constexpr int kSRedBytes = kRowsPerItem * kMaxR * 4;
+constexpr int kSUnitBytes = kUnitRing * static_cast<int>(sizeof(UnitDesc));
+constexpr int kSVopBytes = 2 * kRowsPerItem * kMaxR * 2;  // v hi / lo MMA operands, 16 rows x R each
+constexpr int kSBarCount = 3 * kSlots + 2 * kUnitRing + 2;
+constexpr int kGroupSmemRaw = kSRingBytes + kSVopBytes + 2 * kSVBytes + kSRedBytes + kSUnitBytes + kSBarCount * 8 + 16;
+constexpr int kGroupSmem = (kGroupSmemRaw + 1023) / 1024 * 1024;
+constexpr int kSplitSmemBytes = kGroups * kGroupSmem + 1024;
+static_assert(kSplitSmemBytes <= 227 * 1024, "one CTA per SM");
+
+struct SplitSmem {
+  uint8_t* ring;
+  uint8_t* vop;  // [hi | lo] expand operands (1024-aligned)
+  float* pv;   // [16][R] this unit's partial / the item's v
+  float* vf;   // [16][R] the item's v for the expand
+  float* red;  // per-warp MMA tiles / maxima
+  UnitDesc* units;
+  uint64_t* full;
+  uint64_t* empty;
+  uint64_t* ufull;
+  uint64_t* uempty;
+  uint64_t* mma_done;  // [kSlots] expand MMAs of the slot's stage complete
+  uint64_t* vready;    // the expand unit's v operands are in shared memory
+  uint64_t* mma_fin;   // every MMA of the CTA complete (before TMEM is freed)
+  int* flag;
+  uint32_t* tmem_base;
+};
+
+__device__ __forceinline__ SplitSmem carve(uint8_t* raw, int grp) {
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023)) +
+                  grp * kGroupSmem;
+  SplitSmem p;
+  p.ring = base;
+  p.vop = base + kSRingBytes;
+  uint8_t* q = base + kSRingBytes + kSVopBytes;
+  p.pv = reinterpret_cast<float*>(q);
+  p.vf = reinterpret_cast<float*>(q + kSVBytes);
+  p.red = reinterpret_cast<float*>(q + 2 * kSVBytes);
+  p.units = reinterpret_cast<UnitDesc*>(q + 2 * kSVBytes + kSRedBytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(q + 2 * kSVBytes + kSRedBytes + kSUnitBytes);
+  p.full = bars;
+  p.empty = bars + kSlots;
+  p.ufull = bars + 2 * kSlots;
+  p.uempty = bars + 2 * kSlots + kUnitRing;
+  p.mma_done = bars + 2 * kSlots + 2 * kUnitRing;
+  p.vready = bars + 3 * kSlots + 2 * kUnitRing;
+  p.mma_fin = bars + 3 * kSlots + 2 * kUnitRing + 1;
+  p.flag = reinterpret_cast<int*>(bars + kSBarCount);
+  p.tmem_base = reinterpret_cast<uint32_t*>(bars + kSBarCount) + 1;
+  return p;
+}
+
+// Slice geometry; every thread of every CTA computes the same values.
+struct SplitGeom {
+  int kst, nst;      // A stages over K, B stages over N
+  int ks_st, es_st;  // stages per shrink / expand slice
+  int nks, nes;      // slices per item
+  int units_s, units;
+};
+
+__device__ __forceinline__ SplitGeom split_geom(int n_items, int K, int N, int kc, int stage_rows, int grid,
+                                                int units_per_cta, bool shrink, bool expand) {
+  SplitGeom g;
+  g.kst = shrink ? (K + kc - 1) / kc : 0;
+  g.nst = expand ? (N + stage_rows - 1) / stage_rows : 0;
+  const int items = n_items > 0 ? n_items : 1;
+  const int upc = units_per_cta > 0 ? units_per_cta : kUnitsPerCta;
+  const int per_item = max(1, (upc * grid + items - 1) / items);
+  int nks = 1, nes = 1;
+  if (shrink && expand) {
+    nks = max(1, (per_item * g.kst + (g.kst + g.nst) / 2) / (g.kst + g.nst));
+    nes = max(1, per_item - nks);
+  } else if (shrink) {
+    nks = per_item;
+  } else {
+    nes = per_item;
+  }
+  nks = min(min(nks, max(1, g.kst)), max(1, kPartSlots / items));
+  nes = min(nes, max(1, g.nst));
+  g.ks_st = shrink ? (g.kst + nks - 1) / nks : 0;
+  g.nks = shrink ? (g.kst + g.ks_st - 1) / g.ks_st : 0;
+  g.es_st = expand ? (g.nst + nes - 1) / nes : 0;
+  g.nes = expand ? (g.nst + g.es_st - 1) / g.es_st : 0;
+  g.units_s = n_items * g.nks;
+  g.units = g.units_s + n_items * g.nes;
+  return g;
+}
+
+__device__ __forceinline__ uint16_t lds16(uint32_t addr) {
+  uint16_t v;
+  asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(addr));
+  return v;
+}
+__device__ __forceinline__ void sts32(uint32_t addr, uint32_t v) {
+  asm volatile("st.shared.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ int ld_acquire(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release(int* p, int v) {
+  asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Spin (bounded) until *p == want; false (and the timeout bit) if it never does.
+__device__ __forceinline__ bool wait_word(const int* p, int want, int32_t* err) {
+  if (ld_acquire(p) == want) return true;
+  const long long t0 = clock64();
+  while (ld_acquire(p) != want) {
+    if (clock64() - t0 > kWaitBudgetCycles) {
+      raise_error(err, PERSONA_DEV_ERR_TIMEOUT);
+      return false;
+    }
+    __nanosleep(64);
+  }
+  return true;
+}
+
+}  // namespace
+
+template <typename DT, int R, int MODE>
+__global__ void __launch_bounds__(kSplitThreads, 1)
+    bgmv_split_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                      const BgmvArgs args) {
+  using C = RankCfg<R>;
+  constexpr bool kDoShrink = (MODE & kModeShrink) != 0;
+  constexpr bool kDoExpand = (MODE & kModeExpand) != 0;
+  constexpr bool kTcE = kDoExpand && R >= 16;  // expand on tcgen05
+  // expand MMA operands: K-major rows of 2R bytes, swizzled over 2R bytes
+  constexpr uint32_t kOpLayout = R >= 64 ? tc::kLayoutSw128 : R == 32 ? tc::kLayoutSw64 : tc::kLayoutSw32;
+  constexpr uint32_t kOpSbo = 8 * 2 * R;
+  constexpr uint32_t kIdesc = tc::idesc_f16(std::is_same<DT, __nv_bfloat16>::value ? 1u : 0u, 128, kRowsPerItem);
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ uint32_t s_tmem;
+  const int grp = static_cast<int>(threadIdx.x) / kGroupThreads;  // pipeline of this thread
+  const int tid = static_cast<int>(threadIdx.x) - grp * kGroupThreads;
+  const int warp = tid >> 5, lane = tid & 31;
+  const int bar_cons = kNamedBarConsumers + grp;  // named barrier of this group's consumers
+  SplitSmem sm = carve(smem_raw, grp);
+
+  if (tid == 0) {
+    for (int s = 0; s < kSlots; ++s) {
+      mbar_init(&sm.full[s], 1);
+      mbar_init(&sm.empty[s], kConsumerWarps);
+    }
+    for (int i = 0; i < kUnitRing; ++i) {
+      mbar_init(&sm.ufull[i], 1);
+      mbar_init(&sm.uempty[i], kConsumerWarps + 1);  // consumers + the MMA warp
+    }
+    for (int s = 0; s < kSlots; ++s) mbar_init(&sm.mma_done[s], 1);
+    mbar_init(sm.vready, 1);
+    mbar_init(sm.mma_fin, 1);
+    *sm.tmem_base = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (kTcE && grp == 0 && warp == kMmaWarp) {  // one allocation for both groups
+    tc::tmem_alloc(&s_tmem, kTmemCols);
+    tc::tmem_relinquish();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = s_tmem + static_cast<uint32_t>(grp) * kGroupTmemCols;
+
+  int32_t* ws = const_cast<int32_t*>(args.plan);
+  PlanView pv = plan_view(ws, args.T);
+  WorkView wv = work_view(ws, args.T);
+  const int n_items = pv.hdr[kHdrItems];
+  const int epoch = wv.sync[kSyncEpoch];
+  const int stage_rows = (C::kNB / args.n_box) * args.n_box;
+  const SplitGeom G = split_geom(n_items, args.K, args.N, C::kKC, stage_rows, static_cast<int>(gridDim.x) * kGroups,
+                                 args.units_per_cta, kDoShrink, kDoExpand);
+
+  if (warp == kConsumerWarps) {
+    // ------------------------------------------------------- producer --
+    const uint16_t* x = static_cast<const uint16_t*>(args.x);
+    const uint16_t* yg = static_cast<const uint16_t*>(args.y);
+    if (lane == 0) {
+      if (kDoShrink) tma_prefetch_desc(&tmA);
+      if (kDoExpand) tma_prefetch_desc(&tmB);
+    }
+    // Claims run two units ahead: the atomic for unit j+2 is issued while
+    // unit j streams, and its result is first read one unit later, so the
+    // round trip to L2 never stalls the loads.
+    auto claim_issue = [&]() -> int { return lane == 0 ? atomicAdd(&wv.sync[kSyncQueue], 1) : 0; };
+    auto claim_read = [&](int pending) -> int { return __shfl_sync(0xffffffffu, pending, 0); };
+    struct Dec {
+      int kind, item, slice, lo, hi;  // [lo, hi): k range (shrink) or n range (expand)
+    };
+    auto decode = [&](int u) -> Dec {
+      Dec d;
+      if (u >= G.units) {
+        d.kind = kUnitEnd;
+        d.item = d.slice = d.lo = d.hi = 0;
+      } else if (u < G.units_s) {
+        d.kind = kUnitShrink;
+        d.item = u / G.nks;
+        d.slice = u - d.item * G.nks;
+        d.lo = d.slice * G.ks_st * C::kKC;
+        d.hi = min(args.K, d.lo + G.ks_st * C::kKC);
+      } else {
+        const int v = u - G.units_s;
+        d.kind = kUnitExpand;
+        d.item = v / G.nes;
+        d.slice = v - d.item * G.nes;
+        d.lo = d.slice * G.es_st * stage_rows;
+        d.hi = min(args.N, d.lo + G.es_st * stage_rows);
+      }
+      return d;
+    };
+    uint32_t g = 0;
+    auto claim_slot = [&](uint32_t bytes) -> int {
+      const int s = static_cast<int>(g % kSlots);
+      if (lane == 0) {
+        if (g >= kSlots) mbar_wait(&sm.empty[s], ((g / kSlots) - 1) & 1, args.err);
+        mbar_arrive_expect_tx(&sm.full[s], bytes);
+      }
+      __syncwarp();
+      return s;
+    };
+    int u = claim_read(claim_issue());
+    int pending = claim_issue();
+    for (int j = 0;; ++j) {
+      const Dec d = decode(u);
+      const int iq = j % kUnitRing;
+      if (lane == 0 && j >= kUnitRing) mbar_wait(&sm.uempty[iq], ((j / kUnitRing) - 1) & 1, args.err);
+      __syncwarp();
+      int4 it = make_int4(0, 0, 0, 0);
+      int row = 0;
+      if (d.kind != kUnitEnd) {
+        it = pv.items[d.item];
+        row = lane < it.z ? pv.perm[it.y + lane] : 0;
+      }
+      UnitDesc* ud = &sm.units[iq];
+      if (lane < kRowsPerItem) ud->rows[lane] = row;
+      if (lane == 0) {
+        ud->kind = d.kind;
+        ud->item = d.item;
+        ud->slice = d.slice;
+        ud->slot = it.x;
+        ud->count = it.z;
+        ud->pos = it.y;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.ufull[iq]);
+      if (d.kind == kUnitEnd) break;
+
+      // The next unit is known; start pulling its data into L2 so that its
+      // loads hit L2 and more bytes are in flight than the ring holds.
+      const int un = claim_read(pending);
+      pending = un < G.units ? claim_issue() : 0;
+      const Dec dn = decode(un);
+      if (dn.kind != kUnitEnd) {
+        const int4 nit = pv.items[dn.item];
+        const int nrow = lane < nit.z ? pv.perm[nit.y + lane] : 0;
+        if (dn.kind == kUnitShrink) {
+          for (int k0 = dn.lo + 64 * lane; k0 < dn.hi; k0 += 64 * 32) tma_prefetch_3d(&tmA, k0, 0, nit.x);
+          if (lane < nit.z)
+            bulk_prefetch_l2(x + static_cast<int64_t>(nrow) * args.ldx + dn.lo,
+                             static_cast<uint32_t>(dn.hi - dn.lo) * 2u);
+        } else {
+          for (int n0 = dn.lo + args.n_box * lane; n0 < dn.hi; n0 += args.n_box * 32)
+            tma_prefetch_3d(&tmB, 0, n0, nit.x);
+          if (lane < nit.z)
+            bulk_prefetch_l2(yg + static_cast<int64_t>(nrow) * args.ldy + dn.lo,
+                             static_cast<uint32_t>(dn.hi - dn.lo) * 2u);
+        }
+      }
+
+      const int slot = it.x, c = it.z;
+      if (d.kind == kUnitShrink) {
+        for (int k0 = d.lo; k0 < d.hi; k0 += C::kKC) {
+          const int valid = min(C::kKC, d.hi - k0);
+          const int nbox = (valid + 63) / 64;
+          const uint32_t xb = static_cast<uint32_t>(valid) * 2u;
+          const int s = claim_slot(static_cast<uint32_t>(nbox * C::kABoxBytes) + static_cast<uint32_t>(c) * xb);
+          uint8_t* st = sm.ring + s * kSlotBytes;
+          if (lane == 0)
+            for (int b = 0; b < nbox; ++b) tma_load_3d(st + b * C::kABoxBytes, &tmA, &sm.full[s], k0 + 64 * b, 0, slot);
+          if (lane < c)
+            bulk_load(st + C::kXOff + lane * C::kXPitch, x + static_cast<int64_t>(row) * args.ldx + k0, xb,
+                      &sm.full[s]);
+          ++g;
+        }
+      } else {
+        if (MODE == kModeExpand) {
+          const int s = claim_slot(static_cast<uint32_t>(c * R * 4));
+          if (lane < c)
+            bulk_load(sm.ring + s * kSlotBytes + lane * R * 4, args.v_in + static_cast<int64_t>(row) * R, R * 4,
+                      &sm.full[s]);
+          ++g;
+        }
+        for (int n0 = d.lo; n0 < d.hi; n0 += stage_rows) {
+          const int rows_here = min(stage_rows, d.hi - n0);
+          const int nbox = (rows_here + args.n_box - 1) / args.n_box;
+          const uint32_t yb = static_cast<uint32_t>(rows_here) * 2u;
+          const int s = claim_slot(static_cast<uint32_t>(nbox * args.n_box * 2 * R) + static_cast<uint32_t>(c) * yb);
+          uint8_t* st = sm.ring + s * kSlotBytes;
+          if (lane == 0)
+            for (int b = 0; b < nbox; ++b)
+              tma_load_3d(st + b * args.n_box * 2 * R, &tmB, &sm.full[s], 0, n0 + b * args.n_box, slot);
+          if (lane < c)
+            bulk_load(st + C::kYOff + lane * C::kYStride, yg + static_cast<int64_t>(row) * args.ldy + n0, yb,
+                      &sm.full[s]);
+          ++g;
+        }
+      }
+      u = un;
+    }
+    __syncwarp();
+  } else if (warp == kMmaWarp) {
+    // ------------------------------------------------------------ MMA --
+    // Follows the unit ring and the stage ring; for every expand stage of a
+    // tensor-core kernel it issues D[box] = B_box * (v_hi + v_lo)^T into the
+    // slot's accumulators and commits to mma_done[slot]; every other stage
+    // gets a plain arrive so that mma_done keeps one phase per slot use.
+    if (lane == 0) {
+      uint32_t g = 0, ue = 0;
+      const uint32_t vop = smem_u32(sm.vop);
+      for (int j = 0;; ++j) {
+        const int iq = j % kUnitRing;
+        mbar_wait(&sm.ufull[iq], (j / kUnitRing) & 1, args.err);
+        const int kind = sm.units[iq].kind, slice = sm.units[iq].slice;
+        if (kind == kUnitEnd) break;
+        int nst, lo = 0, hi = 0;
+        if (kind == kUnitShrink) {
+          const int klo = slice * G.ks_st * C::kKC;
+          nst = (min(args.K, klo + G.ks_st * C::kKC) - klo + C::kKC - 1) / C::kKC;
+        } else {
+          lo = slice * G.es_st * stage_rows;
+          hi = min(args.N, lo + G.es_st * stage_rows);
+          nst = (hi - lo + stage_rows - 1) / stage_rows;
+          if (MODE == kModeExpand) {  // the v stage
+            const int s = static_cast<int>(g % kSlots);
+            mbar_wait(&sm.full[s], (g / kSlots) & 1, args.err);
+            mbar_arrive(&sm.mma_done[s]);
+            ++g;
+          }
+        }
+        const bool tc_unit = kTcE && kind == kUnitExpand;
+        if (tc_unit) {
+          mbar_wait(sm.vready, ue & 1, args.err);
+          tc::fence_after_sync();
+          ++ue;
+        }
+        for (int i = 0; i < nst; ++i, ++g) {
+          const int s = static_cast<int>(g % kSlots);
+          mbar_wait(&sm.full[s], (g / kSlots) & 1, args.err);
+          if (tc_unit) {
+            tc::fence_after_sync();
+            const int rows_here = min(stage_rows, hi - (lo + i * stage_rows));
+            const int nbt = (rows_here + 127) / 128;
+            const uint32_t sb = smem_u32(sm.ring + s * kSlotBytes);
+            for (int b = 0; b < nbt; ++b) {
+              const uint32_t d = tmem + static_cast<uint32_t>((s * 2 + b) * kRowsPerItem);
+#pragma unroll
+              for (int ks = 0; ks < R / 16; ++ks) {
+                const uint64_t a = tc::smem_desc(sb + b * 128 * 2 * R + ks * 32, kOpSbo, kOpLayout);
+                tc::mma_f16(d, a, tc::smem_desc(vop + ks * 32, kOpSbo, kOpLayout), kIdesc, ks > 0 ? 1u : 0u);
+                tc::mma_f16(d, a, tc::smem_desc(vop + kRowsPerItem * 2 * R + ks * 32, kOpSbo, kOpLayout), kIdesc,
+                            1u);
+              }
+            }
+            tc::commit(&sm.mma_done[s]);
+          } else {
+            mbar_arrive(&sm.mma_done[s]);
+          }
+        }
+        mbar_arrive(&sm.uempty[iq]);
+      }
+      // Every MMA this thread issued completes before TMEM is released.
+      tc::commit(sm.mma_fin);
+      mbar_wait(sm.mma_fin, 0, args.err);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------ consumers --
+    uint16_t* y = static_cast<uint16_t*>(args.y);
+    if (MODE == kModeShrink) {
+      // Rows without a (valid) adapter get v = 0; the items never touch them.
+      const int gtid = (blockIdx.x * kGroups + grp) * kConsumers + tid;
+      const int gstride = gridDim.x * kGroups * kConsumers;
+      for (int i = gtid; i < args.T * R; i += gstride) {
+        const int s = args.slots[i / R];
+        if (s < 0 || s >= args.S) args.v_out[i] = 0.f;
+      }
+    }
+    uint32_t g = 0;
+    for (int j = 0;; ++j) {
+      const int iq = j % kUnitRing;
+      mbar_wait(&sm.ufull[iq], (j / kUnitRing) & 1, args.err);
+      const UnitDesc* ud = &sm.units[iq];
+      const int kind = ud->kind;
+      if (kind == kUnitEnd) break;
+      const int c = ud->count, item = ud->item, slice = ud->slice, pos = ud->pos;
+      const int* rows = ud->rows;
+      const int E = c * R;
+
+      if (kDoShrink && kind == kUnitShrink) {
+        const int klo = slice * G.ks_st * C::kKC;
+        const int khi = min(args.K, klo + G.ks_st * C::kKC);
+        float d[C::kTPW][2][4];
+#pragma unroll
+        for (int t = 0; t < C::kTPW; ++t)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) d[t][0][i] = d[t][1][i] = 0.f;
+        for (int k0 = klo; k0 < khi; k0 += C::kKC, ++g) {
+          const int s = static_cast<int>(g % kSlots);
+          mbar_wait(&sm.full[s], (g / kSlots) & 1, args.err);
+          uint8_t* st = sm.ring + s * kSlotBytes;
+          const int valid = min(C::kKC, khi - k0);
+          if (valid & 63) {
+            // The last A tile reads zeros past K; zero the matching x columns so
+            // that stale shared memory cannot inject NaN * 0.
+            const int tail = ((valid + 63) & ~63) - valid;
+            for (int e = tid; e < c * tail; e += kConsumers) {
+              const int rr = e / tail, kk = valid + e % tail;
+              reinterpret_cast<uint16_t*>(st + C::kXOff + rr * C::kXPitch)[kk] = 0;
+            }
+            named_sync(bar_cons, kConsumers);
+          }
+          shrink_stage<DT, R>(st, ((valid + 63) / 64) * 4, warp, lane, d);
+          __syncwarp();
+          if (lane == 0) mbar_arrive_relaxed(&sm.empty[s]);
+        }
+        // This slice's partial v: sum the two accumulators and the warps that
+        // split k for each rank tile.
+#pragma unroll
+        for (int t = 0; t < C::kTPW; ++t) {
+          float* rw = sm.red + (warp * C::kTPW + t) * (kRowsPerItem * 8);
+          const int gg = lane >> 2, tt = lane & 3;
+          rw[gg * 8 + 2 * tt] = d[t][0][0] + d[t][1][0];
+          rw[gg * 8 + 2 * tt + 1] = d[t][0][1] + d[t][1][1];
+          rw[(gg + 8) * 8 + 2 * tt] = d[t][0][2] + d[t][1][2];
+          rw[(gg + 8) * 8 + 2 * tt + 1] = d[t][0][3] + d[t][1][3];
+        }
+        named_sync(bar_cons, kConsumers);
+        for (int e = tid; e < E; e += kConsumers) {
+          const int rr = e / R, r = e - rr * R;
+          const int T = r >> 3, col = r & 7;
+          float sum = 0.f;
+#pragma unroll
+          for (int ks = 0; ks < C::kKS; ++ks)
+            sum += sm.red[(((T / C::kTPW) * C::kKS + ks) * C::kTPW + (T % C::kTPW)) * (kRowsPerItem * 8) +
+                          rr * 8 + col];
+          sm.pv[e] = sum;
+        }
+        named_sync(bar_cons, kConsumers);
+        bool finisher = true;
+        if (G.nks > 1) {
+          float* part = wv.parts + static_cast<int64_t>(item * G.nks + slice) * (kRowsPerItem * R);
+          for (int e = tid; e < E; e += kConsumers) part[e] = sm.pv[e];
+          named_sync(bar_cons, kConsumers);
+          // One cumulative fence after the barrier orders every consumer's
+          // partial stores before the count.
+          if (tid == 0) {
+            __threadfence();
+            *sm.flag = atomicAdd(&wv.s_cnt[item], 1) == G.nks - 1;
+            if (*sm.flag) __threadfence();  // acquire side: the other slices' partials
+          }
+          named_sync(bar_cons, kConsumers);
+          finisher = *sm.flag != 0;
+          if (finisher) {
+            const float* p0 = wv.parts + static_cast<int64_t>(item * G.nks) * (kRowsPerItem * R);
+            for (int e = tid; e < E; e += kConsumers) {
+              float sum = 0.f;
+              for (int s = 0; s < G.nks; ++s) sum += __ldcg(p0 + s * (kRowsPerItem * R) + e);
+              sm.pv[e] = sum;
+            }
+          }
+        }
+        if (finisher) {
+          if (MODE == kModeShrink) {
+            for (int e = tid; e < E; e += kConsumers) {
+              const int rr = e / R, rk = e - rr * R;
+              args.v_out[static_cast<int64_t>(rows[rr]) * R + rk] = sm.pv[e];
+            }
+          } else {
+            float* vfin = wv.vfinal + static_cast<int64_t>(pos) * R;
+            for (int e = tid; e < E; e += kConsumers) vfin[e] = sm.pv[e];
+          }
+          named_sync(bar_cons, kConsumers);
+          if (tid == 0) {
+            if (G.nks > 1) wv.s_cnt[item] = 0;  // every slice has counted: ready for the next launch
+            __threadfence();
+            if (MODE != kModeShrink) st_release(&wv.ready[item], epoch);
+          }
+        }
+        named_sync(bar_cons, kConsumers);
+      }
+
+      if (kDoExpand && kind == kUnitExpand) {
+        float* vfb = sm.vf;
+        if (MODE == kModeExpand) {
+          const int s = static_cast<int>(g % kSlots);
+          mbar_wait(&sm.full[s], (g / kSlots) & 1, args.err);
+          const float* vs = reinterpret_cast<const float*>(sm.ring + s * kSlotBytes);
+          for (int e = tid; e < E; e += kConsumers) vfb[e] = vs[e];
+          __syncwarp();
+          if (lane == 0) mbar_arrive_relaxed(&sm.empty[s]);
+          ++g;
+        } else {
+          if (tid == 0) wait_word(&wv.ready[item], epoch, args.err);
+          named_sync(bar_cons, kConsumers);
+          const float* vfin = wv.vfinal + static_cast<int64_t>(pos) * R;
+          for (int e = tid; e < E; e += kConsumers) vfb[e] = __ldcg(vfin + e);
+        }
+        named_sync(bar_cons, kConsumers);
+        // Power-of-two scale that keeps the 16-bit v halves finite (f16 only).
+        float scale_down = 1.f, scale_up = 1.f;
+        if (std::is_same<DT, __half>::value) {
+          float m = 0.f;
+          for (int e = tid; e < E; e += kConsumers) m = fmaxf(m, fabsf(vfb[e]));
+#pragma unroll
+          for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+          if (lane == 0) sm.red[warp] = m;
+          named_sync(bar_cons, kConsumers);
+          m = sm.red[0];
+#pragma unroll
+          for (int w = 1; w < kConsumerWarps; ++w) m = fmaxf(m, sm.red[w]);
+          const int ex = static_cast<int>((__float_as_uint(m) >> 23) & 0xff) - 127;
+          const int e2 = ex > 14 ? ex - 14 : 0;
+          if (e2 > 0) {
+            scale_down = __uint_as_float(static_cast<uint32_t>(127 - e2) << 23);
+            scale_up = __uint_as_float(static_cast<uint32_t>(127 + (e2 < 127 ? e2 : 127)) << 23);
+          }
+        }
+        const int nlo = slice * G.es_st * stage_rows;
+        const int nhi = min(args.N, nlo + G.es_st * stage_rows);
+        if constexpr (kTcE) {
+          // MMA operands: rows of v_hi and v_lo (2R bytes each, swizzled like
+          // the TMA-written B tile); rows >= c are zero.
+          const uint32_t vop = smem_u32(sm.vop);
+          for (int e = tid; e < kRowsPerItem * R / 2; e += kConsumers) {
+            const int t = e / (R / 2), k = (e - t * (R / 2)) * 2;
+            float a = 0.f, b = 0.f;
+            if (t < c) {
+              a = vfb[t * R + k] * scale_down;
+              b = vfb[t * R + k + 1] * scale_down;
+            }
+            const float ha = Mma<DT>::round_trip(a), hb = Mma<DT>::round_trip(b);
+            const uint32_t off = swz(static_cast<uint32_t>(t * 2 * R + k * 2), C::kBSwz);
+            sts32(vop + off, Mma<DT>::pack(ha, hb));
+            sts32(vop + kRowsPerItem * 2 * R + off, Mma<DT>::pack(a - ha, b - hb));
+          }
+          tc::fence_proxy_async();
+          named_sync(bar_cons, kConsumers);
+          if (tid == 0) mbar_arrive(sm.vready);
+          // tcgen05.ld lets a warp reach the TMEM lanes of its physical warp
+          // id mod 4; lane = output column within the 128-row box.
+          const int quarter = (static_cast<int>(threadIdx.x) >> 5) & 3;
+          const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
+          for (int n0 = nlo; n0 < nhi; n0 += stage_rows, ++g) {
+            const int s = static_cast<int>(g % kSlots);
+            mbar_wait(&sm.full[s], (g / kSlots) & 1, args.err);
+            mbar_wait(&sm.mma_done[s], (g / kSlots) & 1, args.err);
+            __syncwarp();
+            tc::fence_after_sync();
+            const int rows_here = min(stage_rows, nhi - n0);
+            const int nbt = (rows_here + 127) / 128;
+            const uint32_t ytile = smem_u32(sm.ring + s * kSlotBytes + C::kYOff);
+            uint16_t out[2][kRowsPerItem];
+#pragma unroll
+            for (int b = 0; b < 2; ++b) {
+              if (b < nbt) {
+                uint32_t dr[16];
+                tc::ld16(tmem + lane_addr + static_cast<uint32_t>((s * 2 + b) * kRowsPerItem), dr);
+                tc::wait_ld();
+                const int n = b * 128 + quarter * 32 + lane;
+#pragma unroll
+                for (int t = 0; t < kRowsPerItem; ++t) {
+                  if (t < c) {
+                    const float yo = Cvt<DT>::to1(lds16(ytile + t * C::kYStride + n * 2));
+                    out[b][t] = Cvt<DT>::from1(yo + scale_up * __uint_as_float(dr[t]));
+                  }
+                }
+              }
+            }
+            tc::fence_before_sync();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_relaxed(&sm.empty[s]);
+#pragma unroll
+            for (int b = 0; b < 2; ++b) {
+              const int n = n0 + b * 128 + quarter * 32 + lane;
+              if (b < nbt && n < nhi) {
+#pragma unroll
+                for (int t = 0; t < kRowsPerItem; ++t)
+                  if (t < c) y[static_cast<int64_t>(rows[t]) * args.ldy + n] = out[b][t];
+              }
+            }
+          }
+        } else {
+          uint32_t vhi[C::kKSteps][4], vlo[C::kKSteps][4];
+          v_fragments<DT, R>(vfb, scale_down, lane, vhi, vlo);
+          for (int n0 = nlo; n0 < nhi; n0 += stage_rows, ++g) {
+            const int s = static_cast<int>(g % kSlots);
+            mbar_wait(&sm.full[s], (g / kSlots) & 1, args.err);
+            const int rows_here = min(stage_rows, nhi - n0);
+            expand_stage<DT, R>(sm.ring + s * kSlotBytes, vhi, vlo, rows_here, args.n_box, n0, c, rows, y,
+                                args.ldy, scale_up, warp, lane, &sm.empty[s]);
+          }
+        }
+        named_sync(bar_cons, kConsumers);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive_relaxed(&sm.uempty[iq]);
+    }
+  }
+  // The last CTA to finish resets the claim counter and bumps the epoch for
+  // the next launch on this workspace.
+  tc::fence_before_sync();
+  __syncthreads();
+  if (kTcE && grp == 0 && warp == kMmaWarp) {
+    tc::fence_after_sync();
+    tc::tmem_dealloc(s_tmem, kTmemCols);
+  }
+  if (threadIdx.x == 0) {
+    __threadfence();
+    if (atomicAdd(&wv.sync[kSyncDone], 1) == static_cast<int>(gridDim.x) - 1) {
+      __threadfence();
+      wv.sync[kSyncQueue] = 0;
+      wv.sync[kSyncDone] = 0;
+      wv.sync[kSyncEpoch] = epoch + 1 > 0 ? epoch + 1 : 1;
+      __threadfence();
+    }
+  }
+}
+
+// ------------------------------------------------------------------ host --
+
+template <typename DT, int R, int MODE>
+static cudaError_t split_launch(const CUtensorMap& tmA, const CUtensorMap& tmB, const BgmvArgs& a, int max_ctas,
+                                cudaStream_t stream) {
+  auto kern = bgmv_split_kernel<DT, R, MODE>;
+  constexpr int kMaxDev = 64;
+  static int ctas[kMaxDev] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kMaxDev) return cudaErrorInvalidDevice;
+  if (ctas[dev] == 0) {
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSplitSmemBytes);
+    if (e != cudaSuccess) return e;
+    int per_sm = 0, sms = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kSplitThreads, kSplitSmemBytes);
+    if (e != cudaSuccess) return e;
+    e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return e;
+    ctas[dev] = (per_sm > 0 ? per_sm : 1) * sms;
+  }
+  int grid = ctas[dev] < max_ctas ? ctas[dev] : max_ctas;
+  if (grid < 1) grid = 1;
+  kern<<<grid, kSplitThreads, kSplitSmemBytes, stream>>>(tmA, tmB, a);
+  return cudaGetLastError();
+}
+
+template <typename DT, int MODE>
+static cudaError_t split_rank(int R, const CUtensorMap& tmA, const CUtensorMap& tmB, const BgmvArgs& a, int max_ctas,
+                              cudaStream_t st) {
+  switch (R) {
+    case 8: return split_launch<DT, 8, MODE>(tmA, tmB, a, max_ctas, st);
+    case 16: return split_launch<DT, 16, MODE>(tmA, tmB, a, max_ctas, st);
+    case 32: return split_launch<DT, 32, MODE>(tmA, tmB, a, max_ctas, st);
+    case 64: return split_launch<DT, 64, MODE>(tmA, tmB, a, max_ctas, st);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+cudaError_t launch_bgmv_split(int mode, int dtype, int R, const CUtensorMap& tmA, const CUtensorMap& tmB,
+                              const BgmvArgs& a, int max_ctas, cudaStream_t st) {
+  const bool bf = dtype == PERSONA_DTYPE_BF16;
+  switch (mode) {
+    case kModeShrink:
+      return bf ? split_rank<__nv_bfloat16, kModeShrink>(R, tmA, tmB, a, max_ctas, st)
+                : split_rank<__half, kModeShrink>(R, tmA, tmB, a, max_ctas, st);
+    case kModeExpand:
+      return bf ? split_rank<__nv_bfloat16, kModeExpand>(R, tmA, tmB, a, max_ctas, st)
+                : split_rank<__half, kModeExpand>(R, tmA, tmB, a, max_ctas, st);
+    default:
+      return bf ? split_rank<__nv_bfloat16, kModeFused>(R, tmA, tmB, a, max_ctas, st)
+                : split_rank<__half, kModeFused>(R, tmA, tmB, a, max_ctas, st);
+  }
+}
+
+}  // namespace persona

@@ -128,7 +128,7 @@ int check_common(int64_t T, int64_t S, int dtype, const void* workspace, size_t 
   if (T > kI32Max / 64) return PERSONA_ERR_SHAPE;
   if (dtype != PERSONA_DTYPE_F16 && dtype != PERSONA_DTYPE_BF16) return PERSONA_ERR_DTYPE;
   if (T > 0 && slots == nullptr) return PERSONA_ERR_INVALID_ARG;
-  if (T > 0 && (workspace == nullptr || ws_bytes < plan_bytes(T))) return PERSONA_ERR_WORKSPACE;
+  if (T > 0 && (workspace == nullptr || ws_bytes < bgmv_ws_bytes(T))) return PERSONA_ERR_WORKSPACE;
   if (T > 0 && !aligned16(workspace)) return PERSONA_ERR_ALIGNMENT;
   return PERSONA_OK;
 }
@@ -155,6 +155,59 @@ int check_b(const void* b_pool, int64_t b_slot_stride, const void* y, int64_t ld
   if (!aligned16(b_pool) || !aligned16(y)) return PERSONA_ERR_ALIGNMENT;  // :230-233
   if (ldy % 8 || b_slot_stride % 8) return PERSONA_ERR_ALIGNMENT;
   return PERSONA_OK;
+}
+
+// The split kernel runs by default; PERSONA_BGMV_KERNEL=cluster selects the
+// clustered kernel (one item per 2-CTA cluster) instead.
+bool use_cluster_kernel() {
+  static const bool v = [] {
+    const char* e = std::getenv("PERSONA_BGMV_KERNEL");
+    return e != nullptr && std::strcmp(e, "cluster") == 0;
+  }();
+  return v;
+}
+
+// Fills the slice fields of `a` (n_box before the B map is encoded) and
+// returns the cluster size, 0 for the split kernel.
+int kernel_geometry(int mode, int64_t T, int64_t K, int64_t N, int64_t R, BgmvArgs* a) {
+  if (use_cluster_kernel()) {
+    const int cs = cluster_size_for(T);
+    a->k_per_cta = 0;
+    a->n_per_cta = 0;
+    a->n_box = 8;
+    if (mode & kModeShrink) split_k(K, cs, &a->k_per_cta);
+    if (mode & kModeExpand) split_n(N, cs, static_cast<int>(R), &a->n_per_cta, &a->n_box);
+    return cs;
+  }
+  a->k_per_cta = 0;
+  a->n_per_cta = 0;
+  a->n_box = 8;
+  if (mode & kModeExpand) {
+    // Ranks 16..64 expand on tcgen05: B boxes are the MMA's 128-row M side.
+    const int64_t nb = R >= 16 ? 128 : bgmv_stage_rows(static_cast<int>(R));
+    const int64_t n8 = (N + 7) / 8 * 8;
+    a->n_box = static_cast<int>(n8 < nb ? n8 : nb);
+  }
+  return 0;
+}
+
+// Work units per CTA of the split kernels (PERSONA_UNITS_PER_CTA overrides).
+int units_per_cta() {
+  static const int v = [] {
+    const char* e = std::getenv("PERSONA_UNITS_PER_CTA");
+    const int n = e != nullptr ? std::atoi(e) : 0;
+    return n > 0 && n <= 64 ? n : 0;
+  }();
+  return v;
+}
+
+int run_bgmv(int mode, int dtype, int64_t R, const CUtensorMap& tmA, const CUtensorMap& tmB, BgmvArgs a,
+             int cs, int64_t T, cudaStream_t stream) {
+  a.units_per_cta = units_per_cta();
+  const cudaError_t e =
+      cs > 0 ? launch_bgmv_cluster(mode, dtype, static_cast<int>(R), tmA, tmB, a, cs, static_cast<int>(T), stream)
+             : launch_bgmv_split(mode, dtype, static_cast<int>(R), tmA, tmB, a, 1 << 20, stream);
+  return e == cudaSuccess ? PERSONA_OK : PERSONA_ERR_CUDA;
 }
 
 int plan_if_needed(const int32_t* slots, int64_t T, int64_t S, void* ws, int flags,
@@ -190,7 +243,7 @@ const char* persona_status_string(int status) {
 
 int persona_abi_version(void) { return PERSONA_ABI_VERSION; }
 
-size_t persona_bgmv_workspace_size(int64_t T) { return T < 0 ? 0 : plan_bytes(T); }
+size_t persona_bgmv_workspace_size(int64_t T) { return T < 0 ? 0 : bgmv_ws_bytes(T); }
 
 int persona_bgmv_plan(const int32_t* slots, int64_t T, int64_t S, void* workspace,
                       size_t workspace_bytes, int32_t* dev_err, cudaStream_t stream) {
@@ -233,17 +286,12 @@ int persona_bgmv_shrink(const void* x, int64_t ldx, const void* a_pool, int64_t 
   std::memset(&tmB, 0, sizeof(tmB));
   if ((st = encode_a_map(&tmA, a_pool, dtype, K, R, S, a_row_stride, a_slot_stride)) != PERSONA_OK) return st;
   if ((st = plan_if_needed(slots, T, S, workspace, flags, dev_err, stream)) != PERSONA_OK) return st;
-  const int cs = cluster_size_for(T);
   BgmvArgs a = {};
+  const int cs = kernel_geometry(kModeShrink, T, K, 0, R, &a);
   a.x = x; a.ldx = ldx; a.v_out = v; a.slots = slots;
   a.plan = static_cast<const int32_t*>(workspace); a.err = dev_err;
   a.T = static_cast<int>(T); a.K = static_cast<int>(K); a.N = 0; a.S = static_cast<int>(S);
-  split_k(K, cs, &a.k_per_cta);
-  a.n_per_cta = 0; a.n_box = 8;
-  return launch_bgmv_cluster(kModeShrink, dtype, static_cast<int>(R), tmA, tmB, a, cs,
-                             static_cast<int>(T), stream) == cudaSuccess
-             ? PERSONA_OK
-             : PERSONA_ERR_CUDA;
+  return run_bgmv(kModeShrink, dtype, R, tmA, tmB, a, cs, T, stream);
 }
 
 int persona_bgmv_expand(const float* v, const void* b_pool, int64_t b_slot_stride,
@@ -259,9 +307,8 @@ int persona_bgmv_expand(const float* v, const void* b_pool, int64_t b_slot_strid
   if ((st = check_b(b_pool, b_slot_stride, y, ldy, N, R)) != PERSONA_OK) return st;
   if (v == nullptr) return PERSONA_ERR_INVALID_ARG;
   if (!aligned16(v)) return PERSONA_ERR_ALIGNMENT;
-  const int cs = cluster_size_for(T);
   BgmvArgs a = {};
-  split_n(N, cs, static_cast<int>(R), &a.n_per_cta, &a.n_box);
+  const int cs = kernel_geometry(kModeExpand, T, 0, N, R, &a);
   CUtensorMap tmA, tmB;
   std::memset(&tmA, 0, sizeof(tmA));
   if ((st = encode_b_map(&tmB, b_pool, dtype, N, R, S, b_slot_stride, a.n_box)) != PERSONA_OK) return st;
@@ -269,11 +316,7 @@ int persona_bgmv_expand(const float* v, const void* b_pool, int64_t b_slot_strid
   a.v_in = v; a.y = y; a.ldy = ldy; a.slots = slots;
   a.plan = static_cast<const int32_t*>(workspace); a.err = dev_err;
   a.T = static_cast<int>(T); a.K = 0; a.N = static_cast<int>(N); a.S = static_cast<int>(S);
-  a.k_per_cta = 0;
-  return launch_bgmv_cluster(kModeExpand, dtype, static_cast<int>(R), tmA, tmB, a, cs,
-                             static_cast<int>(T), stream) == cudaSuccess
-             ? PERSONA_OK
-             : PERSONA_ERR_CUDA;
+  return run_bgmv(kModeExpand, dtype, R, tmA, tmB, a, cs, T, stream);
 }
 
 int persona_bgmv_fused(const void* x, int64_t ldx, const void* a_pool, int64_t a_slot_stride,
@@ -290,10 +333,8 @@ int persona_bgmv_fused(const void* x, int64_t ldx, const void* a_pool, int64_t a
   if ((st = check_a(x, ldx, a_pool, a_slot_stride, a_row_stride, K, R, S)) != PERSONA_OK) return st;
   if ((st = check_b(b_pool, b_slot_stride, y, ldy, N, R)) != PERSONA_OK) return st;
   if (K < 64) return PERSONA_ERR_SHAPE;
-  const int cs = cluster_size_for(T);
   BgmvArgs a = {};
-  split_k(K, cs, &a.k_per_cta);
-  split_n(N, cs, static_cast<int>(R), &a.n_per_cta, &a.n_box);
+  const int cs = kernel_geometry(kModeFused, T, K, N, R, &a);
   CUtensorMap tmA, tmB;
   if ((st = encode_a_map(&tmA, a_pool, dtype, K, R, S, a_row_stride, a_slot_stride)) != PERSONA_OK) return st;
   if ((st = encode_b_map(&tmB, b_pool, dtype, N, R, S, b_slot_stride, a.n_box)) != PERSONA_OK) return st;
@@ -302,10 +343,7 @@ int persona_bgmv_fused(const void* x, int64_t ldx, const void* a_pool, int64_t a
   a.plan = static_cast<const int32_t*>(workspace); a.err = dev_err;
   a.T = static_cast<int>(T); a.K = static_cast<int>(K); a.N = static_cast<int>(N);
   a.S = static_cast<int>(S);
-  return launch_bgmv_cluster(kModeFused, dtype, static_cast<int>(R), tmA, tmB, a, cs,
-                             static_cast<int>(T), stream) == cudaSuccess
-             ? PERSONA_OK
-             : PERSONA_ERR_CUDA;
+  return run_bgmv(kModeFused, dtype, R, tmA, tmB, a, cs, T, stream);
 }
 
 int persona_gemv_fp16(const void* x, const void* W, void* y, int64_t K, int64_t N,
@@ -322,7 +360,7 @@ int persona_gemv_fp16(const void* x, const void* W, void* y, int64_t K, int64_t 
 
 // ----------------------------------------------------------------- SGMV ---
 namespace {
-size_t sgmv_ws_bytes(int64_t T) { return persona::plan_bytes(T) + 4 * static_cast<size_t>(persona::plan_tpad(T)); }
+size_t sgmv_ws_bytes(int64_t T) { return persona::bgmv_ws_bytes(T) + 4 * static_cast<size_t>(persona::plan_tpad(T)); }
 
 int sgmv_prepare(const int32_t* seg_indptr, const int32_t* seg_slots, int64_t nseg, int64_t T, int64_t S,
                  void* workspace, size_t workspace_bytes, int32_t* dev_err, cudaStream_t stream,
@@ -332,7 +370,7 @@ int sgmv_prepare(const int32_t* seg_indptr, const int32_t* seg_slots, int64_t ns
   if (seg_indptr == nullptr || (nseg > 0 && seg_slots == nullptr)) return PERSONA_ERR_INVALID_ARG;
   if (workspace == nullptr || workspace_bytes < sgmv_ws_bytes(T)) return PERSONA_ERR_WORKSPACE;
   if ((reinterpret_cast<uintptr_t>(workspace) & 15) != 0) return PERSONA_ERR_ALIGNMENT;
-  *row_slots = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(workspace) + persona::plan_bytes(T));
+  *row_slots = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(workspace) + persona::bgmv_ws_bytes(T));
   return persona::launch_sgmv_plan(seg_indptr, seg_slots, static_cast<int>(nseg), static_cast<int>(T),
                                    static_cast<int>(S), persona::kRowsPerItem, static_cast<int32_t*>(workspace),
                                    *row_slots, dev_err, stream) == cudaSuccess
@@ -384,7 +422,7 @@ int sgmv_tc_run(int mode, const void* x, int64_t ldx, const void* a_pool, int64_
   }
   if (mode == kModeShrink && (v_out == nullptr || !aligned16(v_out))) return PERSONA_ERR_ALIGNMENT;
   if (mode == kModeExpand && (v_in == nullptr || !aligned16(v_in))) return PERSONA_ERR_ALIGNMENT;
-  int32_t* row_slots = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(workspace) + plan_bytes(T));
+  int32_t* row_slots = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(workspace) + bgmv_ws_bytes(T));
   if (launch_sgmv_plan(seg_indptr, seg_slots, static_cast<int>(nseg), static_cast<int>(T), static_cast<int>(S),
                        128, static_cast<int32_t*>(workspace), row_slots, dev_err, stream) != cudaSuccess)
     return PERSONA_ERR_CUDA;
@@ -429,7 +467,7 @@ int persona_sgmv_shrink(const void* x, int64_t ldx, const void* a_pool, int64_t 
                         &row_slots);
   if (st != PERSONA_OK || T == 0) return st;
   return persona_bgmv_shrink(x, ldx, a_pool, a_slot_stride, a_row_stride, row_slots, v, T, K, R, S, dtype,
-                             workspace, persona::plan_bytes(T), PERSONA_REUSE_PLAN, dev_err, stream);
+                             workspace, persona::bgmv_ws_bytes(T), PERSONA_REUSE_PLAN, dev_err, stream);
 }
 
 int persona_sgmv_expand(const float* v, const void* b_pool, int64_t b_slot_stride, const int32_t* seg_indptr,
@@ -447,7 +485,7 @@ int persona_sgmv_expand(const float* v, const void* b_pool, int64_t b_slot_strid
                         &row_slots);
   if (st != PERSONA_OK || T == 0) return st;
   return persona_bgmv_expand(v, b_pool, b_slot_stride, row_slots, y, ldy, T, N, R, S, dtype, workspace,
-                             persona::plan_bytes(T), PERSONA_REUSE_PLAN, dev_err, stream);
+                             persona::bgmv_ws_bytes(T), PERSONA_REUSE_PLAN, dev_err, stream);
 }
 
 int persona_sgmv_fused(const void* x, int64_t ldx, const void* a_pool, int64_t a_slot_stride, int64_t a_row_stride,
@@ -466,7 +504,7 @@ int persona_sgmv_fused(const void* x, int64_t ldx, const void* a_pool, int64_t a
                         &row_slots);
   if (st != PERSONA_OK || T == 0) return st;
   return persona_bgmv_fused(x, ldx, a_pool, a_slot_stride, a_row_stride, b_pool, b_slot_stride, row_slots, y, ldy,
-                            T, K, N, R, S, dtype, workspace, persona::plan_bytes(T), PERSONA_REUSE_PLAN, dev_err,
+                            T, K, N, R, S, dtype, workspace, persona::bgmv_ws_bytes(T), PERSONA_REUSE_PLAN, dev_err,
                             stream);
 }
 

@@ -8,20 +8,21 @@
 // calls cudaMalloc / cudaFree or any allocating routine.
 //
 // The plan kernel rewrites every field the fused kernel reads (header, row
-// permutation, items) on each call, so no part of the array has to start at
-// zero.  All calls on one device share the array: calls whose device work
+// permutation, items) and resets the kernel's shared counters on each call,
+// so no part of the array has to start at zero.  All calls on one device share the array: calls whose device work
 // overlaps in time (different streams, or threads without ordering) race on
 // it and must be serialised, e.g. by issuing them on one stream.
 #include <mutex>
 
 #include "persona_bgmv.h"
+#include "plan_layout.h"
 
 namespace persona {
 namespace {
 
 constexpr int64_t kNoAllocMaxRows = PERSONA_NOALLOC_MAX_ROWS;
-constexpr size_t kNoAllocPlanBytes = (32 + 20 * ((kNoAllocMaxRows + 3) / 4 * 4));
-static_assert(kNoAllocPlanBytes % 16 == 0, "plan scratch size");
+constexpr size_t kNoAllocPlanBytes = bgmv_ws_bytes(kNoAllocMaxRows);
+static_assert(kNoAllocPlanBytes % 16 == 0, "workspace size");
 
 // Host-side name is a stand-in for the per-device copies; only its device
 // address (cudaGetSymbolAddress) is ever used.

@@ -49,37 +49,45 @@ def test_reference_schemas_registered(built):
 
 def test_workspace_size_matches_layout(built):
     lib = capi_lib.load()
+    def a256(n):
+        return (n + 255) // 256 * 256
+
     for T in (0, 1, 8, 512, 16384):
         tp = (T + 3) // 4 * 4
-        assert lib.persona_bgmv_workspace_size(T) == 32 + 4 * tp + 16 * tp
+        plan = 32 + 4 * tp + 16 * tp              # header, perm, items
+        sync = a256(plan)                          # counters, per-item state
+        vfinal = a256(sync + 4 * (16 + 2 * tp))    # v per plan position, 64 floats
+        parts = a256(vfinal + tp * 64 * 4)         # 1024 partial-v slots of 16 x 64 floats
+        assert lib.persona_bgmv_workspace_size(T) == parts + 1024 * 16 * 64 * 4
+        assert lib.persona_sgmv_workspace_size(T) == parts + 1024 * 16 * 64 * 4 + 4 * tp
 
 
 def test_host_validation_codes(built):
     lib = capi_lib.load()
-    ws = ctypes.create_string_buffer(4096 + 16)
-    wsp = (ctypes.addressof(ws) + 15) & ~15
     fake = 1 << 20  # 16-byte aligned, never dereferenced: validation fails first
+    wsp = fake
+    big = lib.persona_bgmv_workspace_size(512)  # enough for every call below
     # unsupported dtype
     assert lib.persona_bgmv_fused(fake, 64, fake, 64 * 16, 64, fake, 64 * 16, fake, fake, 64, 8, 64,
-                                  64, 16, 4, 7, wsp, 4096, 0, None, None) == 3
+                                  64, 16, 4, 7, wsp, big, 0, None, None) == 3
     # rank 12 is not a fused/expand rank
     assert lib.persona_bgmv_fused(fake, 64, fake, 64 * 12, 64, fake, 64 * 12, fake, fake, 64, 8, 64,
-                                  64, 12, 4, 0, wsp, 4096, 0, None, None) == 5
+                                  64, 12, 4, 0, wsp, big, 0, None, None) == 5
     # K not a multiple of 8
     assert lib.persona_bgmv_shrink(fake, 68, fake, 68 * 16, 68, fake, fake, 8, 68, 16, 4, 0,
-                                   wsp, 4096, 0, None, None) == 2
+                                   wsp, big, 0, None, None) == 2
     # misaligned x
     assert lib.persona_bgmv_shrink(fake + 8, 64, fake, 64 * 16, 64, fake, fake, 8, 64, 16, 4, 0,
-                                   wsp, 4096, 0, None, None) == 4
+                                   wsp, big, 0, None, None) == 4
     # workspace too small
     assert lib.persona_bgmv_expand(fake, fake, 64 * 16, fake, fake, 64, 512, 64, 16, 4, 0, wsp, 64,
                                    0, None, None) == 6
     # unknown flag
-    assert lib.persona_bgmv_expand(fake, fake, 64 * 16, fake, fake, 64, 8, 64, 16, 4, 0, wsp, 4096,
+    assert lib.persona_bgmv_expand(fake, fake, 64 * 16, fake, fake, 64, 8, 64, 16, 4, 0, wsp, big,
                                    8, None, None) == 1
     # T == 0 is a no-op
     assert lib.persona_bgmv_fused(fake, 64, fake, 64 * 16, 64, fake, 64 * 16, fake, fake, 64, 0, 64,
-                                  64, 16, 4, 0, wsp, 4096, 0, None, None) == 0
+                                  64, 16, 4, 0, wsp, big, 0, None, None) == 0
     assert b"R must be" in lib.persona_status_string(5)
 
 
