@@ -6,7 +6,8 @@ projections of one decoder layer (q/o 4096->4096, k/v 4096->1024, gate/up
 4096->14336, down 14336->4096), fp16, rank 64, a pool of 256 adapters
 resident in HBM, 512 rows per GPU whose slots are drawn from a truncated
 Zipf(1.1) with 5 % of rows without an adapter.  One step = the device-side
-row-grouping plan plus one fused shrink->expand launch per projection.
+row-grouping plan plus one fused shrink->expand launch that carries all seven
+projections.
 
 N GPUs (torchrun, one process per GPU): the global batch is 512*N rows,
 partitioned across ranks by adapter affinity (persona.sharding) with the pool
@@ -212,7 +213,7 @@ def workload_config(world: int) -> dict:
         "pool_slots": POOL_SLOTS, "projections": [n for n, _, _ in projections()],
         "parallelism": f"row-sharded x{world} (adapter affinity), pool replicated",
         "l2": "inputs larger than L2: ~1.4 GB of adapter/x/y traffic per step vs 126 MB L2",
-        "launches_per_step": 1 + len(projections()),
+        "launches_per_step": 2,
     }
 
 
@@ -299,14 +300,19 @@ def run_ours(args):
     step_bytes = sum(p["bytes"] for p in projs)
     stream = torch.cuda.current_stream()
 
+    xs = [p["x"] for p in projs]
+    a_s = [p["a"] for p in projs]
+    b_s = [p["b"] for p in projs]
+    ys = [p["y"] for p in projs]
+
     def step(ev=None):
+        # one plan for the batch's slots + one launch for all the projections
         plan = ops.bgmv_plan(slots_d, POOL_SLOTS)
-        for i, p in enumerate(projs):
-            if ev is not None:
-                ev[i][0].record(stream)
-            ops.bgmv_fused(p["x"], p["a"], p["b"], slots_d, p["y"], plan=plan)
-            if ev is not None:
-                ev[i][1].record(stream)
+        if ev is not None:
+            ev[0].record(stream)
+        ops.bgmv_fused_multi(xs, a_s, b_s, slots_d, ys, plan=plan)
+        if ev is not None:
+            ev[1].record(stream)
 
     def barrier():
         if world > 1:
@@ -338,8 +344,7 @@ def run_ours(args):
 
     # ---- timed region (device time, CUDA events; per-launch events for the roofline)
     K_steps = max(1, args.steps)
-    evs = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-            for _ in projs] for _ in range(K_steps)]
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K_steps)]
     barrier()
     torch.cuda.synchronize()
     t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -352,7 +357,7 @@ def run_ours(args):
     host_t1 = time.monotonic()
     barrier()
     ms_local = t_start.elapsed_time(t_end) / K_steps
-    fused_ms = sum(evs[s][i][0].elapsed_time(evs[s][i][1]) for s in range(K_steps) for i in range(len(projs)))
+    fused_ms = sum(evs[s][0].elapsed_time(evs[s][1]) for s in range(K_steps))
     fused_ms_per_step = fused_ms / K_steps
     ops.check_errors(dev)
 
@@ -368,11 +373,11 @@ def run_ours(args):
     def e2e_step():
         sd = slots_h.to(dev, non_blocking=True)
         plan = ops.bgmv_plan(sd, POOL_SLOTS)
-        for p, h in zip(projs, host):
-            xd = h["x"].to(dev, non_blocking=True)
-            yd = h["y_in"].to(dev, non_blocking=True)
-            ops.bgmv_fused(xd, p["a"], p["b"], sd, yd, plan=plan)
-            h["y_out"].copy_(yd, non_blocking=True)
+        xd = [h["x"].to(dev, non_blocking=True) for h in host]
+        yd = [h["y_in"].to(dev, non_blocking=True) for h in host]
+        ops.bgmv_fused_multi(xd, a_s, b_s, sd, yd, plan=plan)
+        for h, y in zip(host, yd):
+            h["y_out"].copy_(y, non_blocking=True)
 
     for _ in range(max(3, args.warmup)):
         e2e_step()
@@ -420,7 +425,7 @@ def run_ours(args):
             "rows_per_s": total_rows / (ms * 1e-3),
             "roofline": {
                 "bound": "hbm",
-                "kernel": "bgmv_cluster_kernel<half,64,fused>",
+                "kernel": "bgmv_split_kernel<half,64,fused> (7 projections per launch)",
                 "achieved": achieved,
                 "peak": peak,
                 "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else
@@ -428,14 +433,14 @@ def run_ours(args):
                 "unit": "GB/s",
                 "frac": achieved / peak,
                 "traffic": traffic,
-                "algorithmic_bytes_per_launch": step_bytes / len(projs),
-                "launch_us_avg": fused_ms_per_step * 1e3 / len(projs),
+                "algorithmic_bytes_per_launch": step_bytes,
+                "launch_us_avg": fused_ms_per_step * 1e3,
             },
             "e2e": {"value": total_bytes / (e2e_ms * 1e-3) / 1e9, "unit": UNIT,
                     "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
                     "ms_per_step": e2e_ms,
-                    "path": "persona.ops.bgmv_plan + bgmv_fused, pinned host x/y/slots copied in, y out"},
-            "gpu_launches": K_steps * (1 + len(projs)),
+                    "path": "persona.ops.bgmv_plan + bgmv_fused_multi, pinned host x/y/slots copied in, y out"},
+            "gpu_launches": K_steps * 2,
             "clocks": clk,
             "fused_ms_per_step_max_rank": fused_ms_max,
         }
@@ -581,6 +586,13 @@ def run_extra(args):
     def fused_all():
         for st in sets:
             plan = ops.bgmv_plan(st["slots"], S)
+            ops.bgmv_fused_multi([p["x"] for p in st["projs"]], [p["a"] for p in st["projs"]],
+                                 [p["b"] for p in st["projs"]], st["slots"], [p["y"] for p in st["projs"]],
+                                 plan=plan)
+
+    def per_projection_all():
+        for st in sets:
+            plan = ops.bgmv_plan(st["slots"], S)
             for p in st["projs"]:
                 ops.bgmv_fused(p["x"], p["a"], p["b"], st["slots"], p["y"], plan=plan)
 
@@ -593,10 +605,12 @@ def run_extra(args):
 
     for _ in range(warm):
         fused_all()
+        per_projection_all()
         separate_all()
     ops.check_errors(dev)
     reps = max(1, steps // copies)
     eager_f = _timed(fused_all, reps, stream) / copies
+    eager_p = _timed(per_projection_all, reps, stream) / copies
     eager_s = _timed(separate_all, reps, stream) / copies
     g = torch.cuda.CUDAGraph()
     side = torch.cuda.Stream()
@@ -619,12 +633,12 @@ def run_extra(args):
         "config": {"workload": "7 Mistral-7B projections, 8 rows, rank 16, 8 adapters (one per row), fp16",
                    "l2": f"{copies} independent input sets rotated (~{copies * step_bytes / 1e6:.0f} MB > L2)"},
         "us_per_step": {"fused_graph": graph_f * 1e3, "fused_eager": eager_f * 1e3,
-                        "separate_eager": eager_s * 1e3},
+                        "fused_per_projection_eager": eager_p * 1e3, "separate_eager": eager_s * 1e3},
         "algorithmic_bytes_per_step": step_bytes,
         "GB/s": {"fused_graph": step_bytes / (graph_f * 1e-3) / 1e9,
                  "fused_eager": step_bytes / (eager_f * 1e-3) / 1e9},
         "hbm_frac_fused_graph": step_bytes / (graph_f * 1e-3) / 1e9 / peak,
-        "launches_per_step": 1 + len(sets[0]["projs"]),
+        "launches_per_step": 2,
     }
     g.reset()
     print(json.dumps(line), flush=True)

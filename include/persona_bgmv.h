@@ -75,7 +75,7 @@ int persona_bgmv_plan(const int32_t* slots, int64_t T, int64_t S, void* workspac
  * v[t, :] = A[slots[t]] @ x[t, :] in fp32; rows with slot -1 get zeros.
  * Replaces bgmv_shrink_cuda (csrc/bgmv_shrink.cu:81-122) behind
  * torch.ops.persona.bgmv_shrink (csrc/bindings.cpp:20).  R in {8,16,32,64}
- * runs the clustered kernel; any other R runs a row-by-row kernel.         */
+ * runs the split kernel over a plan; any other R runs a row-by-row kernel.  */
 int persona_bgmv_shrink(const void* x, int64_t ldx, const void* a_pool, int64_t a_slot_stride,
                         int64_t a_row_stride, const int32_t* slots, float* v, int64_t T,
                         int64_t K, int64_t R, int64_t S, int dtype, void* workspace,
@@ -94,9 +94,10 @@ int persona_bgmv_expand(const float* v, const void* b_pool, int64_t b_slot_strid
                         cudaStream_t stream);
 
 /* ---- fused BGMV shrink -> expand -----------------------------------------
- * y[t, :] = round(y[t, :] + B[s] @ (A[s] @ x[t, :])) with the rank-R
- * intermediate kept on chip (distributed shared memory of a thread-block
- * cluster).  The reference's fused kernel is a stub (docs/BENCHMARKS.md:238);
+ * y[t, :] = round(y[t, :] + B[s] @ (A[s] @ x[t, :])) in one launch; the
+ * rank-R intermediate never goes through HBM as a tensor (its K-slice
+ * partials meet in L2-resident workspace).  The reference's fused kernel is a
+ * stub (docs/BENCHMARKS.md:238);
  * its result equals bgmv_shrink followed by bgmv_expand
  * (persona/ops.py:59-68).  R in {8,16,32,64}.                              */
 int persona_bgmv_fused(const void* x, int64_t ldx, const void* a_pool, int64_t a_slot_stride,
@@ -105,6 +106,35 @@ int persona_bgmv_fused(const void* x, int64_t ldx, const void* a_pool, int64_t a
                        int64_t N, int64_t R, int64_t S, int dtype, void* workspace,
                        size_t workspace_bytes, int flags, int32_t* dev_err,
                        cudaStream_t stream);
+
+/* ---- fused BGMV over several projections in one launch ------------------
+ * No reference counterpart (the reference launches shrink and expand per
+ * projection; persona/lora_layer.py:55-57).  Up to PERSONA_MAX_PROBLEMS
+ * projections of one decoder layer (q/k/v/o/gate/up/down) that share the
+ * batch's slots, the rank R, the pool size S and the dtype run as one
+ * launch: each problem has its own x, pools (strides as for
+ * persona_bgmv_fused) and y, and the result of each equals
+ * persona_bgmv_fused on it.  The plan depends only on the slots, so
+ * PERSONA_REUSE_PLAN works with a plan built by persona_bgmv_plan on this
+ * workspace.  Workspace: persona_bgmv_multi_workspace_size(T, num_problems). */
+#define PERSONA_MAX_PROBLEMS 8
+typedef struct persona_bgmv_problem {
+  const void* x;
+  int64_t ldx;
+  const void* a_pool;
+  int64_t a_slot_stride;
+  int64_t a_row_stride;
+  const void* b_pool;
+  int64_t b_slot_stride;
+  void* y;
+  int64_t ldy;
+  int64_t K;
+  int64_t N;
+} persona_bgmv_problem;
+size_t persona_bgmv_multi_workspace_size(int64_t T, int num_problems);
+int persona_bgmv_fused_multi(const persona_bgmv_problem* problems, int num_problems, const int32_t* slots,
+                             int64_t T, int64_t R, int64_t S, int dtype, void* workspace, size_t workspace_bytes,
+                             int flags, int32_t* dev_err, cudaStream_t stream);
 
 /* ---- segmented (SGMV) ------------------------------------------------------
  * A prefill batch whose rows are grouped contiguously by adapter: segment i
@@ -119,7 +149,7 @@ int persona_bgmv_fused(const void* x, int64_t ldx, const void* a_pool, int64_t a
  * segment sets PERSONA_DEV_ERR_SEGMENT and is skipped.
  * Ranks 16 and 32 with K % 64 == 0 (shrink) and N % 128 == 0 (expand) run on
  * the tensor cores (tcgen05, accumulators in TMEM, 128-row tiles); other
- * shapes run the clustered BGMV kernels over the segments' rows.
+ * shapes run the split BGMV kernels over the segments' rows.
  * Workspace: persona_sgmv_workspace_size(T). */
 size_t persona_sgmv_workspace_size(int64_t T);
 int persona_sgmv_shrink(const void* x, int64_t ldx, const void* a_pool, int64_t a_slot_stride,

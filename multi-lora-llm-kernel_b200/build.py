@@ -33,8 +33,7 @@ CUDA_HOME = Path(os.environ.get("CUDA_HOME", "/usr/local/cuda"))
 NVCC = str(CUDA_HOME / "bin" / "nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
-CU_SOURCES = ["capi.cu", "bgmv_plan.cu", "bgmv_cluster.cu", "bgmv_split.cu", "sgmv_tcgen05.cu",
-              "simple_kernels.cu",
+CU_SOURCES = ["capi.cu", "bgmv_plan.cu", "bgmv_split.cu", "sgmv_tcgen05.cu", "simple_kernels.cu",
               "noalloc.cu"]
 LIB = OUT / "libpersona_bgmv.so"
 EXT = OUT / ("_C" + sysconfig.get_config_var("EXT_SUFFIX"))

@@ -1,5 +1,5 @@
-// Kernel arguments of the clustered BGMV kernel, shared by the host entry
-// points (capi.cu) and the kernel (bgmv_cluster.cu).
+// Kernel arguments of the BGMV kernels, shared by the host entry points
+// (capi.cu) and the kernels.
 #pragma once
 
 #include <stdint.h>
@@ -7,32 +7,15 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include "plan_layout.h"
+
 namespace persona {
 
 enum BgmvMode : int { kModeShrink = 1, kModeExpand = 2, kModeFused = 3 };
 
-struct BgmvArgs {
-  const void* x;       // [T, K] 16-bit, row stride ldx
-  int64_t ldx;
-  const float* v_in;   // expand: [T, R] fp32
-  float* v_out;        // shrink: [T, R] fp32
-  void* y;             // [T, N] 16-bit, row stride ldy
-  int64_t ldy;
-  const int32_t* slots;
-  const int32_t* plan;
-  int32_t* err;
-  int T, K, N, S;
-  int units_per_cta;  // split kernels: target work units per CTA (0 = default)
-  int k_per_cta;       // K slice of one cluster CTA, multiple of 64
-  int n_per_cta;       // N slice of one cluster CTA, multiple of n_box
-  int n_box;           // rows of one B tile, multiple of 8, <= 256
-};
 
 cudaError_t launch_bgmv_plan(const int32_t* slots, int T, int S, int rows_per_item, int32_t* plan,
                              int32_t* dev_err, cudaStream_t stream);
-cudaError_t launch_bgmv_cluster(int mode, int dtype, int R, const CUtensorMap& tmA,
-                                const CUtensorMap& tmB, const BgmvArgs& a, int cluster_size,
-                                int max_clusters, cudaStream_t st);
 cudaError_t launch_shrink_rowwise(int dtype, const void* x, int64_t ldx, const void* a_pool,
                                   int64_t a_slot_stride, int64_t a_row_stride,
                                   const int32_t* slots, float* v, int T, int K, int R, int S,
@@ -40,11 +23,34 @@ cudaError_t launch_shrink_rowwise(int dtype, const void* x, int64_t ldx, const v
 cudaError_t launch_sgmv_plan(const int32_t* indptr, const int32_t* seg_slots, int nseg, int T, int S,
                              int rows_per_item, int32_t* plan, int32_t* row_slots, int32_t* dev_err,
                              cudaStream_t stream);
-int bgmv_stage_rows(int R);
-// Split kernels (bgmv_split.cu): every item cut into K / N slices claimed by
-// all CTAs; workspace = bgmv_ws_bytes(T) (plan_layout.h).
-cudaError_t launch_bgmv_split(int mode, int dtype, int R, const CUtensorMap& tmA, const CUtensorMap& tmB,
-                              const BgmvArgs& a, int max_ctas, cudaStream_t st);
+int bgmv_stage_rows(int R);  // B rows one ring slot holds at rank R
+// Split kernels (bgmv_split.cu): every item of every problem cut into K / N
+// slices claimed by all CTAs; workspace = bgmv_ws_bytes(T, problems)
+// (plan_layout.h).  Up to kMaxProblems projections that share the batch's
+// slots, rank and pool size run in one launch.
+struct SplitProblem {
+  const void* x;  // [T, K] 16-bit, row stride ldx
+  void* y;        // [T, N] 16-bit, row stride ldy
+  int64_t ldx, ldy;
+  int K, N;
+  int n_box;  // rows of one B tile (128 for ranks >= 16)
+  int pad;
+};
+struct SplitArgs {
+  SplitProblem prob[kMaxProblems];
+  const float* v_in;  // expand only (one problem): [T, R] fp32
+  float* v_out;       // shrink only (one problem): [T, R] fp32
+  const int32_t* slots;
+  int32_t* ws;  // plan + shared state
+  int32_t* err;
+  int num_problems, T, S, units_per_cta;
+};
+struct SplitMaps {
+  CUtensorMap a[kMaxProblems];  // A pools, box {64, R, 1}
+  CUtensorMap b[kMaxProblems];  // B pools, box {R, n_box, 1}
+};
+cudaError_t launch_bgmv_split(int mode, int dtype, int R, const SplitMaps& maps, const SplitArgs& a,
+                              cudaStream_t st);
 
 // Segmented tensor-core kernels (sgmv_tcgen05.cu).
 struct SgmvTcArgs {

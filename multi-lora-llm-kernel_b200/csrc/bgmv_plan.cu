@@ -31,7 +31,7 @@ namespace persona {
 // ready words) and start the epoch at 1; run by every thread of a plan kernel.
 __device__ __forceinline__ void init_work_state(int32_t* ws, int T, int tid, int nthreads) {
   WorkView w = work_view(ws, T);
-  const int words = kSyncWords + 2 * static_cast<int>(plan_tpad(T));
+  const int words = kSyncWords + 2 * kMaxProblems * static_cast<int>(plan_tpad(T));
   for (int i = tid; i < words; i += nthreads) w.sync[i] = (i == kSyncEpoch) ? 1 : 0;
 }
 

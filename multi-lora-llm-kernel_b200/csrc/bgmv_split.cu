@@ -1,41 +1,46 @@
 // Split BGMV kernels for B200 (sm_100a): shrink, expand and fused
-// shrink->expand over a row-grouping plan, with each item's work cut into
-// slices that every CTA of the GPU can take.
+// shrink->expand over a row-grouping plan, for one projection or for up to
+// kMaxProblems projections that share the batch's slots (one decoder layer's
+// q/k/v/o/gate/up/down), with every item's work cut into slices that every
+// pipeline of the GPU can take.
 //
 // Work units.  A plan item is one adapter slot and up to 16 rows that use it.
-// Its shrink is cut into nks K-slices and its expand into nes N-slices; the
-// unit list is [all shrink slices, item by item] then [all expand slices].
-// Slice counts are chosen on the device from the item count so that the GPU
-// gets about 8 units per CTA: a decode batch of 8 adapters is spread over the
-// whole GPU, and a batch of ~150 adapters no longer leaves most CTAs idle
-// while a few stream a second whole adapter.
+// For each problem its shrink is cut into nks K-slices and its expand into
+// nes N-slices; the unit list is [all shrink slices, problem by problem,
+// item by item] then [all expand slices, same order].  Slice counts are
+// chosen on the device from the item count so that each pipeline gets about
+// units_per_cta units: a decode batch of 8 adapters spreads over the whole
+// GPU, a batch of ~150 adapters leaves no pipeline streaming a second whole
+// adapter while others idle, and the seven projections of a layer fill each
+// other's tails.
 //
-// Scheduling.  Persistent CTAs (two per SM) claim units in list order from a
-// device-wide counter.  Because every shrink unit precedes every expand unit
-// in claim order, a CTA that waits for an item's v only waits on shrink units
-// that running CTAs have already claimed, so the kernel always makes progress
-// even when not all CTAs are resident.
+// Scheduling.  Persistent pipelines claim units in list order from a
+// device-wide counter.  Every shrink unit precedes every expand unit in claim
+// order, so a pipeline that waits for an item's v only waits on shrink units
+// that running pipelines have already claimed: the kernel always makes
+// progress, even when not all CTAs are resident.
 //
 // Partial v.  A shrink slice writes its partial v (16 rows x R, fp32) to the
-// workspace (L2-resident).  The CTA that completes an item's last slice
+// workspace (L2-resident).  The pipeline that completes an item's last slice
 // (per-item counter) sums the partials in slice order -- so the result does
-// not depend on which CTA ran what -- writes v, and releases the item by
-// storing the call's epoch into its ready word.  Expand slices wait for that
-// word (bounded), read v, and stream B and y.  The epoch (bumped by the last
-// CTA of every launch) makes stale ready words from earlier calls harmless,
-// and the last CTA also resets the claim counter for the next launch.
+// not depend on which pipeline ran what -- writes v, and releases the item by
+// storing the launch's epoch into its ready word.  Expand slices wait for
+// that word (bounded), read v, and stream B and y.  The epoch (bumped by the
+// last CTA of every launch) makes stale ready words from earlier launches
+// harmless, and the last CTA also resets the claim counter.
 //
-// Inside a CTA (six warps): one producer warp (TMA boxes of A / B, 1-D bulk
-// copies of the x / y / v rows, L2 prefetch of the next unit) feeds a 4-slot
-// ring.  Four consumer warps run the shrink stages on the 16-row warp-MMA
-// tiles of bgmv_stages.cuh.  For ranks 16 / 32 / 64 the expand runs on the
-// tensor cores: the item's rows are the N = 16 side of a tcgen05 MMA whose
-// M = 128 side is a TMA-loaded B tile, so one MMA warp turns a stage into
-// D[128 output columns][16 rows] in tensor memory with 2 * R / 16
-// instructions (v split into 16-bit hi and lo halves, both as small swizzled
-// shared-memory operands), and a consumer thread per output column only
-// reads its 16 accumulators, adds y and stores.  Rank 8 keeps the warp-MMA
-// expand.
+// Inside a CTA.  Kernels that allocate tensor memory run one CTA per SM, so
+// each CTA carries kGroups independent pipelines of six warps: a producer
+// warp (TMA boxes of A / B, 1-D bulk copies of the x / y / v rows, L2
+// prefetch of the next unit) feeding a 4-slot ring, four consumer warps that
+// run the shrink stages on the 16-row warp-MMA tiles of bgmv_stages.cuh, and
+// an MMA warp.  For ranks 16 / 32 / 64 the expand runs on the tensor cores:
+// the item's rows are the N = 16 side of a tcgen05 MMA whose M = 128 side is
+// a TMA-loaded B tile, so the MMA warp turns a stage into D[128 output
+// columns][16 rows] in tensor memory with 2 * R / 16 instructions (v split
+// into 16-bit hi and lo halves, both small swizzled shared-memory operands),
+// and a consumer thread per output column reads its 16 accumulators, adds y
+// and stores.  Rank 8 keeps the warp-MMA expand.
 #include "bgmv_stages.cuh"
 #include "tcgen05.cuh"
 
@@ -45,33 +50,49 @@ namespace {
 
 constexpr int kUnitRing = 4;
 constexpr int kUnitsPerCta = 8;
-// One CTA per SM (kernels that allocate tensor memory are scheduled one per
-// SM) running kGroups independent pipelines of six warps: 4 consumers, a
-// producer and an MMA warp, each group with its own ring and unit queue.
+enum : int { kUnitEnd = 0, kUnitShrink = 1, kUnitExpand = 2 };
+
 constexpr int kGroups = 2;
 constexpr int kGroupThreads = kBgmvThreads + 32;  // + one MMA warp
 constexpr int kSplitThreads = kGroups * kGroupThreads;
 constexpr int kMmaWarp = kConsumerWarps + 1;
 constexpr uint32_t kGroupTmemCols = 128;  // one 16-column accumulator per (ring slot, 128-row box)
 constexpr uint32_t kTmemCols = kGroups * kGroupTmemCols;
-enum : int { kUnitEnd = 0, kUnitShrink = 1, kUnitExpand = 2 };
 
 struct UnitDesc {
   int kind;
+  int prob;
   int item;
   int slice;
   int slot;
   int count;
   int pos;  // plan position of the item's first row
-  int pad[2];
+  int pad;
   int rows[kRowsPerItem];
 };
 
+// Slice geometry of one problem; identical in every thread of every CTA.
+struct ProbGeom {
+  int kst, nst;      // A stages over K, B stages over N
+  int ks_st, es_st;  // stages per shrink / expand slice
+  int nks, nes;      // slices per item
+  int stage_rows;    // output columns per B stage
+  int s_base;        // first shrink unit of this problem
+  int e_base;        // first expand unit of this problem
+  int p_base;        // first partial-v slot of this problem
+};
+
+struct SplitShared {
+  ProbGeom geom[kMaxProblems];
+  int units_s, units;
+  uint32_t tmem;
+};
+
 constexpr int kSRingBytes = kSlots * kSlotBytes;
+constexpr int kSVopBytes = 2 * kRowsPerItem * kMaxR * 2;  // v hi / lo MMA operands, 16 rows x R each
 constexpr int kSVBytes = kRowsPerItem * kMaxR * 4;
 constexpr int kSRedBytes = kRowsPerItem * kMaxR * 4;
 constexpr int kSUnitBytes = kUnitRing * static_cast<int>(sizeof(UnitDesc));
-constexpr int kSVopBytes = 2 * kRowsPerItem * kMaxR * 2;  // v hi / lo MMA operands, 16 rows x R each
 constexpr int kSBarCount = 3 * kSlots + 2 * kUnitRing + 2;
 constexpr int kGroupSmemRaw = kSRingBytes + kSVopBytes + 2 * kSVBytes + kSRedBytes + kSUnitBytes + kSBarCount * 8 + 16;
 constexpr int kGroupSmem = (kGroupSmemRaw + 1023) / 1024 * 1024;
@@ -81,9 +102,9 @@ static_assert(kSplitSmemBytes <= 227 * 1024, "one CTA per SM");
 struct SplitSmem {
   uint8_t* ring;
   uint8_t* vop;  // [hi | lo] expand operands (1024-aligned)
-  float* pv;   // [16][R] this unit's partial / the item's v
-  float* vf;   // [16][R] the item's v for the expand
-  float* red;  // per-warp MMA tiles / maxima
+  float* pv;     // [16][R] this unit's partial / the item's v
+  float* vf;     // [16][R] the item's v for the expand
+  float* red;    // per-warp MMA tiles / maxima
   UnitDesc* units;
   uint64_t* full;
   uint64_t* empty;
@@ -91,9 +112,8 @@ struct SplitSmem {
   uint64_t* uempty;
   uint64_t* mma_done;  // [kSlots] expand MMAs of the slot's stage complete
   uint64_t* vready;    // the expand unit's v operands are in shared memory
-  uint64_t* mma_fin;   // every MMA of the CTA complete (before TMEM is freed)
+  uint64_t* mma_fin;   // every MMA of the pipeline complete (before TMEM is freed)
   int* flag;
-  uint32_t* tmem_base;
 };
 
 __device__ __forceinline__ SplitSmem carve(uint8_t* raw, int grp) {
@@ -116,44 +136,55 @@ __device__ __forceinline__ SplitSmem carve(uint8_t* raw, int grp) {
   p.vready = bars + 3 * kSlots + 2 * kUnitRing;
   p.mma_fin = bars + 3 * kSlots + 2 * kUnitRing + 1;
   p.flag = reinterpret_cast<int*>(bars + kSBarCount);
-  p.tmem_base = reinterpret_cast<uint32_t*>(bars + kSBarCount) + 1;
   return p;
 }
 
-// Slice geometry; every thread of every CTA computes the same values.
-struct SplitGeom {
-  int kst, nst;      // A stages over K, B stages over N
-  int ks_st, es_st;  // stages per shrink / expand slice
-  int nks, nes;      // slices per item
-  int units_s, units;
-};
-
-__device__ __forceinline__ SplitGeom split_geom(int n_items, int K, int N, int kc, int stage_rows, int grid,
-                                                int units_per_cta, bool shrink, bool expand) {
-  SplitGeom g;
-  g.kst = shrink ? (K + kc - 1) / kc : 0;
-  g.nst = expand ? (N + stage_rows - 1) / stage_rows : 0;
+// Slice counts for every problem: about units_per_cta units per pipeline in
+// total, shared between the problems by their stage counts and, within a
+// problem, between shrink and expand by theirs.  Run by one thread.
+__device__ void plan_units(SplitShared& sh, const SplitArgs& a, int n_items, int kc, int nb_rows, int pipes,
+                           bool shrink, bool expand) {
+  const int P = a.num_problems;
   const int items = n_items > 0 ? n_items : 1;
-  const int upc = units_per_cta > 0 ? units_per_cta : kUnitsPerCta;
-  const int per_item = max(1, (upc * grid + items - 1) / items);
-  int nks = 1, nes = 1;
-  if (shrink && expand) {
-    nks = max(1, (per_item * g.kst + (g.kst + g.nst) / 2) / (g.kst + g.nst));
-    nes = max(1, per_item - nks);
-  } else if (shrink) {
-    nks = per_item;
-  } else {
-    nes = per_item;
+  const int upc = a.units_per_cta > 0 ? a.units_per_cta : kUnitsPerCta;
+  int work = 0;
+  for (int p = 0; p < P; ++p) {
+    ProbGeom& g = sh.geom[p];
+    g.stage_rows = (nb_rows / a.prob[p].n_box) * a.prob[p].n_box;
+    g.kst = shrink ? (a.prob[p].K + kc - 1) / kc : 0;
+    g.nst = expand ? (a.prob[p].N + g.stage_rows - 1) / g.stage_rows : 0;
+    work += g.kst + g.nst;
   }
-  nks = min(min(nks, max(1, g.kst)), max(1, kPartSlots / items));
-  nes = min(nes, max(1, g.nst));
-  g.ks_st = shrink ? (g.kst + nks - 1) / nks : 0;
-  g.nks = shrink ? (g.kst + g.ks_st - 1) / g.ks_st : 0;
-  g.es_st = expand ? (g.nst + nes - 1) / nes : 0;
-  g.nes = expand ? (g.nst + g.es_st - 1) / g.es_st : 0;
-  g.units_s = n_items * g.nks;
-  g.units = g.units_s + n_items * g.nes;
-  return g;
+  int s_units = 0, e_units = 0;
+  for (int p = 0; p < P; ++p) {
+    ProbGeom& g = sh.geom[p];
+    const long long budget = static_cast<long long>(upc) * pipes * (g.kst + g.nst) / (work > 0 ? work : 1);
+    const int per_item = max(1, static_cast<int>((budget + items - 1) / items));
+    int nks = 1, nes = 1;
+    if (shrink && expand) {
+      nks = max(1, (per_item * g.kst + (g.kst + g.nst) / 2) / max(1, g.kst + g.nst));
+      nes = max(1, per_item - nks);
+    } else if (shrink) {
+      nks = per_item;
+    } else {
+      nes = per_item;
+    }
+    nks = min(min(nks, max(1, g.kst)), max(1, kPartSlots / (items * P)));
+    nes = min(nes, max(1, g.nst));
+    g.ks_st = shrink ? (g.kst + nks - 1) / nks : 0;
+    g.nks = shrink ? (g.kst + g.ks_st - 1) / g.ks_st : 0;
+    g.es_st = expand ? (g.nst + nes - 1) / nes : 0;
+    g.nes = expand ? (g.nst + g.es_st - 1) / g.es_st : 0;
+    g.s_base = s_units;
+    g.p_base = s_units;  // partial slots follow the shrink units one to one
+    s_units += n_items * g.nks;
+  }
+  for (int p = 0; p < P; ++p) {
+    sh.geom[p].e_base = s_units + e_units;
+    e_units += n_items * sh.geom[p].nes;
+  }
+  sh.units_s = s_units;
+  sh.units = s_units + e_units;
 }
 
 __device__ __forceinline__ uint16_t lds16(uint32_t addr) {
@@ -192,8 +223,7 @@ __device__ __forceinline__ bool wait_word(const int* p, int want, int32_t* err) 
 
 template <typename DT, int R, int MODE>
 __global__ void __launch_bounds__(kSplitThreads, 1)
-    bgmv_split_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                      const BgmvArgs args) {
+    bgmv_split_kernel(const __grid_constant__ SplitMaps maps, const SplitArgs args) {
   using C = RankCfg<R>;
   constexpr bool kDoShrink = (MODE & kModeShrink) != 0;
   constexpr bool kDoExpand = (MODE & kModeExpand) != 0;
@@ -203,83 +233,93 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
   constexpr uint32_t kOpSbo = 8 * 2 * R;
   constexpr uint32_t kIdesc = tc::idesc_f16(std::is_same<DT, __nv_bfloat16>::value ? 1u : 0u, 128, kRowsPerItem);
   extern __shared__ uint8_t smem_raw[];
-  __shared__ uint32_t s_tmem;
+  __shared__ SplitShared sh;
   const int grp = static_cast<int>(threadIdx.x) / kGroupThreads;  // pipeline of this thread
   const int tid = static_cast<int>(threadIdx.x) - grp * kGroupThreads;
   const int warp = tid >> 5, lane = tid & 31;
   const int bar_cons = kNamedBarConsumers + grp;  // named barrier of this group's consumers
   SplitSmem sm = carve(smem_raw, grp);
 
+  PlanView pv = plan_view(args.ws, args.T);
+  const int P = args.num_problems;
+  WorkView wv = work_view(args.ws, args.T, P);
+  const int n_items = pv.hdr[kHdrItems];
+  const int epoch = wv.sync[kSyncEpoch];
+  const int64_t tpad = plan_tpad(args.T);
+
   if (tid == 0) {
     for (int s = 0; s < kSlots; ++s) {
       mbar_init(&sm.full[s], 1);
       mbar_init(&sm.empty[s], kConsumerWarps);
+      mbar_init(&sm.mma_done[s], 1);
     }
     for (int i = 0; i < kUnitRing; ++i) {
       mbar_init(&sm.ufull[i], 1);
       mbar_init(&sm.uempty[i], kConsumerWarps + 1);  // consumers + the MMA warp
     }
-    for (int s = 0; s < kSlots; ++s) mbar_init(&sm.mma_done[s], 1);
     mbar_init(sm.vready, 1);
     mbar_init(sm.mma_fin, 1);
-    *sm.tmem_base = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
+  if (threadIdx.x == 0)
+    plan_units(sh, args, n_items, C::kKC, C::kNB, static_cast<int>(gridDim.x) * kGroups, kDoShrink, kDoExpand);
   if (kTcE && grp == 0 && warp == kMmaWarp) {  // one allocation for both groups
-    tc::tmem_alloc(&s_tmem, kTmemCols);
+    tc::tmem_alloc(&sh.tmem, kTmemCols);
     tc::tmem_relinquish();
   }
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
-  const uint32_t tmem = s_tmem + static_cast<uint32_t>(grp) * kGroupTmemCols;
+  const uint32_t tmem = sh.tmem + static_cast<uint32_t>(grp) * kGroupTmemCols;
+  const int units_s = sh.units_s, units = sh.units;
 
-  int32_t* ws = const_cast<int32_t*>(args.plan);
-  PlanView pv = plan_view(ws, args.T);
-  WorkView wv = work_view(ws, args.T);
-  const int n_items = pv.hdr[kHdrItems];
-  const int epoch = wv.sync[kSyncEpoch];
-  const int stage_rows = (C::kNB / args.n_box) * args.n_box;
-  const SplitGeom G = split_geom(n_items, args.K, args.N, C::kKC, stage_rows, static_cast<int>(gridDim.x) * kGroups,
-                                 args.units_per_cta, kDoShrink, kDoExpand);
+  // Unit u -> (kind, problem, item, slice); [lo, hi) is the k range of a
+  // shrink slice or the n range of an expand slice.
+  struct Dec {
+    int kind, prob, item, slice, lo, hi;
+  };
+  auto decode = [&](int u) -> Dec {
+    Dec d;
+    d.kind = kUnitEnd;
+    d.prob = d.item = d.slice = d.lo = d.hi = 0;
+    if (u >= units) return d;
+    if (u < units_s) {
+      int p = 0;
+      while (p + 1 < P && sh.geom[p + 1].s_base <= u) ++p;
+      const ProbGeom& gg = sh.geom[p];
+      const int v = u - gg.s_base;
+      d.kind = kUnitShrink;
+      d.prob = p;
+      d.item = v / gg.nks;
+      d.slice = v - d.item * gg.nks;
+      d.lo = d.slice * gg.ks_st * C::kKC;
+      d.hi = min(args.prob[p].K, d.lo + gg.ks_st * C::kKC);
+    } else {
+      int p = 0;
+      while (p + 1 < P && sh.geom[p + 1].e_base <= u) ++p;
+      const ProbGeom& gg = sh.geom[p];
+      const int v = u - gg.e_base;
+      d.kind = kUnitExpand;
+      d.prob = p;
+      d.item = v / gg.nes;
+      d.slice = v - d.item * gg.nes;
+      d.lo = d.slice * gg.es_st * gg.stage_rows;
+      d.hi = min(args.prob[p].N, d.lo + gg.es_st * gg.stage_rows);
+    }
+    return d;
+  };
 
   if (warp == kConsumerWarps) {
     // ------------------------------------------------------- producer --
-    const uint16_t* x = static_cast<const uint16_t*>(args.x);
-    const uint16_t* yg = static_cast<const uint16_t*>(args.y);
-    if (lane == 0) {
-      if (kDoShrink) tma_prefetch_desc(&tmA);
-      if (kDoExpand) tma_prefetch_desc(&tmB);
+    if (lane < P) {
+      if (kDoShrink) tma_prefetch_desc(&maps.a[lane]);
+      if (kDoExpand) tma_prefetch_desc(&maps.b[lane]);
     }
     // Claims run two units ahead: the atomic for unit j+2 is issued while
     // unit j streams, and its result is first read one unit later, so the
     // round trip to L2 never stalls the loads.
     auto claim_issue = [&]() -> int { return lane == 0 ? atomicAdd(&wv.sync[kSyncQueue], 1) : 0; };
     auto claim_read = [&](int pending) -> int { return __shfl_sync(0xffffffffu, pending, 0); };
-    struct Dec {
-      int kind, item, slice, lo, hi;  // [lo, hi): k range (shrink) or n range (expand)
-    };
-    auto decode = [&](int u) -> Dec {
-      Dec d;
-      if (u >= G.units) {
-        d.kind = kUnitEnd;
-        d.item = d.slice = d.lo = d.hi = 0;
-      } else if (u < G.units_s) {
-        d.kind = kUnitShrink;
-        d.item = u / G.nks;
-        d.slice = u - d.item * G.nks;
-        d.lo = d.slice * G.ks_st * C::kKC;
-        d.hi = min(args.K, d.lo + G.ks_st * C::kKC);
-      } else {
-        const int v = u - G.units_s;
-        d.kind = kUnitExpand;
-        d.item = v / G.nes;
-        d.slice = v - d.item * G.nes;
-        d.lo = d.slice * G.es_st * stage_rows;
-        d.hi = min(args.N, d.lo + G.es_st * stage_rows);
-      }
-      return d;
-    };
     uint32_t g = 0;
     auto claim_slot = [&](uint32_t bytes) -> int {
       const int s = static_cast<int>(g % kSlots);
@@ -307,6 +347,7 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
       if (lane < kRowsPerItem) ud->rows[lane] = row;
       if (lane == 0) {
         ud->kind = d.kind;
+        ud->prob = d.prob;
         ud->item = d.item;
         ud->slice = d.slice;
         ud->slot = it.x;
@@ -320,27 +361,30 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
       // The next unit is known; start pulling its data into L2 so that its
       // loads hit L2 and more bytes are in flight than the ring holds.
       const int un = claim_read(pending);
-      pending = un < G.units ? claim_issue() : 0;
+      pending = un < units ? claim_issue() : 0;
       const Dec dn = decode(un);
       if (dn.kind != kUnitEnd) {
         const int4 nit = pv.items[dn.item];
         const int nrow = lane < nit.z ? pv.perm[nit.y + lane] : 0;
+        const SplitProblem& np = args.prob[dn.prob];
         if (dn.kind == kUnitShrink) {
-          for (int k0 = dn.lo + 64 * lane; k0 < dn.hi; k0 += 64 * 32) tma_prefetch_3d(&tmA, k0, 0, nit.x);
+          for (int k0 = dn.lo + 64 * lane; k0 < dn.hi; k0 += 64 * 32) tma_prefetch_3d(&maps.a[dn.prob], k0, 0, nit.x);
           if (lane < nit.z)
-            bulk_prefetch_l2(x + static_cast<int64_t>(nrow) * args.ldx + dn.lo,
+            bulk_prefetch_l2(static_cast<const uint16_t*>(np.x) + static_cast<int64_t>(nrow) * np.ldx + dn.lo,
                              static_cast<uint32_t>(dn.hi - dn.lo) * 2u);
         } else {
-          for (int n0 = dn.lo + args.n_box * lane; n0 < dn.hi; n0 += args.n_box * 32)
-            tma_prefetch_3d(&tmB, 0, n0, nit.x);
+          for (int n0 = dn.lo + np.n_box * lane; n0 < dn.hi; n0 += np.n_box * 32)
+            tma_prefetch_3d(&maps.b[dn.prob], 0, n0, nit.x);
           if (lane < nit.z)
-            bulk_prefetch_l2(yg + static_cast<int64_t>(nrow) * args.ldy + dn.lo,
+            bulk_prefetch_l2(static_cast<const uint16_t*>(np.y) + static_cast<int64_t>(nrow) * np.ldy + dn.lo,
                              static_cast<uint32_t>(dn.hi - dn.lo) * 2u);
         }
       }
 
       const int slot = it.x, c = it.z;
+      const SplitProblem& pr = args.prob[d.prob];
       if (d.kind == kUnitShrink) {
+        const uint16_t* x = static_cast<const uint16_t*>(pr.x);
         for (int k0 = d.lo; k0 < d.hi; k0 += C::kKC) {
           const int valid = min(C::kKC, d.hi - k0);
           const int nbox = (valid + 63) / 64;
@@ -348,13 +392,15 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
           const int s = claim_slot(static_cast<uint32_t>(nbox * C::kABoxBytes) + static_cast<uint32_t>(c) * xb);
           uint8_t* st = sm.ring + s * kSlotBytes;
           if (lane == 0)
-            for (int b = 0; b < nbox; ++b) tma_load_3d(st + b * C::kABoxBytes, &tmA, &sm.full[s], k0 + 64 * b, 0, slot);
+            for (int b = 0; b < nbox; ++b)
+              tma_load_3d(st + b * C::kABoxBytes, &maps.a[d.prob], &sm.full[s], k0 + 64 * b, 0, slot);
           if (lane < c)
-            bulk_load(st + C::kXOff + lane * C::kXPitch, x + static_cast<int64_t>(row) * args.ldx + k0, xb,
-                      &sm.full[s]);
+            bulk_load(st + C::kXOff + lane * C::kXPitch, x + static_cast<int64_t>(row) * pr.ldx + k0, xb, &sm.full[s]);
           ++g;
         }
       } else {
+        const uint16_t* yg = static_cast<const uint16_t*>(pr.y);
+        const int stage_rows = sh.geom[d.prob].stage_rows;
         if (MODE == kModeExpand) {
           const int s = claim_slot(static_cast<uint32_t>(c * R * 4));
           if (lane < c)
@@ -364,15 +410,15 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
         }
         for (int n0 = d.lo; n0 < d.hi; n0 += stage_rows) {
           const int rows_here = min(stage_rows, d.hi - n0);
-          const int nbox = (rows_here + args.n_box - 1) / args.n_box;
+          const int nbox = (rows_here + pr.n_box - 1) / pr.n_box;
           const uint32_t yb = static_cast<uint32_t>(rows_here) * 2u;
-          const int s = claim_slot(static_cast<uint32_t>(nbox * args.n_box * 2 * R) + static_cast<uint32_t>(c) * yb);
+          const int s = claim_slot(static_cast<uint32_t>(nbox * pr.n_box * 2 * R) + static_cast<uint32_t>(c) * yb);
           uint8_t* st = sm.ring + s * kSlotBytes;
           if (lane == 0)
             for (int b = 0; b < nbox; ++b)
-              tma_load_3d(st + b * args.n_box * 2 * R, &tmB, &sm.full[s], 0, n0 + b * args.n_box, slot);
+              tma_load_3d(st + b * pr.n_box * 2 * R, &maps.b[d.prob], &sm.full[s], 0, n0 + b * pr.n_box, slot);
           if (lane < c)
-            bulk_load(st + C::kYOff + lane * C::kYStride, yg + static_cast<int64_t>(row) * args.ldy + n0, yb,
+            bulk_load(st + C::kYOff + lane * C::kYStride, yg + static_cast<int64_t>(row) * pr.ldy + n0, yb,
                       &sm.full[s]);
           ++g;
         }
@@ -392,16 +438,17 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
       for (int j = 0;; ++j) {
         const int iq = j % kUnitRing;
         mbar_wait(&sm.ufull[iq], (j / kUnitRing) & 1, args.err);
-        const int kind = sm.units[iq].kind, slice = sm.units[iq].slice;
+        const int kind = sm.units[iq].kind, prob = sm.units[iq].prob, slice = sm.units[iq].slice;
         if (kind == kUnitEnd) break;
+        const ProbGeom& gg = sh.geom[prob];
         int nst, lo = 0, hi = 0;
         if (kind == kUnitShrink) {
-          const int klo = slice * G.ks_st * C::kKC;
-          nst = (min(args.K, klo + G.ks_st * C::kKC) - klo + C::kKC - 1) / C::kKC;
+          const int klo = slice * gg.ks_st * C::kKC;
+          nst = (min(args.prob[prob].K, klo + gg.ks_st * C::kKC) - klo + C::kKC - 1) / C::kKC;
         } else {
-          lo = slice * G.es_st * stage_rows;
-          hi = min(args.N, lo + G.es_st * stage_rows);
-          nst = (hi - lo + stage_rows - 1) / stage_rows;
+          lo = slice * gg.es_st * gg.stage_rows;
+          hi = min(args.prob[prob].N, lo + gg.es_st * gg.stage_rows);
+          nst = (hi - lo + gg.stage_rows - 1) / gg.stage_rows;
           if (MODE == kModeExpand) {  // the v stage
             const int s = static_cast<int>(g % kSlots);
             mbar_wait(&sm.full[s], (g / kSlots) & 1, args.err);
@@ -420,7 +467,7 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
           mbar_wait(&sm.full[s], (g / kSlots) & 1, args.err);
           if (tc_unit) {
             tc::fence_after_sync();
-            const int rows_here = min(stage_rows, hi - (lo + i * stage_rows));
+            const int rows_here = min(gg.stage_rows, hi - (lo + i * gg.stage_rows));
             const int nbt = (rows_here + 127) / 128;
             const uint32_t sb = smem_u32(sm.ring + s * kSlotBytes);
             for (int b = 0; b < nbt; ++b) {
@@ -447,7 +494,6 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
     __syncwarp();
   } else {
     // ------------------------------------------------------ consumers --
-    uint16_t* y = static_cast<uint16_t*>(args.y);
     if (MODE == kModeShrink) {
       // Rows without a (valid) adapter get v = 0; the items never touch them.
       const int gtid = (blockIdx.x * kGroups + grp) * kConsumers + tid;
@@ -464,13 +510,15 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
       const UnitDesc* ud = &sm.units[iq];
       const int kind = ud->kind;
       if (kind == kUnitEnd) break;
-      const int c = ud->count, item = ud->item, slice = ud->slice, pos = ud->pos;
+      const int prob = ud->prob, c = ud->count, item = ud->item, slice = ud->slice, pos = ud->pos;
       const int* rows = ud->rows;
       const int E = c * R;
+      const ProbGeom& gg = sh.geom[prob];
+      const SplitProblem& pr = args.prob[prob];
 
       if (kDoShrink && kind == kUnitShrink) {
-        const int klo = slice * G.ks_st * C::kKC;
-        const int khi = min(args.K, klo + G.ks_st * C::kKC);
+        const int klo = slice * gg.ks_st * C::kKC;
+        const int khi = min(pr.K, klo + gg.ks_st * C::kKC);
         float d[C::kTPW][2][4];
 #pragma unroll
         for (int t = 0; t < C::kTPW; ++t)
@@ -500,11 +548,11 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
 #pragma unroll
         for (int t = 0; t < C::kTPW; ++t) {
           float* rw = sm.red + (warp * C::kTPW + t) * (kRowsPerItem * 8);
-          const int gg = lane >> 2, tt = lane & 3;
-          rw[gg * 8 + 2 * tt] = d[t][0][0] + d[t][1][0];
-          rw[gg * 8 + 2 * tt + 1] = d[t][0][1] + d[t][1][1];
-          rw[(gg + 8) * 8 + 2 * tt] = d[t][0][2] + d[t][1][2];
-          rw[(gg + 8) * 8 + 2 * tt + 1] = d[t][0][3] + d[t][1][3];
+          const int gq = lane >> 2, tq = lane & 3;
+          rw[gq * 8 + 2 * tq] = d[t][0][0] + d[t][1][0];
+          rw[gq * 8 + 2 * tq + 1] = d[t][0][1] + d[t][1][1];
+          rw[(gq + 8) * 8 + 2 * tq] = d[t][0][2] + d[t][1][2];
+          rw[(gq + 8) * 8 + 2 * tq + 1] = d[t][0][3] + d[t][1][3];
         }
         named_sync(bar_cons, kConsumers);
         for (int e = tid; e < E; e += kConsumers) {
@@ -518,25 +566,26 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
           sm.pv[e] = sum;
         }
         named_sync(bar_cons, kConsumers);
+        int* s_cnt = wv.s_cnt + prob * tpad + item;
         bool finisher = true;
-        if (G.nks > 1) {
-          float* part = wv.parts + static_cast<int64_t>(item * G.nks + slice) * (kRowsPerItem * R);
+        if (gg.nks > 1) {
+          float* part = wv.parts + static_cast<int64_t>(gg.p_base + item * gg.nks + slice) * kPartFloats;
           for (int e = tid; e < E; e += kConsumers) part[e] = sm.pv[e];
           named_sync(bar_cons, kConsumers);
           // One cumulative fence after the barrier orders every consumer's
           // partial stores before the count.
           if (tid == 0) {
             __threadfence();
-            *sm.flag = atomicAdd(&wv.s_cnt[item], 1) == G.nks - 1;
+            *sm.flag = atomicAdd(s_cnt, 1) == gg.nks - 1;
             if (*sm.flag) __threadfence();  // acquire side: the other slices' partials
           }
           named_sync(bar_cons, kConsumers);
           finisher = *sm.flag != 0;
           if (finisher) {
-            const float* p0 = wv.parts + static_cast<int64_t>(item * G.nks) * (kRowsPerItem * R);
+            const float* p0 = wv.parts + static_cast<int64_t>(gg.p_base + item * gg.nks) * kPartFloats;
             for (int e = tid; e < E; e += kConsumers) {
               float sum = 0.f;
-              for (int s = 0; s < G.nks; ++s) sum += __ldcg(p0 + s * (kRowsPerItem * R) + e);
+              for (int q = 0; q < gg.nks; ++q) sum += __ldcg(p0 + q * kPartFloats + e);
               sm.pv[e] = sum;
             }
           }
@@ -548,20 +597,21 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
               args.v_out[static_cast<int64_t>(rows[rr]) * R + rk] = sm.pv[e];
             }
           } else {
-            float* vfin = wv.vfinal + static_cast<int64_t>(pos) * R;
+            float* vfin = wv.vfinal + (static_cast<int64_t>(prob) * tpad + pos) * R;
             for (int e = tid; e < E; e += kConsumers) vfin[e] = sm.pv[e];
           }
           named_sync(bar_cons, kConsumers);
           if (tid == 0) {
-            if (G.nks > 1) wv.s_cnt[item] = 0;  // every slice has counted: ready for the next launch
+            if (gg.nks > 1) *s_cnt = 0;  // every slice has counted: ready for the next launch
             __threadfence();
-            if (MODE != kModeShrink) st_release(&wv.ready[item], epoch);
+            if (MODE != kModeShrink) st_release(wv.ready + prob * tpad + item, epoch);
           }
         }
         named_sync(bar_cons, kConsumers);
       }
 
       if (kDoExpand && kind == kUnitExpand) {
+        uint16_t* y = static_cast<uint16_t*>(pr.y);
         float* vfb = sm.vf;
         if (MODE == kModeExpand) {
           const int s = static_cast<int>(g % kSlots);
@@ -572,9 +622,9 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
           if (lane == 0) mbar_arrive_relaxed(&sm.empty[s]);
           ++g;
         } else {
-          if (tid == 0) wait_word(&wv.ready[item], epoch, args.err);
+          if (tid == 0) wait_word(wv.ready + prob * tpad + item, epoch, args.err);
           named_sync(bar_cons, kConsumers);
-          const float* vfin = wv.vfinal + static_cast<int64_t>(pos) * R;
+          const float* vfin = wv.vfinal + (static_cast<int64_t>(prob) * tpad + pos) * R;
           for (int e = tid; e < E; e += kConsumers) vfb[e] = __ldcg(vfin + e);
         }
         named_sync(bar_cons, kConsumers);
@@ -597,8 +647,9 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
             scale_up = __uint_as_float(static_cast<uint32_t>(127 + (e2 < 127 ? e2 : 127)) << 23);
           }
         }
-        const int nlo = slice * G.es_st * stage_rows;
-        const int nhi = min(args.N, nlo + G.es_st * stage_rows);
+        const int stage_rows = gg.stage_rows;
+        const int nlo = slice * gg.es_st * stage_rows;
+        const int nhi = min(pr.N, nlo + gg.es_st * stage_rows);
         if constexpr (kTcE) {
           // MMA operands: rows of v_hi and v_lo (2R bytes each, swizzled like
           // the TMA-written B tile); rows >= c are zero.
@@ -657,7 +708,7 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
               if (b < nbt && n < nhi) {
 #pragma unroll
                 for (int t = 0; t < kRowsPerItem; ++t)
-                  if (t < c) y[static_cast<int64_t>(rows[t]) * args.ldy + n] = out[b][t];
+                  if (t < c) y[static_cast<int64_t>(rows[t]) * pr.ldy + n] = out[b][t];
               }
             }
           }
@@ -668,8 +719,8 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
             const int s = static_cast<int>(g % kSlots);
             mbar_wait(&sm.full[s], (g / kSlots) & 1, args.err);
             const int rows_here = min(stage_rows, nhi - n0);
-            expand_stage<DT, R>(sm.ring + s * kSlotBytes, vhi, vlo, rows_here, args.n_box, n0, c, rows, y,
-                                args.ldy, scale_up, warp, lane, &sm.empty[s]);
+            expand_stage<DT, R>(sm.ring + s * kSlotBytes, vhi, vlo, rows_here, pr.n_box, n0, c, rows, y, pr.ldy,
+                                scale_up, warp, lane, &sm.empty[s]);
           }
         }
         named_sync(bar_cons, kConsumers);
@@ -684,7 +735,7 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
   __syncthreads();
   if (kTcE && grp == 0 && warp == kMmaWarp) {
     tc::fence_after_sync();
-    tc::tmem_dealloc(s_tmem, kTmemCols);
+    tc::tmem_dealloc(sh.tmem, kTmemCols);
   }
   if (threadIdx.x == 0) {
     __threadfence();
@@ -700,9 +751,17 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
 
 // ------------------------------------------------------------------ host --
 
+int bgmv_stage_rows(int R) {
+  switch (R) {
+    case 8: return RankCfg<8>::kNB;
+    case 16: return RankCfg<16>::kNB;
+    case 32: return RankCfg<32>::kNB;
+    default: return RankCfg<64>::kNB;
+  }
+}
+
 template <typename DT, int R, int MODE>
-static cudaError_t split_launch(const CUtensorMap& tmA, const CUtensorMap& tmB, const BgmvArgs& a, int max_ctas,
-                                cudaStream_t stream) {
+static cudaError_t split_launch(const SplitMaps& maps, const SplitArgs& a, cudaStream_t stream) {
   auto kern = bgmv_split_kernel<DT, R, MODE>;
   constexpr int kMaxDev = 64;
   static int ctas[kMaxDev] = {};
@@ -720,37 +779,36 @@ static cudaError_t split_launch(const CUtensorMap& tmA, const CUtensorMap& tmB, 
     if (e != cudaSuccess) return e;
     ctas[dev] = (per_sm > 0 ? per_sm : 1) * sms;
   }
-  int grid = ctas[dev] < max_ctas ? ctas[dev] : max_ctas;
-  if (grid < 1) grid = 1;
-  kern<<<grid, kSplitThreads, kSplitSmemBytes, stream>>>(tmA, tmB, a);
+  kern<<<ctas[dev], kSplitThreads, kSplitSmemBytes, stream>>>(maps, a);
   return cudaGetLastError();
 }
 
 template <typename DT, int MODE>
-static cudaError_t split_rank(int R, const CUtensorMap& tmA, const CUtensorMap& tmB, const BgmvArgs& a, int max_ctas,
-                              cudaStream_t st) {
+static cudaError_t split_rank(int R, const SplitMaps& maps, const SplitArgs& a, cudaStream_t st) {
   switch (R) {
-    case 8: return split_launch<DT, 8, MODE>(tmA, tmB, a, max_ctas, st);
-    case 16: return split_launch<DT, 16, MODE>(tmA, tmB, a, max_ctas, st);
-    case 32: return split_launch<DT, 32, MODE>(tmA, tmB, a, max_ctas, st);
-    case 64: return split_launch<DT, 64, MODE>(tmA, tmB, a, max_ctas, st);
+    case 8: return split_launch<DT, 8, MODE>(maps, a, st);
+    case 16: return split_launch<DT, 16, MODE>(maps, a, st);
+    case 32: return split_launch<DT, 32, MODE>(maps, a, st);
+    case 64: return split_launch<DT, 64, MODE>(maps, a, st);
     default: return cudaErrorInvalidValue;
   }
 }
 
-cudaError_t launch_bgmv_split(int mode, int dtype, int R, const CUtensorMap& tmA, const CUtensorMap& tmB,
-                              const BgmvArgs& a, int max_ctas, cudaStream_t st) {
+cudaError_t launch_bgmv_split(int mode, int dtype, int R, const SplitMaps& maps, const SplitArgs& a,
+                              cudaStream_t st) {
+  if (a.num_problems < 1 || a.num_problems > kMaxProblems) return cudaErrorInvalidValue;
+  if (mode != kModeFused && a.num_problems != 1) return cudaErrorInvalidValue;
   const bool bf = dtype == PERSONA_DTYPE_BF16;
   switch (mode) {
     case kModeShrink:
-      return bf ? split_rank<__nv_bfloat16, kModeShrink>(R, tmA, tmB, a, max_ctas, st)
-                : split_rank<__half, kModeShrink>(R, tmA, tmB, a, max_ctas, st);
+      return bf ? split_rank<__nv_bfloat16, kModeShrink>(R, maps, a, st)
+                : split_rank<__half, kModeShrink>(R, maps, a, st);
     case kModeExpand:
-      return bf ? split_rank<__nv_bfloat16, kModeExpand>(R, tmA, tmB, a, max_ctas, st)
-                : split_rank<__half, kModeExpand>(R, tmA, tmB, a, max_ctas, st);
+      return bf ? split_rank<__nv_bfloat16, kModeExpand>(R, maps, a, st)
+                : split_rank<__half, kModeExpand>(R, maps, a, st);
     default:
-      return bf ? split_rank<__nv_bfloat16, kModeFused>(R, tmA, tmB, a, max_ctas, st)
-                : split_rank<__half, kModeFused>(R, tmA, tmB, a, max_ctas, st);
+      return bf ? split_rank<__nv_bfloat16, kModeFused>(R, maps, a, st)
+                : split_rank<__half, kModeFused>(R, maps, a, st);
   }
 }
 

@@ -118,8 +118,9 @@ int dtype_code(const at::Tensor& t, const char* op) {
 // fine); returns the row stride in elements.
 int64_t row_stride(const at::Tensor& t) { return t.size(0) <= 1 ? t.size(1) : t.stride(0); }
 
+// Sized for a multi-projection launch, so that any plan serves every op.
 at::Tensor workspace_for(int64_t T, const at::Tensor& like) {
-  const size_t bytes = persona_bgmv_workspace_size(T);
+  const size_t bytes = persona_bgmv_multi_workspace_size(T, PERSONA_MAX_PROBLEMS);
   return at::empty({static_cast<int64_t>(bytes)}, like.options().dtype(at::kByte));
 }
 
@@ -243,6 +244,53 @@ void fused_impl(const at::Tensor& x, const at::Tensor& a_pool, const at::Tensor&
                                     S, dt, ws.data_ptr(), ws.numel(), flags, error_word_device(dev),
                                     stream);
   check_status(st, op);
+  after_launch(dev, op, stream);
+}
+
+void fused_multi_impl(at::TensorList xs, at::TensorList a_pools, at::TensorList b_pools, const at::Tensor& slots,
+                      at::TensorList ys, const c10::optional<at::Tensor>& plan) {
+  const char* op = "bgmv_fused_multi";
+  const int P = static_cast<int>(xs.size());
+  TORCH_CHECK(P >= 1 && P <= PERSONA_MAX_PROBLEMS, op, ": 1 to ", PERSONA_MAX_PROBLEMS, " projections");
+  TORCH_CHECK(a_pools.size() == xs.size() && b_pools.size() == xs.size() && ys.size() == xs.size(), op,
+              ": xs, a_pools, b_pools and ys must have the same length");
+  TORCH_CHECK(slots.is_cuda() && slots.is_contiguous() && slots.dim() == 1 && slots.scalar_type() == at::kInt, op,
+              ": slots must be a contiguous int32 CUDA vector");
+  const int64_t T = slots.size(0);
+  const int64_t S = a_pools[0].size(0), R = a_pools[0].size(1);
+  const int dt = dtype_code(xs[0], op);
+  persona_bgmv_problem probs[PERSONA_MAX_PROBLEMS];
+  for (int p = 0; p < P; ++p) {
+    const at::Tensor &x = xs[p], &a = a_pools[p], &b = b_pools[p], &y = ys[p];
+    TORCH_CHECK(x.is_cuda() && a.is_cuda() && b.is_cuda() && y.is_cuda(), op, ": all tensors must be CUDA");
+    TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1 && y.dim() == 2 && y.stride(1) == 1, op,
+                ": tensors must be contiguous");
+    check_pool_a(a, op);
+    check_pool_b(b, op);
+    TORCH_CHECK(x.size(0) == T && y.size(0) == T, op, ": x / y rows must match slots");
+    TORCH_CHECK(a.size(0) == S && a.size(1) == R && a.size(2) == x.size(1), op, ": a_pool shape mismatch");
+    TORCH_CHECK(b.size(0) == S && b.size(2) == R && b.size(1) == y.size(1), op, ": b_pool shape mismatch");
+    TORCH_CHECK(x.scalar_type() == xs[0].scalar_type() && a.scalar_type() == x.scalar_type() &&
+                    b.scalar_type() == x.scalar_type() && y.scalar_type() == x.scalar_type(),
+                op, ": dtype mismatch");
+    TORCH_CHECK(x.get_device() == slots.get_device() && y.get_device() == slots.get_device(), op,
+                ": tensors on different devices");
+    probs[p] = persona_bgmv_problem{x.data_ptr(), row_stride(x), a.data_ptr(), a.stride(0), a.stride(1),
+                                    b.data_ptr(), b.stride(0),   y.data_ptr(), row_stride(y), x.size(1),
+                                    y.size(1)};
+  }
+  const at::cuda::OptionalCUDAGuard guard(slots.device());
+  const int dev = slots.get_device();
+  raise_pending(dev, op);
+  if (T == 0) return;
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  at::Tensor ws = plan.has_value() ? *plan : workspace_for(T, slots);
+  const int flags = plan.has_value() ? PERSONA_REUSE_PLAN : 0;
+  TORCH_CHECK(static_cast<size_t>(ws.numel()) >= persona_bgmv_multi_workspace_size(T, P), op,
+              ": plan was built for fewer rows");
+  check_status(persona_bgmv_fused_multi(probs, P, slots.data_ptr<int32_t>(), T, R, S, dt, ws.data_ptr(),
+                                        ws.numel(), flags, error_word_device(dev), stream),
+               op);
   after_launch(dev, op, stream);
 }
 
@@ -424,6 +472,8 @@ TORCH_LIBRARY(persona, m) {
   m.def("bgmv_fused(Tensor x, Tensor a_pool, Tensor b_pool, Tensor slots, Tensor(a!) y) -> ()");
   m.def("bgmv_fused_with_plan(Tensor x, Tensor a_pool, Tensor b_pool, Tensor slots, Tensor plan, "
         "Tensor(a!) y) -> ()");
+  m.def("bgmv_fused_multi(Tensor[] xs, Tensor[] a_pools, Tensor[] b_pools, Tensor slots, Tensor(a!)[] ys, "
+        "Tensor? plan=None) -> ()");
   m.def("sgmv_shrink(Tensor x, Tensor a_pool, Tensor seg_indptr, Tensor seg_slots, Tensor(a!) v) -> ()");
   m.def("sgmv_expand(Tensor v, Tensor b_pool, Tensor seg_indptr, Tensor seg_slots, Tensor(a!) y) -> ()");
   m.def("sgmv_fused(Tensor x, Tensor a_pool, Tensor b_pool, Tensor seg_indptr, Tensor seg_slots, "
@@ -439,6 +489,7 @@ TORCH_LIBRARY_IMPL(persona, CUDA, m) {
   m.impl("bgmv_expand_with_plan", &expand_with_plan);
   m.impl("bgmv_fused", &fused_noplan);
   m.impl("bgmv_fused_with_plan", &fused_with_plan);
+  m.impl("bgmv_fused_multi", &fused_multi_impl);
   m.impl("sgmv_shrink", &sgmv_shrink_op);
   m.impl("sgmv_expand", &sgmv_expand_op);
   m.impl("sgmv_fused", &sgmv_fused_op);

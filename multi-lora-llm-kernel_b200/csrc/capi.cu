@@ -3,7 +3,7 @@
 // Host side of every op: validate the arguments (the reference's TORCH_CHECKs,
 // csrc/bgmv_shrink.cu:85-121 and csrc/bgmv_expand.cu:92-128, as status
 // codes), build the TMA tensor maps of the adapter pools, then enqueue the
-// plan kernel (unless the caller reuses a plan) and the clustered kernel.
+// plan kernel (unless the caller reuses a plan) and the split kernel.
 // Nothing here synchronises with the device or allocates device memory.
 #include <cudaTypedefs.h>
 
@@ -36,20 +36,6 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 bool rank_supported(int64_t R) { return R == 8 || R == 16 || R == 32 || R == 64; }
 constexpr int64_t kI32Max = 2147483647;
-
-// Cluster size: 2 CTAs (each shrinks half of K and expands half of N of an
-// item, so twice as many CTAs share the work of the batch's items).  The
-// kernel holds one peer receive buffer, so 2 is the maximum.
-// PERSONA_CLUSTER_SIZE (1 or 2) overrides.
-int cluster_size_for(int64_t T) {
-  static const int forced = [] {
-    const char* e = std::getenv("PERSONA_CLUSTER_SIZE");
-    const int v = e ? std::atoi(e) : 0;
-    return (v == 1 || v == 2) ? v : 0;
-  }();
-  (void)T;
-  return forced ? forced : 2;
-}
 
 // A pool [S, R, K] (k fastest) as a 3-D tensor {K, R, S}; box {64 k, R rows, 1 slot}.
 int encode_a_map(CUtensorMap* m, const void* a_pool, int dtype, int64_t K, int64_t R, int64_t S,
@@ -107,21 +93,6 @@ int encode_2d_map(CUtensorMap* m, const void* base, int dtype, int64_t cols, int
   return r == CUDA_SUCCESS ? PERSONA_OK : PERSONA_ERR_CUDA;
 }
 
-void split_k(int64_t K, int cs, int* k_per_cta) {
-  const int64_t per = (K + cs - 1) / cs;
-  *k_per_cta = static_cast<int>((per + 63) / 64 * 64);
-}
-
-// N slice of each cluster CTA and the rows of one B tile: tiles of at most
-// the rank's stage rows, slices a whole number of tiles.
-void split_n(int64_t N, int cs, int R, int* n_per_cta, int* n_box) {
-  const int64_t per = (N + cs - 1) / cs;
-  const int64_t nb = bgmv_stage_rows(R);
-  const int64_t per8 = (per + 7) / 8 * 8;
-  *n_box = static_cast<int>(per8 < nb ? per8 : nb);
-  *n_per_cta = static_cast<int>((per + *n_box - 1) / *n_box * *n_box);
-}
-
 int check_common(int64_t T, int64_t S, int dtype, const void* workspace, size_t ws_bytes,
                  const int32_t* slots) {
   if (T < 0 || S <= 0) return PERSONA_ERR_SHAPE;
@@ -157,41 +128,15 @@ int check_b(const void* b_pool, int64_t b_slot_stride, const void* y, int64_t ld
   return PERSONA_OK;
 }
 
-// The split kernel runs by default; PERSONA_BGMV_KERNEL=cluster selects the
-// clustered kernel (one item per 2-CTA cluster) instead.
-bool use_cluster_kernel() {
-  static const bool v = [] {
-    const char* e = std::getenv("PERSONA_BGMV_KERNEL");
-    return e != nullptr && std::strcmp(e, "cluster") == 0;
-  }();
-  return v;
+// Rows of one B tile: the tcgen05 M side (128) for ranks >= 16, else as
+// many rows as a ring slot holds.
+int b_box_rows(int64_t N, int64_t R) {
+  const int64_t nb = R >= 16 ? 128 : bgmv_stage_rows(static_cast<int>(R));
+  const int64_t n8 = (N + 7) / 8 * 8;
+  return static_cast<int>(n8 < nb ? n8 : nb);
 }
 
-// Fills the slice fields of `a` (n_box before the B map is encoded) and
-// returns the cluster size, 0 for the split kernel.
-int kernel_geometry(int mode, int64_t T, int64_t K, int64_t N, int64_t R, BgmvArgs* a) {
-  if (use_cluster_kernel()) {
-    const int cs = cluster_size_for(T);
-    a->k_per_cta = 0;
-    a->n_per_cta = 0;
-    a->n_box = 8;
-    if (mode & kModeShrink) split_k(K, cs, &a->k_per_cta);
-    if (mode & kModeExpand) split_n(N, cs, static_cast<int>(R), &a->n_per_cta, &a->n_box);
-    return cs;
-  }
-  a->k_per_cta = 0;
-  a->n_per_cta = 0;
-  a->n_box = 8;
-  if (mode & kModeExpand) {
-    // Ranks 16..64 expand on tcgen05: B boxes are the MMA's 128-row M side.
-    const int64_t nb = R >= 16 ? 128 : bgmv_stage_rows(static_cast<int>(R));
-    const int64_t n8 = (N + 7) / 8 * 8;
-    a->n_box = static_cast<int>(n8 < nb ? n8 : nb);
-  }
-  return 0;
-}
-
-// Work units per CTA of the split kernels (PERSONA_UNITS_PER_CTA overrides).
+// Work units per pipeline of the split kernel (PERSONA_UNITS_PER_CTA overrides).
 int units_per_cta() {
   static const int v = [] {
     const char* e = std::getenv("PERSONA_UNITS_PER_CTA");
@@ -201,13 +146,10 @@ int units_per_cta() {
   return v;
 }
 
-int run_bgmv(int mode, int dtype, int64_t R, const CUtensorMap& tmA, const CUtensorMap& tmB, BgmvArgs a,
-             int cs, int64_t T, cudaStream_t stream) {
+int run_split(int mode, int dtype, int64_t R, const SplitMaps& maps, SplitArgs& a, cudaStream_t stream) {
   a.units_per_cta = units_per_cta();
-  const cudaError_t e =
-      cs > 0 ? launch_bgmv_cluster(mode, dtype, static_cast<int>(R), tmA, tmB, a, cs, static_cast<int>(T), stream)
-             : launch_bgmv_split(mode, dtype, static_cast<int>(R), tmA, tmB, a, 1 << 20, stream);
-  return e == cudaSuccess ? PERSONA_OK : PERSONA_ERR_CUDA;
+  return launch_bgmv_split(mode, dtype, static_cast<int>(R), maps, a, stream) == cudaSuccess ? PERSONA_OK
+                                                                                             : PERSONA_ERR_CUDA;
 }
 
 int plan_if_needed(const int32_t* slots, int64_t T, int64_t S, void* ws, int flags,
@@ -259,11 +201,11 @@ int persona_bgmv_shrink(const void* x, int64_t ldx, const void* a_pool, int64_t 
                         size_t workspace_bytes, int flags, int32_t* dev_err,
                         cudaStream_t stream) {
   if (flags & ~PERSONA_REUSE_PLAN) return PERSONA_ERR_INVALID_ARG;
-  // Ranks 8/16/32/64 with K >= 64 run the clustered kernel over a plan;
-  // any other rank runs row by row and needs no workspace.
-  const bool clustered = rank_supported(R) && K >= 64;
+  // Ranks 8/16/32/64 with K >= 64 run the split kernel over a plan; any
+  // other rank runs row by row and needs no workspace.
+  const bool planned = rank_supported(R) && K >= 64;
   int st;
-  if (clustered) {
+  if (planned) {
     st = check_common(T, S, dtype, workspace, workspace_bytes, slots);
   } else {
     st = check_common(T, S, dtype, nullptr, 0, slots);
@@ -275,23 +217,30 @@ int persona_bgmv_shrink(const void* x, int64_t ldx, const void* a_pool, int64_t 
   if (v == nullptr) return PERSONA_ERR_INVALID_ARG;
   if (!aligned16(v)) return PERSONA_ERR_ALIGNMENT;
   if (R > 4096 || T * R > kI32Max) return PERSONA_ERR_SHAPE;
-  if (!clustered) {
+  if (!planned) {
     return launch_shrink_rowwise(dtype, x, ldx, a_pool, a_slot_stride, a_row_stride, slots, v,
                                  static_cast<int>(T), static_cast<int>(K), static_cast<int>(R),
                                  static_cast<int>(S), dev_err, stream) == cudaSuccess
                ? PERSONA_OK
                : PERSONA_ERR_CUDA;
   }
-  CUtensorMap tmA, tmB;
-  std::memset(&tmB, 0, sizeof(tmB));
-  if ((st = encode_a_map(&tmA, a_pool, dtype, K, R, S, a_row_stride, a_slot_stride)) != PERSONA_OK) return st;
+  SplitMaps maps;
+  std::memset(&maps, 0, sizeof(maps));
+  if ((st = encode_a_map(&maps.a[0], a_pool, dtype, K, R, S, a_row_stride, a_slot_stride)) != PERSONA_OK) return st;
   if ((st = plan_if_needed(slots, T, S, workspace, flags, dev_err, stream)) != PERSONA_OK) return st;
-  BgmvArgs a = {};
-  const int cs = kernel_geometry(kModeShrink, T, K, 0, R, &a);
-  a.x = x; a.ldx = ldx; a.v_out = v; a.slots = slots;
-  a.plan = static_cast<const int32_t*>(workspace); a.err = dev_err;
-  a.T = static_cast<int>(T); a.K = static_cast<int>(K); a.N = 0; a.S = static_cast<int>(S);
-  return run_bgmv(kModeShrink, dtype, R, tmA, tmB, a, cs, T, stream);
+  SplitArgs a = {};
+  a.prob[0].x = x;
+  a.prob[0].ldx = ldx;
+  a.prob[0].K = static_cast<int>(K);
+  a.prob[0].n_box = 8;
+  a.num_problems = 1;
+  a.v_out = v;
+  a.slots = slots;
+  a.ws = static_cast<int32_t*>(workspace);
+  a.err = dev_err;
+  a.T = static_cast<int>(T);
+  a.S = static_cast<int>(S);
+  return run_split(kModeShrink, dtype, R, maps, a, stream);
 }
 
 int persona_bgmv_expand(const float* v, const void* b_pool, int64_t b_slot_stride,
@@ -307,16 +256,24 @@ int persona_bgmv_expand(const float* v, const void* b_pool, int64_t b_slot_strid
   if ((st = check_b(b_pool, b_slot_stride, y, ldy, N, R)) != PERSONA_OK) return st;
   if (v == nullptr) return PERSONA_ERR_INVALID_ARG;
   if (!aligned16(v)) return PERSONA_ERR_ALIGNMENT;
-  BgmvArgs a = {};
-  const int cs = kernel_geometry(kModeExpand, T, 0, N, R, &a);
-  CUtensorMap tmA, tmB;
-  std::memset(&tmA, 0, sizeof(tmA));
-  if ((st = encode_b_map(&tmB, b_pool, dtype, N, R, S, b_slot_stride, a.n_box)) != PERSONA_OK) return st;
+  SplitArgs a = {};
+  a.prob[0].y = y;
+  a.prob[0].ldy = ldy;
+  a.prob[0].N = static_cast<int>(N);
+  a.prob[0].n_box = b_box_rows(N, R);
+  SplitMaps maps;
+  std::memset(&maps, 0, sizeof(maps));
+  if ((st = encode_b_map(&maps.b[0], b_pool, dtype, N, R, S, b_slot_stride, a.prob[0].n_box)) != PERSONA_OK)
+    return st;
   if ((st = plan_if_needed(slots, T, S, workspace, flags, dev_err, stream)) != PERSONA_OK) return st;
-  a.v_in = v; a.y = y; a.ldy = ldy; a.slots = slots;
-  a.plan = static_cast<const int32_t*>(workspace); a.err = dev_err;
-  a.T = static_cast<int>(T); a.K = 0; a.N = static_cast<int>(N); a.S = static_cast<int>(S);
-  return run_bgmv(kModeExpand, dtype, R, tmA, tmB, a, cs, T, stream);
+  a.num_problems = 1;
+  a.v_in = v;
+  a.slots = slots;
+  a.ws = static_cast<int32_t*>(workspace);
+  a.err = dev_err;
+  a.T = static_cast<int>(T);
+  a.S = static_cast<int>(S);
+  return run_split(kModeExpand, dtype, R, maps, a, stream);
 }
 
 int persona_bgmv_fused(const void* x, int64_t ldx, const void* a_pool, int64_t a_slot_stride,
@@ -333,17 +290,76 @@ int persona_bgmv_fused(const void* x, int64_t ldx, const void* a_pool, int64_t a
   if ((st = check_a(x, ldx, a_pool, a_slot_stride, a_row_stride, K, R, S)) != PERSONA_OK) return st;
   if ((st = check_b(b_pool, b_slot_stride, y, ldy, N, R)) != PERSONA_OK) return st;
   if (K < 64) return PERSONA_ERR_SHAPE;
-  BgmvArgs a = {};
-  const int cs = kernel_geometry(kModeFused, T, K, N, R, &a);
-  CUtensorMap tmA, tmB;
-  if ((st = encode_a_map(&tmA, a_pool, dtype, K, R, S, a_row_stride, a_slot_stride)) != PERSONA_OK) return st;
-  if ((st = encode_b_map(&tmB, b_pool, dtype, N, R, S, b_slot_stride, a.n_box)) != PERSONA_OK) return st;
+  SplitArgs a = {};
+  SplitMaps maps;
+  std::memset(&maps, 0, sizeof(maps));
+  a.prob[0].x = x;
+  a.prob[0].ldx = ldx;
+  a.prob[0].y = y;
+  a.prob[0].ldy = ldy;
+  a.prob[0].K = static_cast<int>(K);
+  a.prob[0].N = static_cast<int>(N);
+  a.prob[0].n_box = b_box_rows(N, R);
+  if ((st = encode_a_map(&maps.a[0], a_pool, dtype, K, R, S, a_row_stride, a_slot_stride)) != PERSONA_OK) return st;
+  if ((st = encode_b_map(&maps.b[0], b_pool, dtype, N, R, S, b_slot_stride, a.prob[0].n_box)) != PERSONA_OK)
+    return st;
   if ((st = plan_if_needed(slots, T, S, workspace, flags, dev_err, stream)) != PERSONA_OK) return st;
-  a.x = x; a.ldx = ldx; a.y = y; a.ldy = ldy; a.slots = slots;
-  a.plan = static_cast<const int32_t*>(workspace); a.err = dev_err;
-  a.T = static_cast<int>(T); a.K = static_cast<int>(K); a.N = static_cast<int>(N);
+  a.num_problems = 1;
+  a.slots = slots;
+  a.ws = static_cast<int32_t*>(workspace);
+  a.err = dev_err;
+  a.T = static_cast<int>(T);
   a.S = static_cast<int>(S);
-  return run_bgmv(kModeFused, dtype, R, tmA, tmB, a, cs, T, stream);
+  return run_split(kModeFused, dtype, R, maps, a, stream);
+}
+
+size_t persona_bgmv_multi_workspace_size(int64_t T, int num_problems) {
+  if (T < 0 || num_problems < 1 || num_problems > PERSONA_MAX_PROBLEMS) return 0;
+  return bgmv_ws_bytes(T, num_problems);
+}
+
+int persona_bgmv_fused_multi(const persona_bgmv_problem* problems, int num_problems, const int32_t* slots,
+                             int64_t T, int64_t R, int64_t S, int dtype, void* workspace, size_t workspace_bytes,
+                             int flags, int32_t* dev_err, cudaStream_t stream) {
+  if (flags & ~PERSONA_REUSE_PLAN) return PERSONA_ERR_INVALID_ARG;
+  if (problems == nullptr || num_problems < 1 || num_problems > PERSONA_MAX_PROBLEMS) return PERSONA_ERR_INVALID_ARG;
+  int st = check_common(T, S, dtype, workspace, workspace_bytes, slots);
+  if (st != PERSONA_OK) return st;
+  if (T > 0 && workspace_bytes < bgmv_ws_bytes(T, num_problems)) return PERSONA_ERR_WORKSPACE;
+  if (!rank_supported(R)) return PERSONA_ERR_RANK;
+  SplitArgs a = {};
+  SplitMaps maps;
+  std::memset(&maps, 0, sizeof(maps));
+  for (int p = 0; p < num_problems; ++p) {
+    const persona_bgmv_problem& q = problems[p];
+    if ((st = check_a(q.x, q.ldx, q.a_pool, q.a_slot_stride, q.a_row_stride, q.K, R, S)) != PERSONA_OK) return st;
+    if ((st = check_b(q.b_pool, q.b_slot_stride, q.y, q.ldy, q.N, R)) != PERSONA_OK) return st;
+    if (q.K < 64) return PERSONA_ERR_SHAPE;
+    a.prob[p].x = q.x;
+    a.prob[p].ldx = q.ldx;
+    a.prob[p].y = q.y;
+    a.prob[p].ldy = q.ldy;
+    a.prob[p].K = static_cast<int>(q.K);
+    a.prob[p].N = static_cast<int>(q.N);
+    a.prob[p].n_box = b_box_rows(q.N, R);
+  }
+  if (T == 0) return PERSONA_OK;
+  for (int p = 0; p < num_problems; ++p) {
+    const persona_bgmv_problem& q = problems[p];
+    if ((st = encode_a_map(&maps.a[p], q.a_pool, dtype, q.K, R, S, q.a_row_stride, q.a_slot_stride)) != PERSONA_OK)
+      return st;
+    if ((st = encode_b_map(&maps.b[p], q.b_pool, dtype, q.N, R, S, q.b_slot_stride, a.prob[p].n_box)) !=
+        PERSONA_OK)
+      return st;
+  }
+  if ((st = plan_if_needed(slots, T, S, workspace, flags, dev_err, stream)) != PERSONA_OK) return st;
+  a.num_problems = num_problems;
+  a.slots = slots;
+  a.ws = static_cast<int32_t*>(workspace);
+  a.err = dev_err;
+  a.T = static_cast<int>(T);
+  a.S = static_cast<int>(S);
+  return run_split(kModeFused, dtype, R, maps, a, stream);
 }
 
 int persona_gemv_fp16(const void* x, const void* W, void* y, int64_t K, int64_t N,
@@ -381,7 +397,7 @@ int sgmv_prepare(const int32_t* seg_indptr, const int32_t* seg_slots, int64_t ns
 
 namespace {
 // Tensor-core path: ranks 16 / 32, K a multiple of 64, N a multiple of 128.
-// PERSONA_SGMV_TENSOR_CORES=0 selects the clustered path instead.
+// PERSONA_SGMV_TENSOR_CORES=0 selects the BGMV split path instead.
 bool sgmv_tc_eligible(int64_t R, int64_t K, int64_t N, bool need_k, bool need_n) {
   static const bool enabled = [] {
     const char* e = std::getenv("PERSONA_SGMV_TENSOR_CORES");

@@ -4,7 +4,7 @@
 // The array is a file-scope __device__ variable, one copy per device, loaded
 // with the library's device code.  Its device address is looked up once per
 // device (cudaGetSymbolAddress with that device current) and then handed to
-// the same plan + clustered kernels persona_bgmv_fused runs.  Nothing here
+// the same plan + split kernels persona_bgmv_fused runs.  Nothing here
 // calls cudaMalloc / cudaFree or any allocating routine.
 //
 // The plan kernel rewrites every field the fused kernel reads (header, row

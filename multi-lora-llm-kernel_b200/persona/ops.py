@@ -16,6 +16,8 @@ New in this build:
 
 * ``bgmv_fused`` -- shrink->expand in one launch, rank-R intermediate kept on
   chip (the reference's fused kernel is a stub, ``docs/BENCHMARKS.md:238``).
+* ``bgmv_fused_multi`` -- the fused op for up to 8 projections of a layer
+  that share the slots, in one launch.
 * ``bgmv_plan`` -- groups a batch's rows by adapter slot once on the device;
   pass the result as ``plan=`` to every shrink/expand/fused call that uses
   the same slots (a decode step's 7 projections x 32 layers share one).
@@ -105,6 +107,20 @@ def bgmv_fused(x: torch.Tensor, a_pool: torch.Tensor, b_pool: torch.Tensor, slot
     else:
         torch.ops.persona.bgmv_fused_with_plan(x, a_pool, b_pool, slots, plan, y)
     return y
+
+
+def bgmv_fused_multi(xs, a_pools, b_pools, slots: torch.Tensor, ys,
+                     plan: Optional[torch.Tensor] = None):
+    """``ys[i] += B_i[s] @ (A_i[s] @ xs[i])`` for up to 8 projections that
+    share ``slots`` (one decoder layer), in one launch; returns ``ys``.
+
+    Each result equals ``bgmv_fused`` on that projection.  All pools share
+    the rank and the slot count.
+    """
+    xs, a_pools, b_pools, ys = list(xs), list(a_pools), list(b_pools), list(ys)
+    _require_cuda("bgmv_fused_multi", *xs, *a_pools, *b_pools, slots, *ys)
+    torch.ops.persona.bgmv_fused_multi(xs, a_pools, b_pools, slots, ys, plan)
+    return ys
 
 
 def sgmv_shrink(x: torch.Tensor, a_pool: torch.Tensor, seg_indptr: torch.Tensor,

@@ -27,6 +27,8 @@ SIGNATURES = {
     "persona_bgmv_fused": (_i32, [_p, _i64, _p, _i64, _i64, _p, _i64, _p, _p, _i64, _i64, _i64, _i64,
                                   _i64, _i64, _i32, _p, _sz, _i32, _p, _p]),
     "persona_gemv_fp16": (_i32, [_p, _p, _p, _i64, _i64, _p]),
+    "persona_bgmv_multi_workspace_size": (_sz, [_i64, _i32]),
+    "persona_bgmv_fused_multi": (_i32, [_p, _i32, _p, _i64, _i64, _i64, _i32, _p, _sz, _i32, _p, _p]),
     "persona_bgmv_fused_noalloc": (_i32, [_p, _i64, _p, _i64, _i64, _p, _i64, _p, _p, _i64, _i64, _i64, _i64,
                                           _i64, _i64, _i32, _p, _p]),
     "persona_sgmv_workspace_size": (_sz, [_i64]),
@@ -37,6 +39,12 @@ SIGNATURES = {
     "persona_sgmv_fused": (_i32, [_p, _i64, _p, _i64, _i64, _p, _i64, _p, _p, _i64, _p, _i64, _i64, _i64, _i64,
                                   _i64, _i64, _i32, _p, _sz, _p, _p]),
 }
+
+
+class Problem(ctypes.Structure):
+    """persona_bgmv_problem (include/persona_bgmv.h)."""
+    _fields_ = [("x", _p), ("ldx", _i64), ("a_pool", _p), ("a_slot_stride", _i64), ("a_row_stride", _i64),
+                ("b_pool", _p), ("b_slot_stride", _i64), ("y", _p), ("ldy", _i64), ("K", _i64), ("N", _i64)]
 
 
 def declared_symbols():

@@ -54,12 +54,19 @@ def test_workspace_size_matches_layout(built):
 
     for T in (0, 1, 8, 512, 16384):
         tp = (T + 3) // 4 * 4
-        plan = 32 + 4 * tp + 16 * tp              # header, perm, items
-        sync = a256(plan)                          # counters, per-item state
-        vfinal = a256(sync + 4 * (16 + 2 * tp))    # v per plan position, 64 floats
-        parts = a256(vfinal + tp * 64 * 4)         # 1024 partial-v slots of 16 x 64 floats
-        assert lib.persona_bgmv_workspace_size(T) == parts + 1024 * 16 * 64 * 4
-        assert lib.persona_sgmv_workspace_size(T) == parts + 1024 * 16 * 64 * 4 + 4 * tp
+        plan = 32 + 4 * tp + 16 * tp                  # header, perm, items
+        sync = a256(plan)                              # counters, per-item state of 8 problems
+        vfinal = a256(sync + 4 * (16 + 2 * 8 * tp))    # v per problem and plan position, 64 floats
+
+        def total(problems):
+            parts = a256(vfinal + problems * tp * 64 * 4)  # 1024 partial-v slots of 16 x 64 floats
+            return parts + 1024 * 16 * 64 * 4
+
+        assert lib.persona_bgmv_workspace_size(T) == total(1)
+        assert lib.persona_sgmv_workspace_size(T) == total(1) + 4 * tp
+        for p in (1, 3, 8):
+            assert lib.persona_bgmv_multi_workspace_size(T, p) == total(p)
+        assert lib.persona_bgmv_multi_workspace_size(T, 9) == 0
 
 
 def test_host_validation_codes(built):
