@@ -112,9 +112,8 @@ __global__ void __launch_bounds__(THREADS)
     ScanI(tmp.scan).InclusiveScan(seg_start, seg_start, cub::Max());
     __syncthreads();
     // Items heaviest first: full items (rows_per_item rows) of every slot in
-    // slot order, then the remainder items in slot order.  The BGMV kernels
-    // deal items to clusters in serpentine rounds, so the heavy items are
-    // spread over the clusters and start first.
+    // slot order, then the remainder items in slot order, so that the split
+    // kernel's claim order starts with the items that carry the most rows.
     int full[IPT], part[IPT], cntv[IPT];
 #pragma unroll
     for (int j = 0; j < IPT; ++j) {

@@ -1,6 +1,6 @@
 // Device helpers shared by the B200 (sm_100a) BGMV / SGMV kernels:
 // 16-bit <-> fp32 conversion, mbarriers with bounded waits, TMA tile loads,
-// thread-block-cluster addressing (DSMEM) and the error word.
+// bulk copies, warp-MMA wrappers and the error word.
 //
 // Every wait in this file is bounded by a clock budget.  A wait that runs out
 // sets PERSONA_DEV_ERR_TIMEOUT in the caller's error word and returns, so a
@@ -75,9 +75,6 @@ __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
                : "memory");
 }
 
-__device__ __forceinline__ void fence_mbar_init_cluster() {
-  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-}
 
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(
@@ -103,28 +100,7 @@ __device__ __forceinline__ void mbar_arrive_relaxed(uint64_t* bar) {
                : "memory");
 }
 
-// 16-byte asynchronous store into CTA `rank`'s shared memory (same offset as
-// `dst` here) that completes `bytes` of the transaction count of the mbarrier
-// at `bar`'s offset in that CTA: the receiver learns the data has landed by
-// waiting on its own barrier, with no release fence on the sender.
-__device__ __forceinline__ void st_async_v4(const void* dst, const uint64_t* bar, uint32_t rank, float4 v) {
-  asm volatile(
-      "{\n\t.reg .b32 ra, rb;\n\tmapa.shared::cluster.u32 ra, %0, %1;\n\tmapa.shared::cluster.u32 rb, %2, %1;\n\t"
-      "st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [ra], {%3, %4, %5, %6}, [rb];\n\t}" ::"r"(
-          smem_u32(dst)),
-      "r"(rank), "r"(smem_u32(bar)), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
-      : "memory");
-}
 
-// Arrive (release, cluster scope) on the mbarrier at the same smem offset in
-// CTA `cta_rank` of this cluster.
-__device__ __forceinline__ void mbar_arrive_remote(uint64_t* bar, uint32_t cta_rank) {
-  asm volatile(
-      "{\n\t.reg .b32 ra;\n\tmapa.shared::cluster.u32 ra, %0, %1;\n\t"
-      "mbarrier.arrive.release.cluster.shared::cluster.b64 _, [ra];\n\t}" ::"r"(smem_u32(bar)),
-      "r"(cta_rank)
-      : "memory");
-}
 
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
@@ -137,25 +113,14 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], "
-      "%2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
 
 // Bounded wait for phase `parity` of `bar` to complete.  Returns false (and
 // flags the error word) if the budget ran out.
-template <bool kClusterScope = false>
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int32_t* err) {
-  if (kClusterScope ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity)) return true;
+  if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
   while (true) {
-    if (kClusterScope ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity))
+    if (mbar_try_wait(bar, parity))
       return true;
     if (clock64() - t0 > kWaitBudgetCycles) {
       raise_error(err, PERSONA_DEV_ERR_TIMEOUT);
@@ -206,58 +171,6 @@ __device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes
                : "memory");
 }
 
-// ------------------------------------------------------------- cluster ---
-
-__device__ __forceinline__ uint32_t cluster_ctarank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-__device__ __forceinline__ uint32_t cluster_nctarank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r));
-  return r;
-}
-__device__ __forceinline__ uint32_t cluster_id_x() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
-  return r;
-}
-__device__ __forceinline__ uint32_t nclusters_x() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
-  return r;
-}
-
-// All threads of all CTAs in the cluster (hardware barrier, no spinning).
-__device__ __forceinline__ void cluster_sync_all() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
-                   : "memory");
-}
-
-__device__ __forceinline__ void fence_acq_rel_cluster() {
-  asm volatile("fence.acq_rel.cluster;" ::: "memory");
-}
-
-// Address of `p` (this CTA's smem) inside CTA `rank` of the cluster.
-__device__ __forceinline__ uint32_t mapa(const void* p, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
-  return r;
-}
-
-__device__ __forceinline__ float2 ld_dsmem_f2(uint32_t addr) {
-  float2 v;
-  asm volatile("ld.shared::cluster.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(addr)
-               : "memory");
-  return v;
-}
-
-__device__ __forceinline__ void st_dsmem_f2(uint32_t addr, float2 v) {
-  asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(addr), "f"(v.x), "f"(v.y)
-               : "memory");
-}
-
 // Named barrier over `nthreads` threads (a multiple of 32), id != 0.
 __device__ __forceinline__ void named_sync(uint32_t id, uint32_t nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
@@ -279,19 +192,7 @@ __device__ __forceinline__ uint32_t lds32(uint32_t addr) {
   return v;
 }
 
-__device__ __forceinline__ float2 lds64f(uint32_t addr) {
-  float2 v;
-  asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(addr));
-  return v;
-}
 
-__device__ __forceinline__ float4 lds128f(uint32_t addr) {
-  float4 v;
-  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
-               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-               : "r"(addr));
-  return v;
-}
 
 // ldmatrix: four (x4) or two (x2) 8x8 16-bit matrices from shared memory.
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {

@@ -1,5 +1,5 @@
-// Small kernels outside the clustered hot path:
-// * a row-by-row shrink for ranks the clustered kernel does not specialise
+// Small kernels outside the split hot path:
+// * a row-by-row shrink for ranks the split kernel does not specialise
 //   (the reference's shrink accepts any R: csrc/bgmv_shrink.cu:56-58),
 // * the warm-up fp16 GEMV kept behind torch.ops.persona.gemv_fp16
 //   (reference csrc/gemv_fp16.cu:9-31: y[n] = W[n, :] . x, fp32 accumulate).
