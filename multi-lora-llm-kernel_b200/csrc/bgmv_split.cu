@@ -8,11 +8,11 @@
 // For each problem its shrink is cut into nks K-slices and its expand into
 // nes N-slices; the unit list is [all shrink slices, problem by problem,
 // item by item] then [all expand slices, same order].  Slice counts are
-// chosen on the device from the item count so that each pipeline gets about
-// units_per_cta units: a decode batch of 8 adapters spreads over the whole
-// GPU, a batch of ~150 adapters leaves no pipeline streaming a second whole
-// adapter while others idle, and the seven projections of a layer fill each
-// other's tails.
+// chosen on the device from the item count so that each pipeline gets 8
+// (few items) to 24 (many items) units: a decode batch of 8 adapters
+// spreads over the whole GPU, a batch of ~150 adapters leaves no pipeline
+// streaming a second whole adapter while others idle, and the seven
+// projections of a layer fill each other's tails.
 //
 // Scheduling.  Persistent pipelines claim units in list order from a
 // device-wide counter.  Every shrink unit precedes every expand unit in claim
@@ -49,7 +49,9 @@ namespace persona {
 namespace {
 
 constexpr int kUnitRing = 4;
-constexpr int kUnitsPerCta = 8;
+constexpr int kUnitsPerCta = 8;       // units per pipeline, few items
+constexpr int kUnitsPerCtaMany = 24;  // units per pipeline, kManyItems items or more
+constexpr int kManyItems = 64;
 enum : int { kUnitEnd = 0, kUnitShrink = 1, kUnitExpand = 2 };
 
 constexpr int kGroups = 2;
@@ -146,7 +148,10 @@ __device__ void plan_units(SplitShared& sh, const SplitArgs& a, int n_items, int
                            bool shrink, bool expand) {
   const int P = a.num_problems;
   const int items = n_items > 0 ? n_items : 1;
-  const int upc = a.units_per_cta > 0 ? a.units_per_cta : kUnitsPerCta;
+  // Many items (large batches): small units, so the tail stays short.  Few
+  // items (decode): fewer, larger units, so the latency chain shrink slice ->
+  // finisher -> expand slice has fewer links per item.
+  const int upc = a.units_per_cta > 0 ? a.units_per_cta : n_items >= kManyItems ? kUnitsPerCtaMany : kUnitsPerCta;
   int work = 0;
   for (int p = 0; p < P; ++p) {
     ProbGeom& g = sh.geom[p];
@@ -315,11 +320,37 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
       if (kDoShrink) tma_prefetch_desc(&maps.a[lane]);
       if (kDoExpand) tma_prefetch_desc(&maps.b[lane]);
     }
-    // Claims run two units ahead: the atomic for unit j+2 is issued while
-    // unit j streams, and its result is first read one unit later, so the
-    // round trip to L2 never stalls the loads.
+    // Claims run three units ahead and the L2 prefetch two: while unit j
+    // streams, unit j+2 is prefetched and the atomic for unit j+3 is issued;
+    // its result is first read one unit later, so the round trip to L2 never
+    // stalls the loads, and a unit's data has had a whole unit's time to
+    // reach L2 before its TMA loads are issued.  (A prefetch window of a few
+    // stages ahead of the loads, tried instead, streamed 25% slower.)
     auto claim_issue = [&]() -> int { return lane == 0 ? atomicAdd(&wv.sync[kSyncQueue], 1) : 0; };
     auto claim_read = [&](int pending) -> int { return __shfl_sync(0xffffffffu, pending, 0); };
+    // L2 prefetch of [lo, hi) of a shrink (k range) or expand (n range) unit.
+    auto prefetch_range = [&](const Dec& dd, int slot, int cnt, int rrow, int lo, int hi) {
+      if (lo >= hi) return;
+      const SplitProblem& np = args.prob[dd.prob];
+      if (dd.kind == kUnitShrink) {
+        for (int k0 = lo + 64 * lane; k0 < hi; k0 += 64 * 32) tma_prefetch_3d(&maps.a[dd.prob], k0, 0, slot);
+        if (lane < cnt)
+          bulk_prefetch_l2(static_cast<const uint16_t*>(np.x) + static_cast<int64_t>(rrow) * np.ldx + lo,
+                           static_cast<uint32_t>(hi - lo) * 2u);
+      } else {
+        for (int n0 = lo + np.n_box * lane; n0 < hi; n0 += np.n_box * 32) tma_prefetch_3d(&maps.b[dd.prob], 0, n0, slot);
+        if (lane < cnt)
+          bulk_prefetch_l2(static_cast<const uint16_t*>(np.y) + static_cast<int64_t>(rrow) * np.ldy + lo,
+                           static_cast<uint32_t>(hi - lo) * 2u);
+      }
+    };
+    auto prefetch_unit = [&](int uu) {
+      const Dec dn = decode(uu);
+      if (dn.kind == kUnitEnd) return;
+      const int4 nit = pv.items[dn.item];
+      const int nrow = lane < nit.z ? pv.perm[nit.y + lane] : 0;
+      prefetch_range(dn, nit.x, nit.z, nrow, dn.lo, dn.hi);
+    };
     uint32_t g = 0;
     auto claim_slot = [&](uint32_t bytes) -> int {
       const int s = static_cast<int>(g % kSlots);
@@ -331,7 +362,10 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
       return s;
     };
     int u = claim_read(claim_issue());
-    int pending = claim_issue();
+    int u_next = claim_read(claim_issue());
+    if (u < units) prefetch_unit(u);
+    if (u_next < units) prefetch_unit(u_next);
+    int pending = u_next < units ? claim_issue() : 0;
     for (int j = 0;; ++j) {
       const Dec d = decode(u);
       const int iq = j % kUnitRing;
@@ -358,28 +392,10 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
       if (lane == 0) mbar_arrive(&sm.ufull[iq]);
       if (d.kind == kUnitEnd) break;
 
-      // The next unit is known; start pulling its data into L2 so that its
-      // loads hit L2 and more bytes are in flight than the ring holds.
-      const int un = claim_read(pending);
-      pending = un < units ? claim_issue() : 0;
-      const Dec dn = decode(un);
-      if (dn.kind != kUnitEnd) {
-        const int4 nit = pv.items[dn.item];
-        const int nrow = lane < nit.z ? pv.perm[nit.y + lane] : 0;
-        const SplitProblem& np = args.prob[dn.prob];
-        if (dn.kind == kUnitShrink) {
-          for (int k0 = dn.lo + 64 * lane; k0 < dn.hi; k0 += 64 * 32) tma_prefetch_3d(&maps.a[dn.prob], k0, 0, nit.x);
-          if (lane < nit.z)
-            bulk_prefetch_l2(static_cast<const uint16_t*>(np.x) + static_cast<int64_t>(nrow) * np.ldx + dn.lo,
-                             static_cast<uint32_t>(dn.hi - dn.lo) * 2u);
-        } else {
-          for (int n0 = dn.lo + np.n_box * lane; n0 < dn.hi; n0 += np.n_box * 32)
-            tma_prefetch_3d(&maps.b[dn.prob], 0, n0, nit.x);
-          if (lane < nit.z)
-            bulk_prefetch_l2(static_cast<const uint16_t*>(np.y) + static_cast<int64_t>(nrow) * np.ldy + dn.lo,
-                             static_cast<uint32_t>(dn.hi - dn.lo) * 2u);
-        }
-      }
+      // Unit j+2 becomes known: pull its data into L2 now.
+      const int u_after = u_next < units ? claim_read(pending) : units;
+      pending = u_after < units ? claim_issue() : 0;
+      if (u_after < units) prefetch_unit(u_after);
 
       const int slot = it.x, c = it.z;
       const SplitProblem& pr = args.prob[d.prob];
@@ -423,7 +439,8 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
           ++g;
         }
       }
-      u = un;
+      u = u_next;
+      u_next = u_after;
     }
     __syncwarp();
   } else if (warp == kMmaWarp) {
