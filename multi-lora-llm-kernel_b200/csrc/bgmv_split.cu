@@ -31,8 +31,8 @@
 //
 // Inside a CTA.  Kernels that allocate tensor memory run one CTA per SM, so
 // each CTA carries kGroups independent pipelines of six warps: a producer
-// warp (TMA boxes of A / B, 1-D bulk copies of the x / y / v rows, L2
-// prefetch of the next unit) feeding a 4-slot ring, four consumer warps that
+// warp (TMA boxes of A / B, 1-D bulk copies of the x / y / v rows) feeding a
+// 4-slot ring, four consumer warps that
 // run the shrink stages on the 16-row warp-MMA tiles of bgmv_stages.cuh, and
 // an MMA warp.  For ranks 16 / 32 / 64 the expand runs on the tensor cores:
 // the item's rows are the N = 16 side of a tcgen05 MMA whose M = 128 side is
@@ -43,6 +43,7 @@
 // and stores.  Rank 8 keeps the warp-MMA expand.
 #include "bgmv_stages.cuh"
 #include "tcgen05.cuh"
+
 
 namespace persona {
 
@@ -320,37 +321,15 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
       if (kDoShrink) tma_prefetch_desc(&maps.a[lane]);
       if (kDoExpand) tma_prefetch_desc(&maps.b[lane]);
     }
-    // Claims run three units ahead and the L2 prefetch two: while unit j
-    // streams, unit j+2 is prefetched and the atomic for unit j+3 is issued;
-    // its result is first read one unit later, so the round trip to L2 never
-    // stalls the loads, and a unit's data has had a whole unit's time to
-    // reach L2 before its TMA loads are issued.  (A prefetch window of a few
-    // stages ahead of the loads, tried instead, streamed 25% slower.)
+    // Claims run two units ahead: the atomic for unit j+2 is issued while
+    // unit j streams and its result is first read one unit later, so the
+    // round trip to L2 never stalls the loads.  The kernel issues no L2
+    // prefetch: with the whole GPU streaming, prefetched lines were evicted
+    // before use and prefetching a unit ahead cost up to 25% of the
+    // throughput (measured: 3.53 TB/s with whole units two ahead, 4.33 with
+    // six stages, 4.75 with none).
     auto claim_issue = [&]() -> int { return lane == 0 ? atomicAdd(&wv.sync[kSyncQueue], 1) : 0; };
     auto claim_read = [&](int pending) -> int { return __shfl_sync(0xffffffffu, pending, 0); };
-    // L2 prefetch of [lo, hi) of a shrink (k range) or expand (n range) unit.
-    auto prefetch_range = [&](const Dec& dd, int slot, int cnt, int rrow, int lo, int hi) {
-      if (lo >= hi) return;
-      const SplitProblem& np = args.prob[dd.prob];
-      if (dd.kind == kUnitShrink) {
-        for (int k0 = lo + 64 * lane; k0 < hi; k0 += 64 * 32) tma_prefetch_3d(&maps.a[dd.prob], k0, 0, slot);
-        if (lane < cnt)
-          bulk_prefetch_l2(static_cast<const uint16_t*>(np.x) + static_cast<int64_t>(rrow) * np.ldx + lo,
-                           static_cast<uint32_t>(hi - lo) * 2u);
-      } else {
-        for (int n0 = lo + np.n_box * lane; n0 < hi; n0 += np.n_box * 32) tma_prefetch_3d(&maps.b[dd.prob], 0, n0, slot);
-        if (lane < cnt)
-          bulk_prefetch_l2(static_cast<const uint16_t*>(np.y) + static_cast<int64_t>(rrow) * np.ldy + lo,
-                           static_cast<uint32_t>(hi - lo) * 2u);
-      }
-    };
-    auto prefetch_unit = [&](int uu) {
-      const Dec dn = decode(uu);
-      if (dn.kind == kUnitEnd) return;
-      const int4 nit = pv.items[dn.item];
-      const int nrow = lane < nit.z ? pv.perm[nit.y + lane] : 0;
-      prefetch_range(dn, nit.x, nit.z, nrow, dn.lo, dn.hi);
-    };
     uint32_t g = 0;
     auto claim_slot = [&](uint32_t bytes) -> int {
       const int s = static_cast<int>(g % kSlots);
@@ -362,10 +341,7 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
       return s;
     };
     int u = claim_read(claim_issue());
-    int u_next = claim_read(claim_issue());
-    if (u < units) prefetch_unit(u);
-    if (u_next < units) prefetch_unit(u_next);
-    int pending = u_next < units ? claim_issue() : 0;
+    int pending = u < units ? claim_issue() : 0;
     for (int j = 0;; ++j) {
       const Dec d = decode(u);
       const int iq = j % kUnitRing;
@@ -392,10 +368,9 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
       if (lane == 0) mbar_arrive(&sm.ufull[iq]);
       if (d.kind == kUnitEnd) break;
 
-      // Unit j+2 becomes known: pull its data into L2 now.
-      const int u_after = u_next < units ? claim_read(pending) : units;
-      pending = u_after < units ? claim_issue() : 0;
-      if (u_after < units) prefetch_unit(u_after);
+      // The next unit's claim has returned by now; issue the one after it.
+      const int u_next = claim_read(pending);
+      pending = u_next < units ? claim_issue() : 0;
 
       const int slot = it.x, c = it.z;
       const SplitProblem& pr = args.prob[d.prob];
@@ -440,7 +415,6 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
         }
       }
       u = u_next;
-      u_next = u_after;
     }
     __syncwarp();
   } else if (warp == kMmaWarp) {
