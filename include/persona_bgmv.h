@@ -194,6 +194,34 @@ int persona_bgmv_fused_noalloc(const void* x, int64_t ldx, const void* a_pool, i
                                int64_t N, int64_t R, int64_t S, int dtype, int32_t* dev_err,
                                cudaStream_t stream);
 
+/* ---- tensor-parallel segmented fused, one kernel with its exchange -------
+ * No reference counterpart (the reference is single-GPU).  Rank r of a group
+ * computes columns [n0, n1) of y += B[s] @ (A[s] @ x) for a segmented batch
+ * (same arguments as persona_sgmv_fused; b_pool and y cover all N columns)
+ * and writes every finished tile both to its own y and, over NVLink, to the
+ * y of every other rank: peer_ys[0..num_peers) are those ranks' y buffers
+ * mapped into this process (persona_ipc_import), same shape and ldy.  After
+ * the launch and a cross-rank barrier (any collective on this stream) every
+ * rank holds the full updated y.  Tensor-core shapes only: R in {16, 32},
+ * K % 64 == 0, N % 128 == 0, n0 and n1 multiples of 128; at most
+ * PERSONA_MAX_TP_PEERS peers.  The ranks' y must hold the same values before
+ * the call (rows outside every segment are not written).                   */
+#define PERSONA_MAX_TP_PEERS 7
+int persona_sgmv_fused_tp(const void* x, int64_t ldx, const void* a_pool, int64_t a_slot_stride,
+                          int64_t a_row_stride, const void* b_pool, int64_t b_slot_stride, const int32_t* seg_indptr,
+                          const int32_t* seg_slots, int64_t num_segments, void* y, int64_t ldy, void* const* peer_ys,
+                          int num_peers, int64_t n0, int64_t n1, int64_t T, int64_t K, int64_t N, int64_t R,
+                          int64_t S, int dtype, void* workspace, size_t workspace_bytes, int32_t* dev_err,
+                          cudaStream_t stream);
+
+/* Cross-process mapping of a device buffer (CUDA IPC) for the peer_ys above:
+ * export a 64-byte handle plus the buffer's offset in its allocation on the
+ * owning rank, import it on the others (returns the buffer pointer and the
+ * mapping base to close later).                                            */
+int persona_ipc_export(const void* ptr, void* handle, size_t* offset);
+int persona_ipc_import(const void* handle, size_t offset, void** ptr, void** base);
+int persona_ipc_close(void* base);
+
 /* ---- warm-up GEMV ---------------------------------------------------------
  * y[n] = W[n, :] @ x (fp16, fp32 accumulate).  Replaces
  * persona::gemv_fp16_cuda (csrc/gemv_fp16.cu:33-50), kept so that

@@ -53,14 +53,18 @@ cudaError_t launch_bgmv_split(int mode, int dtype, int R, const SplitMaps& maps,
                               cudaStream_t st);
 
 // Segmented tensor-core kernels (sgmv_tcgen05.cu).
+constexpr int kMaxTpPeers = 7;  // other ranks a tensor-parallel launch writes to
 struct SgmvTcArgs {
   const int32_t* plan;  // segment plan, 128-row items, identity perm
   const float* v_in;    // expand only: [T, R]
   float* v_out;         // shrink only: [T, R]
-  uint16_t* y;          // [T, N] row stride ldy (plain stores of short items)
+  uint16_t* y;          // [T, N_total] row stride ldy (plain stores of short items)
   int64_t ldy;
   int32_t* err;
-  int T, K, N;
+  int T, K, N;  // N: output columns this launch computes, from column n0 of y and B
+  int n0;
+  int num_peers;                   // tensor parallel: other ranks' y (same layout as y)
+  uint16_t* peers[kMaxTpPeers];    // that receive every finished tile
 };
 cudaError_t launch_sgmv_tc(int mode, int dtype, int R, const CUtensorMap& tx, const CUtensorMap& ta,
                            const CUtensorMap& tb, const CUtensorMap& ty, const SgmvTcArgs& a, int max_items,

@@ -495,7 +495,77 @@ TORCH_LIBRARY_IMPL(persona, CUDA, m) {
   m.impl("sgmv_fused", &sgmv_fused_op);
 }
 
+namespace {
+// Tensor-parallel segmented fused op (persona_sgmv_fused_tp); `peers` are the
+// other ranks' y buffers mapped into this process, as integers.
+void sgmv_fused_tp_op(const at::Tensor& x, const at::Tensor& a_pool, const at::Tensor& b_pool,
+                      const at::Tensor& indptr, const at::Tensor& seg_slots, at::Tensor& y,
+                      const std::vector<int64_t>& peers, int64_t n0, int64_t n1) {
+  const char* op = "sgmv_fused_tp";
+  check_segments(indptr, seg_slots, op);
+  TORCH_CHECK(x.is_cuda() && a_pool.is_cuda() && b_pool.is_cuda() && y.is_cuda(), op, ": all tensors must be CUDA");
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1 && y.dim() == 2 && y.stride(1) == 1, op,
+              ": tensors must be contiguous");
+  check_pool_a(a_pool, op);
+  check_pool_b(b_pool, op);
+  const int64_t T = x.size(0), K = x.size(1), S = a_pool.size(0), R = a_pool.size(1), N = b_pool.size(1);
+  TORCH_CHECK(a_pool.size(2) == K && b_pool.size(0) == S && b_pool.size(2) == R, op, ": pool shape mismatch");
+  TORCH_CHECK(y.size(0) == T && y.size(1) == N, op, ": y shape mismatch");
+  TORCH_CHECK(peers.size() <= PERSONA_MAX_TP_PEERS, op, ": too many peers");
+  const int dt = dtype_code(x, op);
+  TORCH_CHECK(a_pool.scalar_type() == x.scalar_type() && b_pool.scalar_type() == x.scalar_type() &&
+                  y.scalar_type() == x.scalar_type(),
+              op, ": dtype mismatch");
+  const at::cuda::OptionalCUDAGuard guard(x.device());
+  const int dev = x.get_device();
+  raise_pending(dev, op);
+  if (T == 0) return;
+  void* pp[PERSONA_MAX_TP_PEERS];
+  for (size_t i = 0; i < peers.size(); ++i) pp[i] = reinterpret_cast<void*>(peers[i]);
+  at::Tensor ws = sgmv_workspace(T, x);
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  check_status(persona_sgmv_fused_tp(x.data_ptr(), row_stride(x), a_pool.data_ptr(), a_pool.stride(0),
+                                     a_pool.stride(1), b_pool.data_ptr(), b_pool.stride(0),
+                                     indptr.data_ptr<int32_t>(), seg_slots.data_ptr<int32_t>(), seg_slots.size(0),
+                                     y.data_ptr(), row_stride(y), pp, static_cast<int>(peers.size()), n0, n1, T, K,
+                                     N, R, S, dt, ws.data_ptr(), ws.numel(), error_word_device(dev), stream),
+               op);
+  after_launch(dev, op, stream);
+}
+}  // namespace
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.def("sgmv_fused_tp", &sgmv_fused_tp_op,
+        "Tensor-parallel segmented fused LoRA: columns [n0, n1) of y, every finished tile also stored into the "
+        "peers' y (pointers from ipc_import).");
+  m.def(
+      "ipc_export",
+      [](const at::Tensor& t) {
+        TORCH_CHECK(t.is_cuda(), "ipc_export: CUDA tensor expected");
+        const at::cuda::OptionalCUDAGuard guard(t.device());
+        char handle[64];
+        size_t offset = 0;
+        check_status(persona_ipc_export(t.data_ptr(), handle, &offset), "ipc_export");
+        return pybind11::make_tuple(pybind11::bytes(handle, sizeof(handle)), static_cast<int64_t>(offset));
+      },
+      "64-byte CUDA IPC handle of the allocation holding `t`, and t's offset in it.");
+  m.def(
+      "ipc_import",
+      [](const std::string& handle, int64_t offset, int device) {
+        TORCH_CHECK(handle.size() == 64, "ipc_import: 64-byte handle expected");
+        const at::cuda::OptionalCUDAGuard guard(at::Device(at::kCUDA, device));
+        void* ptr = nullptr;
+        void* base = nullptr;
+        check_status(persona_ipc_import(handle.data(), static_cast<size_t>(offset), &ptr, &base), "ipc_import");
+        return pybind11::make_tuple(reinterpret_cast<int64_t>(ptr), reinterpret_cast<int64_t>(base));
+      },
+      "Map another process's buffer: returns (pointer, mapping base).");
+  m.def(
+      "ipc_close", [](int64_t base, int device) {
+        const at::cuda::OptionalCUDAGuard guard(at::Device(at::kCUDA, device));
+        check_status(persona_ipc_close(reinterpret_cast<void*>(base)), "ipc_close");
+      },
+      "Unmap a buffer mapped by ipc_import (its mapping base).");
   m.def("noop", []() { return 0; });
   m.def("abi_version", []() { return persona_abi_version(); });
   m.def("workspace_size", [](int64_t T) { return persona_bgmv_workspace_size(T); });

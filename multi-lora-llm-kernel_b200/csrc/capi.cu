@@ -413,9 +413,15 @@ int sgmv_tc_run(int mode, const void* x, int64_t ldx, const void* a_pool, int64_
                 int64_t a_row_stride, const void* b_pool, int64_t b_slot_stride, const int32_t* seg_indptr,
                 const int32_t* seg_slots, int64_t nseg, const float* v_in, float* v_out, void* y, int64_t ldy,
                 int64_t T, int64_t K, int64_t N, int64_t R, int64_t S, int dtype, void* workspace,
-                size_t workspace_bytes, int32_t* dev_err, cudaStream_t stream) {
+                size_t workspace_bytes, int32_t* dev_err, cudaStream_t stream, int64_t n0 = 0, int64_t n1 = -1,
+                void* const* peers = nullptr, int num_peers = 0) {
   using namespace persona;
   if (T < 0 || S <= 0 || nseg < 0 || T > (int64_t{1} << 30)) return PERSONA_ERR_SHAPE;
+  if (n1 < 0) n1 = N;
+  if (n0 < 0 || n1 < n0 || n1 > N || n0 % 128 != 0 || (n1 - n0) % 128 != 0) return PERSONA_ERR_SHAPE;
+  if (num_peers < 0 || num_peers > kMaxTpPeers || (num_peers > 0 && peers == nullptr)) return PERSONA_ERR_INVALID_ARG;
+  for (int q = 0; q < num_peers; ++q)
+    if (peers[q] == nullptr || !aligned16(peers[q])) return PERSONA_ERR_ALIGNMENT;
   if (T == 0) return PERSONA_OK;
   if (seg_indptr == nullptr || (nseg > 0 && seg_slots == nullptr)) return PERSONA_ERR_INVALID_ARG;
   if (workspace == nullptr || workspace_bytes < sgmv_ws_bytes(T)) return PERSONA_ERR_WORKSPACE;
@@ -456,7 +462,11 @@ int sgmv_tc_run(int mode, const void* x, int64_t ldx, const void* a_pool, int64_
   a.err = dev_err;
   a.T = static_cast<int>(T);
   a.K = static_cast<int>(K);
-  a.N = static_cast<int>(N);
+  a.N = static_cast<int>(n1 - n0);
+  a.n0 = static_cast<int>(n0);
+  a.num_peers = num_peers;
+  for (int q = 0; q < num_peers; ++q) a.peers[q] = static_cast<uint16_t*>(peers[q]);
+  if (n1 == n0 && (mode & kModeExpand)) return PERSONA_OK;
   const int64_t max_items = (T + 127) / 128 + nseg;
   return launch_sgmv_tc(mode, dtype, static_cast<int>(R), tx, ta, tb, ty, a,
                         static_cast<int>(max_items < (1 << 30) ? max_items : (1 << 30)), stream) == cudaSuccess
@@ -468,6 +478,69 @@ int sgmv_tc_run(int mode, const void* x, int64_t ldx, const void* a_pool, int64_
 extern "C" {
 
 size_t persona_sgmv_workspace_size(int64_t T) { return T < 0 ? 0 : sgmv_ws_bytes(T); }
+
+int persona_sgmv_fused_tp(const void* x, int64_t ldx, const void* a_pool, int64_t a_slot_stride,
+                          int64_t a_row_stride, const void* b_pool, int64_t b_slot_stride, const int32_t* seg_indptr,
+                          const int32_t* seg_slots, int64_t num_segments, void* y, int64_t ldy, void* const* peer_ys,
+                          int num_peers, int64_t n0, int64_t n1, int64_t T, int64_t K, int64_t N, int64_t R,
+                          int64_t S, int dtype, void* workspace, size_t workspace_bytes, int32_t* dev_err,
+                          cudaStream_t stream) {
+  if (dtype != PERSONA_DTYPE_F16 && dtype != PERSONA_DTYPE_BF16) return PERSONA_ERR_DTYPE;
+  if (!(R == 16 || R == 32)) return PERSONA_ERR_RANK;
+  if (K <= 0 || K % 64 != 0 || N <= 0 || N % 128 != 0) return PERSONA_ERR_SHAPE;
+  return sgmv_tc_run(persona::kModeFused, x, ldx, a_pool, a_slot_stride, a_row_stride, b_pool, b_slot_stride,
+                     seg_indptr, seg_slots, num_segments, nullptr, nullptr, y, ldy, T, K, N, R, S, dtype, workspace,
+                     workspace_bytes, dev_err, stream, n0, n1, peer_ys, num_peers);
+}
+
+// Base of the allocation that holds ptr, through the driver entry point (no
+// link-time dependency on libcuda).
+static int allocation_base(const void* ptr, void** base, size_t* offset) {
+  using Fn = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+  static Fn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<Fn>(p);
+  });
+  if (fn == nullptr) return PERSONA_ERR_CUDA;
+  CUdeviceptr b = 0;
+  size_t size = 0;
+  if (fn(&b, &size, reinterpret_cast<CUdeviceptr>(ptr)) != CUDA_SUCCESS) return PERSONA_ERR_CUDA;
+  *base = reinterpret_cast<void*>(b);
+  *offset = static_cast<size_t>(reinterpret_cast<uintptr_t>(ptr) - static_cast<uintptr_t>(b));
+  return PERSONA_OK;
+}
+
+int persona_ipc_export(const void* ptr, void* handle, size_t* offset) {
+  if (ptr == nullptr || handle == nullptr || offset == nullptr) return PERSONA_ERR_INVALID_ARG;
+  void* base = nullptr;
+  int st = allocation_base(ptr, &base, offset);
+  if (st != PERSONA_OK) return st;
+  cudaIpcMemHandle_t h;
+  if (cudaIpcGetMemHandle(&h, base) != cudaSuccess) return PERSONA_ERR_CUDA;
+  std::memcpy(handle, &h, sizeof(h));
+  return PERSONA_OK;
+}
+
+int persona_ipc_import(const void* handle, size_t offset, void** ptr, void** base) {
+  if (handle == nullptr || ptr == nullptr || base == nullptr) return PERSONA_ERR_INVALID_ARG;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  void* b = nullptr;
+  if (cudaIpcOpenMemHandle(&b, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) return PERSONA_ERR_CUDA;
+  *base = b;
+  *ptr = static_cast<uint8_t*>(b) + offset;
+  return PERSONA_OK;
+}
+
+int persona_ipc_close(void* base) {
+  if (base == nullptr) return PERSONA_ERR_INVALID_ARG;
+  return cudaIpcCloseMemHandle(base) == cudaSuccess ? PERSONA_OK : PERSONA_ERR_CUDA;
+}
 
 int persona_sgmv_shrink(const void* x, int64_t ldx, const void* a_pool, int64_t a_slot_stride, int64_t a_row_stride,
                         const int32_t* seg_indptr, const int32_t* seg_slots, int64_t num_segments, float* v,

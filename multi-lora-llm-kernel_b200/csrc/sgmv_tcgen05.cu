@@ -177,9 +177,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             }
             mbar_arrive_expect_tx(&bars.efull[e], C::kEBytes);
             uint8_t* st = ering + e * C::kEBytes;
-            tc::tma_load_2d(st, &tmY, &bars.efull[e], t * kTcNT, row0);
-            tc::tma_load_2d(st + C::kYBox, &tmY, &bars.efull[e], t * kTcNT + 64, row0);
-            tma_load_3d(st + C::kYBytes, &tmB, &bars.efull[e], 0, t * kTcNT, slot);
+            const int col = args.n0 + t * kTcNT;
+            tc::tma_load_2d(st, &tmY, &bars.efull[e], col, row0);
+            tc::tma_load_2d(st + C::kYBox, &tmY, &bars.efull[e], col + 64, row0);
+            tma_load_3d(st + C::kYBytes, &tmB, &bars.efull[e], 0, col, slot);
             ++ge;
           }
         }
@@ -378,7 +379,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                              "r"(out.z), "r"(out.w)
                              : "memory");
               } else if (valid && live) {
-                *reinterpret_cast<uint4*>(args.y + grow * args.ldy + t * kTcNT + chunk * 8) = out;
+                const int64_t off = grow * args.ldy + args.n0 + t * kTcNT + chunk * 8;
+                *reinterpret_cast<uint4*>(args.y + off) = out;
+                for (int q = 0; q < args.num_peers; ++q) *reinterpret_cast<uint4*>(args.peers[q] + off) = out;
               }
             }
           }
@@ -387,14 +390,30 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           if (lane == 0) mbar_arrive(&bars.acc_empty[buf]);
           if (count == kTcRows) tc::fence_proxy_async();
           named_sync(kEpiBar, 128);
-          if (ew == 0 && lane == 0) {
-            if (count == kTcRows && !*reinterpret_cast<volatile int*>(abort)) {
-              tc::tma_store_2d(&tmY, st, t * kTcNT, row0);
-              tc::tma_store_2d(&tmY, st + C::kYBox, t * kTcNT + 64, row0);
-              tc::bulk_commit();
-              tc::bulk_wait_read0();
-              stored = true;
+          const bool full_live = count == kTcRows && !*reinterpret_cast<volatile int*>(abort);
+          if (ew == 0 && lane == 0 && full_live) {
+            tc::tma_store_2d(&tmY, st, args.n0 + t * kTcNT, row0);
+            tc::tma_store_2d(&tmY, st + C::kYBox, args.n0 + t * kTcNT + 64, row0);
+            tc::bulk_commit();
+            stored = true;
+          }
+          if (args.num_peers > 0 && count == kTcRows) {  // uniform over the epilogue: it ends in a barrier
+            // Tensor parallel: the finished tile also goes to every other
+            // rank's y over NVLink, 256 contiguous bytes per row (16 threads
+            // per row), while the TMA store above writes the local copy.
+            const int64_t col = args.n0 + t * kTcNT;
+#pragma unroll 4
+            for (int i = 0; i < (kTcRows * 16) / 128; ++i) {
+              const int idx = (ew * 32 + lane) + i * 128;
+              const int r = idx >> 4, c16 = idx & 15, box = c16 >> 3, cb = c16 & 7;
+              const uint4 val = lds128(ybase + box * C::kYBox + r * 128 + ((cb ^ (r & 7)) << 4));
+              const int64_t off = (static_cast<int64_t>(row0) + r) * args.ldy + col + c16 * 8;
+              for (int q = 0; q < args.num_peers; ++q) *reinterpret_cast<uint4*>(args.peers[q] + off) = val;
             }
+            named_sync(kEpiBar, 128);
+          }
+          if (ew == 0 && lane == 0) {
+            if (full_live) tc::bulk_wait_read0();
             mbar_arrive(&bars.eempty[e]);
           }
         }

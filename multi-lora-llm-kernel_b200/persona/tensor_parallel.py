@@ -6,8 +6,15 @@ intermediate v itself (the shrink reads x and A once per rank, a small cost
 next to B and y at rank 16), expands into its own column block of y with the
 matching rows of B (a view of the pool, no copy), and the ranks then
 all-gather the column blocks so that every rank holds the full updated y.
-The all-gather is the path's only exchange step; it runs on the process
-group's backend (NCCL over NVLink on B200).
+The all-gather is the path's only exchange step.  Two forms:
+
+* ``sgmv_fused_tp_nvlink`` -- one kernel per rank does the math AND the
+  exchange: every finished 128 x 128 tile of y goes to the rank's own y and,
+  with plain stores over NVLink, into every other rank's y (mapped once with
+  CUDA IPC by ``PeerBuffers``), so the transfer overlaps the math tile by
+  tile; a one-element all-reduce after the launch is the barrier.
+* ``sgmv_fused_tp`` -- the kernel on the column block, then an all-gather on
+  the process group's backend (NCCL); the baseline, and the CPU-testable form.
 
 Column blocks are whole multiples of 128 (the tensor-core tile of the SGMV
 kernel) whenever N allows it.
@@ -63,4 +70,58 @@ def sgmv_fused_tp(x: torch.Tensor, a_pool: torch.Tensor, b_pool: torch.Tensor, s
     for r, (a, b) in enumerate(shards):
         if r != rank and b > a:
             y[:, a:b] = recv[r][:, : b - a]
+    return y
+
+
+class PeerBuffers:
+    """Maps the y buffer of every other rank into this process (CUDA IPC),
+    once per buffer; pass it to ``sgmv_fused_tp_nvlink`` for every call on
+    the same y.  Every rank must build it (it exchanges handles on `group`)."""
+
+    def __init__(self, y: torch.Tensor, group: Optional[dist.ProcessGroup] = None):
+        from persona import ops
+
+        ext = ops._load()
+        self._ext = ext
+        self.device = y.device.index
+        handle, offset = ext.ipc_export(y)
+        world = dist.get_world_size(group)
+        rank = dist.get_rank(group)
+        got = [None] * world
+        dist.all_gather_object(got, (bytes(handle), int(offset)), group=group)
+        self.peers: List[int] = []
+        self._bases: List[int] = []
+        for r, (h, off) in enumerate(got):
+            if r == rank:
+                continue
+            ptr, base = ext.ipc_import(h, off, self.device)
+            self.peers.append(ptr)
+            self._bases.append(base)
+
+    def close(self) -> None:
+        for b in self._bases:
+            self._ext.ipc_close(b, self.device)
+        self._bases, self.peers = [], []
+
+
+def sgmv_fused_tp_nvlink(x: torch.Tensor, a_pool: torch.Tensor, b_pool: torch.Tensor, seg_indptr: torch.Tensor,
+                         seg_slots: torch.Tensor, y: torch.Tensor, peers: PeerBuffers,
+                         group: Optional[dist.ProcessGroup] = None) -> torch.Tensor:
+    """Same result as ``sgmv_fused_tp``, with the all-gather fused into the
+    kernel (NVLink stores of each finished tile into the other ranks' y).
+    Tensor-core shapes only (rank 16 / 32, K % 64 == 0, N % 128 == 0)."""
+    from persona import ops
+
+    ext = ops._load()
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    n0, n1 = column_shards(y.shape[1], world)[rank]
+    flag = torch.zeros(1, dtype=torch.int32, device=y.device)
+    # Barriers on the stream.  Before: no rank writes into a peer's y while
+    # that peer may still be reading it.  After: when it completes on a rank,
+    # every rank's kernel (and so every tile stored into this rank's y) has
+    # finished.
+    dist.all_reduce(flag, group=group)
+    ext.sgmv_fused_tp(x, a_pool, b_pool, seg_indptr, seg_slots, y, peers.peers, n0, n1)
+    dist.all_reduce(flag, group=group)
     return y
