@@ -673,12 +673,124 @@ def run_extra(args):
     return 0
 
 
+def run_sgmv_tp(args):
+    """Config 4 across N GPUs: the segmented prefill with the expand split by
+    output columns and y gathered on every rank, (a) fused: one kernel per rank
+    stores each finished tile into every rank's y over NVLink, (b) baseline:
+    the same kernel on the column block, then an NCCL all-gather."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from persona import ops
+    from persona.tensor_parallel import PeerBuffers, column_shards, sgmv_fused_tp, sgmv_fused_tp_nvlink
+    from persona.workloads import PROJECTIONS, bgmv_bytes
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+    stream = torch.cuda.current_stream()
+    req, rows, R, S = 32, 512, 16, 32
+    T = req * rows
+    rng = np.random.Generator(np.random.PCG64(SEED + 1))
+    seg = rng.permutation(req).astype(np.int32)
+    indptr = (np.arange(req + 1) * rows).astype(np.int32)
+    slots = np.repeat(seg, rows)
+    ip, ss = torch.from_numpy(indptr).to(dev), torch.from_numpy(seg).to(dev)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(SEED * 1000 + 29)  # same inputs on every rank
+    names = [n for n in ("gate_proj", "up_proj", "down_proj") if ONLY is None or n == ONLY]
+    projs = []
+    for n in names:
+        K, N = PROJECTIONS[n]
+        lim = 1.0 / np.sqrt(K)
+        a = ((torch.rand(S, R, K, generator=gen, device=dev) * 2 - 1) * lim).to(torch.bfloat16)
+        b = (torch.randn(S, N, R, generator=gen, device=dev) * 0.04).to(torch.bfloat16)
+        x = torch.randn(T, K, generator=gen, device=dev).to(torch.bfloat16)
+        y = torch.zeros(T, N, device=dev, dtype=torch.bfloat16)
+        projs.append(dict(K=K, N=N, a=a, b=b, x=x, y=y, bytes=bgmv_bytes(K, N, R, slots)))
+    peers = [PeerBuffers(p["y"]) for p in projs]
+    steps, warm = max(1, args.steps), max(3, args.warmup)
+
+    def fused():
+        for p, pb in zip(projs, peers):
+            sgmv_fused_tp_nvlink(p["x"], p["a"], p["b"], ip, ss, p["y"], pb)
+
+    def baseline():
+        for p in projs:
+            sgmv_fused_tp(p["x"], p["a"], p["b"], ip, ss, p["y"])
+
+    def timed(fn):
+        for _ in range(warm):
+            fn()
+        torch.cuda.synchronize()
+        dist.barrier(device_ids=[local])
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1) / steps], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    ms_fused = timed(fused)
+    ms_base = timed(baseline)
+    ops.check_errors(dev)
+    tot = sum(p["bytes"] for p in projs)
+    # bytes this rank sends over NVLink per step: its column block of every y, to each peer
+    nv = sum(T * (column_shards(p["N"], world)[rank][1] - column_shards(p["N"], world)[rank][0]) * 2
+             for p in projs) * (world - 1)
+    # per-rank roofline: HBM bytes this rank moves (x and the used A rows
+    # whole, its block of B, its block of y read and written, the other
+    # blocks of y written by the peers) against the measured copy bandwidth,
+    # and the NVLink bytes it sends against the measured 770 GB/s per direction
+    used = len(set(int(s_) for s_ in seg if s_ >= 0))
+    hbm = 0
+    for p in projs:
+        n0, n1 = column_shards(p["N"], world)[rank]
+        hbm += 2 * (T * p["K"] + used * R * p["K"] + used * (n1 - n0) * R + 2 * T * (n1 - n0)
+                    + T * (p["N"] - (n1 - n0)))
+    peak, _ = load_peaks()
+    t_floor = max(hbm / (peak * 1e9), nv / 770e9)
+    if rank == 0:
+        print(json.dumps({
+            "workload": "sgmv_prefill_tp", "metric": "tensor-parallel SGMV fused shrink+expand GB/s (algorithmic, "
+                                                    "whole job, y gathered on every rank)",
+            "value": tot / (ms_fused * 1e-3) / 1e9, "unit": "GB/s", "n_gpus": world, "steps": steps, "warmup": warm,
+            "ms_per_step": ms_fused, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "segmented prefill: 32 requests x 512 rows, rank 16, 32-slot pool, bf16, "
+                                   "expand split by output columns", "projections": names},
+            "nvlink_bytes_per_rank_per_step": nv,
+            "nvlink_gbs_per_rank": nv / (ms_fused * 1e-3) / 1e9,
+            "baseline_nccl_all_gather": {"ms_per_step": ms_base, "GB/s": tot / (ms_base * 1e-3) / 1e9},
+            "roofline": {"bound": "hbm+nvlink", "hbm_bytes_per_rank": hbm, "hbm_peak_gbs": peak,
+                         "nvlink_peak_gbs": 770.0, "floor_ms": t_floor * 1e3,
+                         "frac": t_floor * 1e3 / ms_fused},
+            "gpu_launches": steps * len(projs) * 2,
+        }), flush=True)
+    for pb in peers:
+        pb.close()
+    dist.barrier(device_ids=[local])
+    dist.destroy_process_group()
+    return 0
+
+
 def main():
     global ONLY
     args = parse_args()
     ONLY = args.only
     if args.impl == "reference":
         return run_reference(args)
+    if args.workload == "sgmv_prefill" and args.gpus > 1:
+        return run_sgmv_tp(args)
     if args.workload != "mixed_decode":
         return run_extra(args)
     return run_ours(args)

@@ -16,7 +16,11 @@
 //   warps 2-5  epilogue, one thread per TMEM lane (= row): read D_v, split v
 //           into 16-bit hi + lo halves (per-row power-of-two scale for f16)
 //           and write them to shared memory as the expand's A operand V';
-//           read D_y, add the y tile, write it back and TMA-store it.
+//           read D_y, add the y tile, write it back and TMA-store it;
+//   warps 6-9  exchange (tensor parallel only): copy each finished y tile
+//           from shared memory into the other ranks' y over NVLink, then
+//           release the y stage, so the transfer runs beside the math of the
+//           next tiles instead of inside the epilogue.
 // The expand multiplies B by hi and by lo, so v keeps ~fp32 precision.
 // Only full items use the TMA store; a short item (segment tail) writes its
 // valid rows with plain stores, so rows of the next segment are never
@@ -35,8 +39,9 @@ constexpr int kTcNT = 128;     // expand output columns per tile (MMA N)
 constexpr int kTcKC = 64;      // shrink K chunk (one 128-byte swizzled row)
 constexpr int kSStages = 4;
 constexpr int kEStages = 3;
-constexpr int kTcThreads = 6 * 32;
+constexpr int kTcThreads = 10 * 32;
 constexpr int kEpiBar = 1;     // named barrier of the four epilogue warps
+constexpr int kXchWarps = 4;   // warps 6-9
 constexpr uint32_t kTmemCols = 512;
 
 
@@ -60,6 +65,7 @@ struct TcCfg {
 struct TcBars {
   uint64_t sfull[kSStages], sempty[kSStages];
   uint64_t efull[kEStages], eempty[kEStages];
+  uint64_t xready[kEStages];  // y tile complete in shared memory (exchange warps)
   uint64_t v_ready, v_used, vsm_ready;
   uint64_t acc_full[2], acc_empty[2];
   uint64_t mma_done;
@@ -108,9 +114,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       mbar_init(&bars.sfull[i], 1);
       mbar_init(&bars.sempty[i], 1);
     }
+    // A y stage is free again once the epilogue's TMA store has read it
+    // and, with peers, once every exchange warp has copied it out.
+    const int xch = args.num_peers > 0 ? kXchWarps : 0;
     for (int i = 0; i < kEStages; ++i) {
       mbar_init(&bars.efull[i], 1);
-      mbar_init(&bars.eempty[i], 1);
+      mbar_init(&bars.eempty[i], 1 + xch);
+      mbar_init(&bars.xready[i], 1);
     }
     mbar_init(&bars.v_ready, 1);
     mbar_init(&bars.v_used, 4);
@@ -259,7 +269,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       mbar_wait(&bars.mma_done, 0, args.err);
     }
     __syncwarp();
-  } else {
+  } else if (warp < 6) {
     // ------------------------------------------------------ epilogue ----
     // Every epilogue thread runs the same item / tile loop to the end, so
     // the named barriers stay matched; after an abort the waits return at
@@ -397,22 +407,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             tc::bulk_commit();
             stored = true;
           }
-          if (args.num_peers > 0 && count == kTcRows) {  // uniform over the epilogue: it ends in a barrier
-            // Tensor parallel: the finished tile also goes to every other
-            // rank's y over NVLink, 256 contiguous bytes per row (16 threads
-            // per row), while the TMA store above writes the local copy.
-            const int64_t col = args.n0 + t * kTcNT;
-#pragma unroll 4
-            for (int i = 0; i < (kTcRows * 16) / 128; ++i) {
-              const int idx = (ew * 32 + lane) + i * 128;
-              const int r = idx >> 4, c16 = idx & 15, box = c16 >> 3, cb = c16 & 7;
-              const uint4 val = lds128(ybase + box * C::kYBox + r * 128 + ((cb ^ (r & 7)) << 4));
-              const int64_t off = (static_cast<int64_t>(row0) + r) * args.ldy + col + c16 * 8;
-              for (int q = 0; q < args.num_peers; ++q) *reinterpret_cast<uint4*>(args.peers[q] + off) = val;
-            }
-            named_sync(kEpiBar, 128);
-          }
           if (ew == 0 && lane == 0) {
+            // The tile is complete in shared memory (barrier above): the
+            // exchange warps may copy it out while the next tile is computed.
+            if (args.num_peers > 0) mbar_arrive(&bars.xready[e]);
             if (full_live) tc::bulk_wait_read0();
             mbar_arrive(&bars.eempty[e]);
           }
@@ -420,6 +418,41 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
     }
     if (stored) tc::bulk_wait0();
+    // Plain stores into the peers' y (short items) are ordered before
+    // whatever this thread's kernel completion is followed by.
+    if (args.num_peers > 0) __threadfence_system();
+  } else if (args.num_peers > 0) {
+    // ------------------------------------------------------ exchange ----
+    // Tensor parallel: every full 128 x 128 tile also goes to every other
+    // rank's y over NVLink, 256 contiguous bytes per row, 16 threads per row
+    // (rows of a short item were stored by the epilogue itself).  Each warp
+    // releases the y stage when its share of the copy is issued; the values
+    // are in registers by then, so the stage may be refilled.
+    const int xw = warp - 6;
+    uint32_t ge = 0;
+    for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
+      const int4 it = pv.items[item];
+      const int row0 = it.y, count = it.z;
+      for (int t = 0; t < nn; ++t, ++ge) {
+        const int e = ge % kEStages;
+        const bool ok = tc_wait(&bars.xready[e], (ge / kEStages) & 1, args.err, abort);
+        if (ok && count == kTcRows && !*reinterpret_cast<volatile int*>(abort)) {
+          const uint32_t ybase = smem_u32(ering + e * C::kEBytes);
+          const int64_t col = args.n0 + t * kTcNT;
+#pragma unroll 4
+          for (int i = 0; i < (kTcRows * 16) / (kXchWarps * 32); ++i) {
+            const int idx = (xw * 32 + lane) + i * (kXchWarps * 32);
+            const int r = idx >> 4, c16 = idx & 15, box = c16 >> 3, cb = c16 & 7;
+            const uint4 val = lds128(ybase + box * C::kYBox + r * 128 + ((cb ^ (r & 7)) << 4));
+            const int64_t off = (static_cast<int64_t>(row0) + r) * args.ldy + col + c16 * 8;
+            for (int q = 0; q < args.num_peers; ++q) *reinterpret_cast<uint4*>(args.peers[q] + off) = val;
+          }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars.eempty[e]);
+      }
+    }
+    __threadfence_system();
   }
   tc::fence_before_sync();
   __syncthreads();
