@@ -147,7 +147,7 @@ int persona_bgmv_fused_multi(const persona_bgmv_problem* problems, int num_probl
  * arrays.  A segment is used only if 0 <= lo <= hi <= T and no earlier
  * seg_indptr entry exceeds lo (used segments never overlap); any other
  * segment sets PERSONA_DEV_ERR_SEGMENT and is skipped.
- * Ranks 16 and 32 with K % 64 == 0 (shrink) and N % 128 == 0 (expand) run on
+ * Ranks 16 and 32 with K % 64 == 0 (shrink) and N % 64 == 0 (expand) run on
  * the tensor cores (tcgen05, accumulators in TMEM, 128-row tiles); other
  * shapes run the split BGMV kernels over the segments' rows.
  * Workspace: persona_sgmv_workspace_size(T). */
@@ -203,7 +203,7 @@ int persona_bgmv_fused_noalloc(const void* x, int64_t ldx, const void* a_pool, i
  * mapped into this process (persona_ipc_import), same shape and ldy.  After
  * the launch and a cross-rank barrier (any collective on this stream) every
  * rank holds the full updated y.  Tensor-core shapes only: R in {16, 32},
- * K % 64 == 0, N % 128 == 0, n0 and n1 multiples of 128; at most
+ * K % 64 == 0, N % 64 == 0, n0 and n1 multiples of 64; at most
  * PERSONA_MAX_TP_PEERS peers.  The ranks' y must hold the same values before
  * the call (rows outside every segment are not written).                   */
 #define PERSONA_MAX_TP_PEERS 7

@@ -54,6 +54,9 @@ cudaError_t launch_bgmv_split(int mode, int dtype, int R, const SplitMaps& maps,
 
 // Segmented tensor-core kernels (sgmv_tcgen05.cu).
 constexpr int kMaxTpPeers = 7;  // other ranks a tensor-parallel launch writes to
+// Width of one tensor-core SGMV fill: the shrink's K chunk and the expand's
+// output tile (MMA N); x, y and A move as 64-element boxes side by side.
+constexpr int kSgmvTcTileN = 128;
 struct SgmvTcArgs {
   const int32_t* plan;  // segment plan, 128-row items, identity perm
   const float* v_in;    // expand only: [T, R]

@@ -195,6 +195,10 @@ __global__ void __launch_bounds__(THREADS)
     sgmv_plan_kernel(const int32_t* __restrict__ indptr, const int32_t* __restrict__ seg_slots, int nseg,
                      int T, int S, int rows_per_item, int32_t* __restrict__ plan, int32_t* __restrict__ row_slots,
                      int32_t* dev_err) {
+  // row_slots == nullptr: items and header only (the tensor-core kernels
+  // read nothing else); otherwise also the per-row slots, the identity
+  // permutation and the split kernels' shared state.
+  const bool rows = row_slots != nullptr;
   using ScanI = cub::BlockScan<int, THREADS>;
   __shared__ typename ScanI::TempStorage scan;
   __shared__ int s_base[2];  // running full / partial item counts
@@ -204,10 +208,12 @@ __global__ void __launch_bounds__(THREADS)
   __shared__ int s_lo[THREADS], s_hi[THREADS], s_slot[THREADS];
   const int tid = threadIdx.x;
   PlanView pv = plan_view(plan, T);
-  init_work_state(plan, T, tid, THREADS);
-  for (int t = tid; t < T; t += THREADS) {
-    row_slots[t] = -1;
-    pv.perm[t] = t;
+  if (rows) {
+    init_work_state(plan, T, tid, THREADS);
+    for (int t = tid; t < T; t += THREADS) {
+      row_slots[t] = -1;
+      pv.perm[t] = t;
+    }
   }
   if (tid == 0) {
     s_base[0] = s_base[1] = 0;
@@ -261,7 +267,7 @@ __global__ void __launch_bounds__(THREADS)
         s_slot[tid] = slot;
       }
       __syncthreads();
-      if (pass == 1) {  // row slots of this chunk's segments, one warp per segment
+      if (pass == 1 && rows) {  // row slots of this chunk's segments, one warp per segment
         const int n = min(THREADS, nseg - base);
         for (int q = tid >> 5; q < n; q += THREADS / 32)
           for (int t = s_lo[q] + (tid & 31); t < s_hi[q]; t += 32) row_slots[t] = s_slot[q];

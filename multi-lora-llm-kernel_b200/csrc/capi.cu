@@ -396,7 +396,7 @@ int sgmv_prepare(const int32_t* seg_indptr, const int32_t* seg_slots, int64_t ns
 }  // namespace
 
 namespace {
-// Tensor-core path: ranks 16 / 32, K a multiple of 64, N a multiple of 128.
+// Tensor-core path: ranks 16 / 32, K and N multiples of 64.
 // PERSONA_SGMV_TENSOR_CORES=0 selects the BGMV split path instead.
 bool sgmv_tc_eligible(int64_t R, int64_t K, int64_t N, bool need_k, bool need_n) {
   static const bool enabled = [] {
@@ -405,7 +405,7 @@ bool sgmv_tc_eligible(int64_t R, int64_t K, int64_t N, bool need_k, bool need_n)
   }();
   if (!enabled || !(R == 16 || R == 32)) return false;
   if (need_k && (K % 64 != 0 || K <= 0)) return false;
-  if (need_n && (N % 128 != 0 || N <= 0)) return false;
+  if (need_n && (N % 64 != 0 || N <= 0)) return false;
   return true;
 }
 
@@ -418,7 +418,7 @@ int sgmv_tc_run(int mode, const void* x, int64_t ldx, const void* a_pool, int64_
   using namespace persona;
   if (T < 0 || S <= 0 || nseg < 0 || T > (int64_t{1} << 30)) return PERSONA_ERR_SHAPE;
   if (n1 < 0) n1 = N;
-  if (n0 < 0 || n1 < n0 || n1 > N || n0 % 128 != 0 || (n1 - n0) % 128 != 0) return PERSONA_ERR_SHAPE;
+  if (n0 < 0 || n1 < n0 || n1 > N || n0 % 64 != 0 || (n1 - n0) % 64 != 0) return PERSONA_ERR_SHAPE;
   if (num_peers < 0 || num_peers > kMaxTpPeers || (num_peers > 0 && peers == nullptr)) return PERSONA_ERR_INVALID_ARG;
   for (int q = 0; q < num_peers; ++q)
     if (peers[q] == nullptr || !aligned16(peers[q])) return PERSONA_ERR_ALIGNMENT;
@@ -440,13 +440,13 @@ int sgmv_tc_run(int mode, const void* x, int64_t ldx, const void* a_pool, int64_
   if (mode & kModeExpand) {
     if ((st = check_b(b_pool, b_slot_stride, y, ldy, N, R)) != PERSONA_OK) return st;
     if ((st = encode_2d_map(&ty, y, dtype, N, T, ldy, 64, 128)) != PERSONA_OK) return st;
-    if ((st = encode_b_map(&tb, b_pool, dtype, N, R, S, b_slot_stride, 128)) != PERSONA_OK) return st;
+    if ((st = encode_b_map(&tb, b_pool, dtype, N, R, S, b_slot_stride, kSgmvTcTileN)) != PERSONA_OK) return st;
   }
   if (mode == kModeShrink && (v_out == nullptr || !aligned16(v_out))) return PERSONA_ERR_ALIGNMENT;
   if (mode == kModeExpand && (v_in == nullptr || !aligned16(v_in))) return PERSONA_ERR_ALIGNMENT;
-  int32_t* row_slots = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(workspace) + bgmv_ws_bytes(T));
+  // items of 128 rows and the header are all the tensor-core kernel reads
   if (launch_sgmv_plan(seg_indptr, seg_slots, static_cast<int>(nseg), static_cast<int>(T), static_cast<int>(S),
-                       128, static_cast<int32_t*>(workspace), row_slots, dev_err, stream) != cudaSuccess)
+                       128, static_cast<int32_t*>(workspace), nullptr, dev_err, stream) != cudaSuccess)
     return PERSONA_ERR_CUDA;
   if (mode == kModeShrink) {
     // rows outside every segment (or with slot -1) get v = 0 first
@@ -487,7 +487,7 @@ int persona_sgmv_fused_tp(const void* x, int64_t ldx, const void* a_pool, int64_
                           cudaStream_t stream) {
   if (dtype != PERSONA_DTYPE_F16 && dtype != PERSONA_DTYPE_BF16) return PERSONA_ERR_DTYPE;
   if (!(R == 16 || R == 32)) return PERSONA_ERR_RANK;
-  if (K <= 0 || K % 64 != 0 || N <= 0 || N % 128 != 0) return PERSONA_ERR_SHAPE;
+  if (K <= 0 || K % 64 != 0 || N <= 0 || N % 64 != 0) return PERSONA_ERR_SHAPE;
   return sgmv_tc_run(persona::kModeFused, x, ldx, a_pool, a_slot_stride, a_row_stride, b_pool, b_slot_stride,
                      seg_indptr, seg_slots, num_segments, nullptr, nullptr, y, ldy, T, K, N, R, S, dtype, workspace,
                      workspace_bytes, dev_err, stream, n0, n1, peer_ys, num_peers);

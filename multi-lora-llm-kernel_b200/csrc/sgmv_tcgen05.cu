@@ -6,9 +6,10 @@
 // segment table assigns to each adapter: v = x A[s]^T, y += v B[s]^T.
 //
 // Work unit: a 128-row item of one segment (from the segment plan), one MMA
-// tile high.  Per CTA (persistent over items), six warps:
-//   warp 0  TMA producer: x / A chunks (K = 64) into a 4-stage shrink ring,
-//           y / B tiles (128 columns) into a 3-stage expand ring;
+// tile high.  Per CTA (persistent over items), ten warps around one ring of
+// equal shared-memory slots; per item the ring carries K/128 shrink fills
+// (x chunk + A chunk) and then N/128 expand fills (y tile + B tile):
+//   warp 0  TMA producer, fills the ring in that order;
 //   warp 1  MMA issuer (one thread): shrink D_v[128 x R] += x_chunk A_chunk^T
 //           (M = 128, N = R, K = 16 per instruction) into TMEM; expand
 //           D_y[128 x 128] = V'[128 x 2R] B_tile^T into one of two TMEM
@@ -16,10 +17,10 @@
 //   warps 2-5  epilogue, one thread per TMEM lane (= row): read D_v, split v
 //           into 16-bit hi + lo halves (per-row power-of-two scale for f16)
 //           and write them to shared memory as the expand's A operand V';
-//           read D_y, add the y tile, write it back and TMA-store it;
+//           read D_y, add the y tile, write it back in place and TMA-store it;
 //   warps 6-9  exchange (tensor parallel only): copy each finished y tile
 //           from shared memory into the other ranks' y over NVLink, then
-//           release the y stage, so the transfer runs beside the math of the
+//           release the slot, so the transfer runs beside the math of the
 //           next tiles instead of inside the epilogue.
 // The expand multiplies B by hi and by lo, so v keeps ~fp32 precision.
 // Only full items use the TMA store; a short item (segment tail) writes its
@@ -35,39 +36,49 @@
 namespace persona {
 
 constexpr int kTcRows = 128;   // rows per item (MMA M)
-constexpr int kTcNT = 128;     // expand output columns per tile (MMA N)
-constexpr int kTcKC = 64;      // shrink K chunk (one 128-byte swizzled row)
-constexpr int kSStages = 4;
-constexpr int kEStages = 3;
+constexpr int kBoxCols = 64;   // elements per 128-byte swizzled row: one TMA box is 128 rows x 64
+constexpr int kBoxes = kSgmvTcTileN / kBoxCols;  // boxes per fill
+constexpr int kTcNT = kSgmvTcTileN;  // expand output columns per tile (MMA N)
+constexpr int kTcKC = kSgmvTcTileN;  // shrink K chunk
 constexpr int kTcThreads = 10 * 32;
 constexpr int kEpiBar = 1;     // named barrier of the four epilogue warps
+constexpr int kXchBar = 2;     // named barrier of the four exchange warps
 constexpr int kXchWarps = 4;   // warps 6-9
+constexpr int kAccBufs = 256 / kTcNT;  // expand accumulators in TMEM, columns [128, 384)
+constexpr int kMaxSlots = 12;
 constexpr uint32_t kTmemCols = 512;
+constexpr int kSmemPerBlock = 227 * 1024;  // opt-in maximum per block on sm_100
 
-
+// One ring of equal slots serves both phases: a shrink fill is an x chunk
+// (128 rows x kTcKC) + the A chunk (R x kTcKC); an expand fill is a y tile
+// (128 rows x kTcNT) + the B tile (kTcNT x R).  x, y and A arrive as boxes
+// of 64 elements (128-byte swizzled rows), several side by side per fill.
+// Sharing the ring keeps ~200 KB of loads in flight in either phase.
 template <int R>
 struct TcCfg {
   static_assert(R == 16 || R == 32, "tensor-core SGMV ranks");
-  static constexpr int kXBytes = kTcRows * kTcKC * 2;  // 16 KB
-  static constexpr int kABytes = R * kTcKC * 2;
-  static constexpr int kSBytes = kXBytes + kABytes;    // multiple of 1024
-  static constexpr int kYBox = kTcRows * 64 * 2;       // 16 KB: 64 columns x 128 rows
-  static constexpr int kYBytes = 2 * kYBox;
+  static constexpr int kBoxBytes = kTcRows * 128;      // one x / y box: 16 KB
+  static constexpr int kTileBytes = kBoxes * kBoxBytes;
+  static constexpr int kABox = R * 128;                // one A box
+  static constexpr int kABytes = kBoxes * kABox;
   static constexpr int kBBytes = kTcNT * R * 2;
-  static constexpr int kEBytes = kYBytes + kBBytes;
+  static constexpr int kSlotBytes = kTileBytes + (kABytes > kBBytes ? kABytes : kBBytes);
+  static constexpr int kVBytes = kTcRows * 128;  // V' rows of 128 bytes (hi | lo | 0)
+  static constexpr int kSlots = (kSmemPerBlock - 2048 - kVBytes) / kSlotBytes < kMaxSlots
+                                    ? (kSmemPerBlock - 2048 - kVBytes) / kSlotBytes
+                                    : kMaxSlots;
+  static constexpr int kSmem = kSlots * kSlotBytes + kVBytes;
   static constexpr uint32_t kBLayout = R == 16 ? tc::kLayoutSw32 : tc::kLayoutSw64;
   static constexpr uint32_t kBSbo = 8 * 2 * R;  // 8 rows of 2R bytes
-  static constexpr int kVBytes = kTcRows * 128;  // V' rows of 128 bytes (hi | lo | 0)
-  static constexpr int kSmem = kSStages * kSBytes + kEStages * kEBytes + kVBytes;
-  static_assert(kSBytes % 1024 == 0 && kEBytes % 1024 == 0, "stage alignment");
+  static_assert(kSlotBytes % 1024 == 0, "slot alignment");
+  static_assert(kSlots >= 4, "ring depth");
 };
 
 struct TcBars {
-  uint64_t sfull[kSStages], sempty[kSStages];
-  uint64_t efull[kEStages], eempty[kEStages];
-  uint64_t xready[kEStages];  // y tile complete in shared memory (exchange warps)
+  uint64_t full[kMaxSlots], empty[kMaxSlots];
+  uint64_t xready[kMaxSlots];  // y tile finished in shared memory, for the store warps
   uint64_t v_ready, v_used, vsm_ready;
-  uint64_t acc_full[2], acc_empty[2];
+  uint64_t acc_full[kAccBufs], acc_empty[kAccBufs];
   uint64_t mma_done;
   uint32_t tmem_base;
   int abort;  // set by the first wait that runs out; later waits return at once
@@ -95,6 +106,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                    const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmY,
                    const SgmvTcArgs args) {
   using C = TcCfg<R>;
+  constexpr int kSlots = C::kSlots;
   constexpr bool kDoShrink = (MODE & kModeShrink) != 0;
   constexpr bool kDoExpand = (MODE & kModeExpand) != 0;
   constexpr uint32_t kFmt = std::is_same<DT, __nv_bfloat16>::value ? 1u : 0u;
@@ -102,30 +114,22 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   constexpr uint32_t kIdescY = tc::idesc_f16(kFmt, kTcRows, kTcNT);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sring = base;
-  uint8_t* ering = base + kSStages * C::kSBytes;
-  uint8_t* vsm = ering + kEStages * C::kEBytes;
+  uint8_t* ring = base;
+  uint8_t* vsm = ring + kSlots * C::kSlotBytes;
   __shared__ TcBars bars;
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
   if (tid == 0) {
-    for (int i = 0; i < kSStages; ++i) {
-      mbar_init(&bars.sfull[i], 1);
-      mbar_init(&bars.sempty[i], 1);
-    }
-    // A y stage is free again once the epilogue's TMA store has read it
-    // and, with peers, once every exchange warp has copied it out.
-    const int xch = args.num_peers > 0 ? kXchWarps : 0;
-    for (int i = 0; i < kEStages; ++i) {
-      mbar_init(&bars.efull[i], 1);
-      mbar_init(&bars.eempty[i], 1 + xch);
-      mbar_init(&bars.xready[i], 1);
+    for (int i = 0; i < kSlots; ++i) {
+      mbar_init(&bars.full[i], 1);
+      mbar_init(&bars.empty[i], 1);   // MMA commit (shrink fill), store leader (expand fill)
+      mbar_init(&bars.xready[i], 4);  // one arrive per epilogue warp
     }
     mbar_init(&bars.v_ready, 1);
     mbar_init(&bars.v_used, 4);
     mbar_init(&bars.vsm_ready, 1);
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < kAccBufs; ++b) {
       mbar_init(&bars.acc_full[b], 1);
       mbar_init(&bars.acc_empty[b], 4);
     }
@@ -145,11 +149,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
   PlanView pv = plan_view(const_cast<int32_t*>(args.plan), args.T);
   const int n_items = pv.hdr[kHdrItems];
-  const int nk = (args.K + kTcKC - 1) / kTcKC;
-  const int nn = args.N / kTcNT;
+  const int nk = kDoShrink ? (args.K + kTcKC - 1) / kTcKC : 0;  // shrink fills per item (last may be part)
+  const int nn = kDoExpand ? (args.N + kTcNT - 1) / kTcNT : 0;  // expand fills per item (last may be part)
 
   if (warp == 0) {
     // ------------------------------------------------------ producer ----
+    // Fills in the order every role walks them: per item, nk shrink chunks
+    // then nn expand tiles.  Fill g uses slot g % kSlots.
     if (lane == 0) {
       if (kDoShrink) {
         tma_prefetch_desc(&tmX);
@@ -159,82 +165,80 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         tma_prefetch_desc(&tmY);
         tma_prefetch_desc(&tmB);
       }
-      uint32_t gs = 0, ge = 0;
+      uint32_t g = 0;
       bool ok = true;
       for (int item = blockIdx.x; ok && item < n_items; item += gridDim.x) {
         const int4 it = pv.items[item];
         const int slot = it.x, row0 = it.y;
-        if (kDoShrink) {
-          for (int kc = 0; kc < nk; ++kc) {
-            const int s = gs % kSStages;
-            if (gs >= kSStages && !tc_wait(&bars.sempty[s], ((gs / kSStages) - 1) & 1, args.err, abort)) {
-              ok = false;
-              break;
-            }
-            mbar_arrive_expect_tx(&bars.sfull[s], C::kSBytes);
-            uint8_t* st = sring + s * C::kSBytes;
-            tc::tma_load_2d(st, &tmX, &bars.sfull[s], kc * kTcKC, row0);
-            tma_load_3d(st + C::kXBytes, &tmA, &bars.sfull[s], kc * kTcKC, 0, slot);
-            ++gs;
+        for (int f = 0; f < nk + nn; ++f, ++g) {
+          const int s = g % kSlots;
+          if (g >= static_cast<uint32_t>(kSlots) &&
+              !tc_wait(&bars.empty[s], ((g / kSlots) - 1) & 1, args.err, abort)) {
+            ok = false;
+            break;
           }
-        }
-        if (kDoExpand && ok) {
-          for (int t = 0; t < nn; ++t) {
-            const int e = ge % kEStages;
-            if (ge >= kEStages && !tc_wait(&bars.eempty[e], ((ge / kEStages) - 1) & 1, args.err, abort)) {
-              ok = false;
-              break;
+          uint8_t* st = ring + s * C::kSlotBytes;
+          if (f < nk) {
+            // only boxes that start inside K are loaded (K is a multiple of 64)
+            const int nb = min(kBoxes, (args.K - f * kTcKC) / kBoxCols);
+            mbar_arrive_expect_tx(&bars.full[s], nb * (C::kBoxBytes + C::kABox));
+            for (int b = 0; b < nb; ++b) {
+              tc::tma_load_2d(st + b * C::kBoxBytes, &tmX, &bars.full[s], f * kTcKC + b * kBoxCols, row0);
+              tma_load_3d(st + C::kTileBytes + b * C::kABox, &tmA, &bars.full[s], f * kTcKC + b * kBoxCols, 0,
+                          slot);
             }
-            mbar_arrive_expect_tx(&bars.efull[e], C::kEBytes);
-            uint8_t* st = ering + e * C::kEBytes;
+          } else {
+            // only y boxes inside the column block are loaded (its width is a
+            // multiple of 64); the B box reads zeros past N
+            const int t = f - nk;
             const int col = args.n0 + t * kTcNT;
-            tc::tma_load_2d(st, &tmY, &bars.efull[e], col, row0);
-            tc::tma_load_2d(st + C::kYBox, &tmY, &bars.efull[e], col + 64, row0);
-            tma_load_3d(st + C::kYBytes, &tmB, &bars.efull[e], 0, col, slot);
-            ++ge;
+            const int nb = min(kBoxes, (args.N - t * kTcNT) / kBoxCols);
+            mbar_arrive_expect_tx(&bars.full[s], nb * C::kBoxBytes + C::kBBytes);
+            for (int b = 0; b < nb; ++b)
+              tc::tma_load_2d(st + b * C::kBoxBytes, &tmY, &bars.full[s], col + b * kBoxCols, row0);
+            tma_load_3d(st + C::kTileBytes, &tmB, &bars.full[s], 0, col, slot);
           }
         }
       }
       // Every load this thread issued lands before the CTA can exit: wait
       // (bounded, whatever the abort flag says) for the last fill of each
-      // stage.  Earlier fills of a stage completed before it was refilled.
-      for (int s = 0; s < kSStages; ++s)
-        if (gs > static_cast<uint32_t>(s)) {
-          const uint32_t last = (gs - 1 - s) / kSStages;  // index of the stage's last fill
-          mbar_wait(&bars.sfull[s], last & 1, args.err);
-        }
-      for (int e = 0; e < kEStages; ++e)
-        if (ge > static_cast<uint32_t>(e)) {
-          const uint32_t last = (ge - 1 - e) / kEStages;
-          mbar_wait(&bars.efull[e], last & 1, args.err);
+      // slot.  Earlier fills of a slot completed before it was refilled.
+      for (int s = 0; s < kSlots; ++s)
+        if (g > static_cast<uint32_t>(s)) {
+          const uint32_t last = (g - 1 - s) / kSlots;  // use count of the slot's last fill
+          mbar_wait(&bars.full[s], last & 1, args.err);
         }
     }
     __syncwarp();
   } else if (warp == 1) {
     // ----------------------------------------------------------- MMA ----
     if (lane == 0) {
-      uint32_t gs = 0, ge = 0, nt = 0, j = 0;
+      uint32_t g = 0, nt = 0, j = 0;
       bool ok = true;
       const uint32_t d_v = tmem;
+      const uint32_t sv = smem_u32(vsm);
       for (int item = blockIdx.x; ok && item < n_items; item += gridDim.x, ++j) {
         if (kDoShrink) {
           if (j > 0 && !tc_wait(&bars.v_used, (j - 1) & 1, args.err, abort)) break;  // D_v of the previous item read
           tc::fence_after_sync();
-          for (int kc = 0; kc < nk; ++kc, ++gs) {
-            const int s = gs % kSStages;
-            if (!tc_wait(&bars.sfull[s], (gs / kSStages) & 1, args.err, abort)) {
+          for (int kc = 0; kc < nk; ++kc, ++g) {
+            const int s = g % kSlots;
+            if (!tc_wait(&bars.full[s], (g / kSlots) & 1, args.err, abort)) {
               ok = false;
               break;
             }
             tc::fence_after_sync();
-            const uint32_t sx = smem_u32(sring + s * C::kSBytes);
+            const uint32_t sx = smem_u32(ring + s * C::kSlotBytes);
+            const int nks = min(kTcKC, args.K - kc * kTcKC) / 16;  // K steps of the boxes loaded
 #pragma unroll
             for (int ks = 0; ks < kTcKC / 16; ++ks) {
-              const uint64_t a = tc::smem_desc(sx + ks * 32, 1024, tc::kLayoutSw128);
-              const uint64_t b = tc::smem_desc(sx + C::kXBytes + ks * 32, 1024, tc::kLayoutSw128);
+              if (ks >= nks) break;
+              const uint32_t box = ks / (kBoxCols / 16), in = (ks % (kBoxCols / 16)) * 32;
+              const uint64_t a = tc::smem_desc(sx + box * C::kBoxBytes + in, 1024, tc::kLayoutSw128);
+              const uint64_t b = tc::smem_desc(sx + C::kTileBytes + box * C::kABox + in, 1024, tc::kLayoutSw128);
               tc::mma_f16(d_v, a, b, kIdescV, (kc > 0 || ks > 0) ? 1u : 0u);
             }
-            tc::commit(&bars.sempty[s]);
+            tc::commit(&bars.empty[s]);  // the chunk is consumed once these MMAs complete
           }
           if (!ok) break;
           tc::commit(&bars.v_ready);
@@ -242,25 +246,24 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         if (kDoExpand) {
           if (!tc_wait(&bars.vsm_ready, j & 1, args.err, abort)) break;
           tc::fence_after_sync();
-          const uint32_t sv = smem_u32(vsm);
-          for (int t = 0; t < nn; ++t, ++ge, ++nt) {
-            const int e = ge % kEStages;
-            const uint32_t buf = nt & 1;
-            if (!tc_wait(&bars.efull[e], (ge / kEStages) & 1, args.err, abort) ||
-                (nt >= 2 && !tc_wait(&bars.acc_empty[buf], ((nt / 2) - 1) & 1, args.err, abort))) {
+          for (int t = 0; t < nn; ++t, ++g, ++nt) {
+            const int s = g % kSlots;
+            const uint32_t buf = nt % kAccBufs;
+            if (!tc_wait(&bars.full[s], (g / kSlots) & 1, args.err, abort) ||
+                (nt >= kAccBufs && !tc_wait(&bars.acc_empty[buf], ((nt / kAccBufs) - 1) & 1, args.err, abort))) {
               ok = false;
               break;
             }
             tc::fence_after_sync();
-            const uint32_t sb = smem_u32(ering + e * C::kEBytes + C::kYBytes);
-            const uint32_t d_y = tmem + 128u * (buf + 1);
+            const uint32_t sb = smem_u32(ring + s * C::kSlotBytes + C::kTileBytes);
+            const uint32_t d_y = tmem + 128u + kTcNT * buf;
 #pragma unroll
             for (int ks = 0; ks < R / 16; ++ks) {
               const uint64_t b = tc::smem_desc(sb + ks * 32, C::kBSbo, C::kBLayout);
               tc::mma_f16(d_y, tc::smem_desc(sv + ks * 32, 1024, tc::kLayoutSw128), b, kIdescY, ks > 0 ? 1u : 0u);
               tc::mma_f16(d_y, tc::smem_desc(sv + (R / 16 + ks) * 32, 1024, tc::kLayoutSw128), b, kIdescY, 1u);
             }
-            tc::commit(&bars.acc_full[buf]);
+            tc::commit(&bars.acc_full[buf]);  // the epilogue releases the slot (it also holds the y tile)
           }
         }
       }
@@ -278,14 +281,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int row = quarter * 32 + lane;   // row of the item this thread owns
     const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
     const int ew = warp - 2;
-    uint32_t ge = 0, nt = 0, j = 0;
-    bool stored = false;
+    uint32_t g = 0, nt = 0, j = 0;
     for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++j) {
       const int4 it = pv.items[item];
       const int row0 = it.y, count = it.z;
       const bool valid = row < count;
       const int64_t grow = static_cast<int64_t>(row0) + row;
       float v[R];
+      g += nk;  // the shrink fills of this item are the MMA warp's
       if (kDoShrink) {
         tc_wait(&bars.v_ready, j & 1, args.err, abort);
         __syncwarp();
@@ -349,27 +352,30 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         named_sync(kEpiBar, 128);
         if (ew == 0 && lane == 0) mbar_arrive(&bars.vsm_ready);
 
-        for (int t = 0; t < nn; ++t, ++ge, ++nt) {
-          const int e = ge % kEStages;
-          const uint32_t buf = nt & 1;
-          tc_wait(&bars.efull[e], (ge / kEStages) & 1, args.err, abort);
-          tc_wait(&bars.acc_full[buf], (nt / 2) & 1, args.err, abort);
+        for (int t = 0; t < nn; ++t, ++g, ++nt) {
+          const int s = g % kSlots;
+          const uint32_t buf = nt % kAccBufs;
+          tc_wait(&bars.full[s], (g / kSlots) & 1, args.err, abort);
+          tc_wait(&bars.acc_full[buf], (nt / kAccBufs) & 1, args.err, abort);
           __syncwarp();
           tc::fence_after_sync();
           const bool live = !*reinterpret_cast<volatile int*>(abort);
-          uint8_t* st = ering + e * C::kEBytes;
+          uint8_t* st = ring + s * C::kSlotBytes;
           const uint32_t ybase = smem_u32(st);
+          const int64_t col = args.n0 + t * kTcNT;
+          // boxes of this tile inside the column block (N is a multiple of 64)
+          const int nbox = min(kBoxes, (args.N - t * kTcNT) / kBoxCols);
 #pragma unroll
           for (int c32 = 0; c32 < kTcNT / 32; ++c32) {
             uint32_t d0[16], d1[16];
-            tc::ld16(tmem + lane_addr + 128u * (buf + 1) + 32 * c32, d0);
-            tc::ld16(tmem + lane_addr + 128u * (buf + 1) + 32 * c32 + 16, d1);
+            tc::ld16(tmem + lane_addr + 128u + kTcNT * buf + 32 * c32, d0);
+            tc::ld16(tmem + lane_addr + 128u + kTcNT * buf + 32 * c32 + 16, d1);
             tc::wait_ld();
 #pragma unroll
             for (int cc = 0; cc < 4; ++cc) {  // 8-column chunks of this 32-column group
-              const int chunk = c32 * 4 + cc;  // 0..15
+              const int chunk = c32 * 4 + cc;  // 16-byte chunk of the row
               const int box = chunk >> 3, cb = chunk & 7;
-              const uint32_t addr = ybase + box * C::kYBox + row * 128 + ((cb ^ (row & 7)) << 4);
+              const uint32_t addr = ybase + box * C::kBoxBytes + row * 128 + ((cb ^ (row & 7)) << 4);
               const uint4 yo = lds128(addr);
               const uint32_t* dd = cc < 2 ? d0 : d1;
               const int o = (cc & 1) * 8;
@@ -384,75 +390,88 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                                     y2.y + scale_up * __uint_as_float(dd[o + 5]));
               out.w = Mma<DT>::pack(y3.x + scale_up * __uint_as_float(dd[o + 6]),
                                     y3.y + scale_up * __uint_as_float(dd[o + 7]));
-              if (count == kTcRows) {
+              if (box >= nbox) {
+                // outside the column block: neither written back nor stored
+              } else if (count == kTcRows) {
                 asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(out.x), "r"(out.y),
                              "r"(out.z), "r"(out.w)
                              : "memory");
               } else if (valid && live) {
-                const int64_t off = grow * args.ldy + args.n0 + t * kTcNT + chunk * 8;
+                const int64_t off = grow * args.ldy + col + chunk * 8;
                 *reinterpret_cast<uint4*>(args.y + off) = out;
                 for (int q = 0; q < args.num_peers; ++q) *reinterpret_cast<uint4*>(args.peers[q] + off) = out;
               }
             }
           }
           tc::fence_before_sync();
+          if (count == kTcRows) tc::fence_proxy_async();  // this warp's rows, for the TMA store
           __syncwarp();
-          if (lane == 0) mbar_arrive(&bars.acc_empty[buf]);
-          if (count == kTcRows) tc::fence_proxy_async();
-          named_sync(kEpiBar, 128);
-          const bool full_live = count == kTcRows && !*reinterpret_cast<volatile int*>(abort);
-          if (ew == 0 && lane == 0 && full_live) {
-            tc::tma_store_2d(&tmY, st, args.n0 + t * kTcNT, row0);
-            tc::tma_store_2d(&tmY, st + C::kYBox, args.n0 + t * kTcNT + 64, row0);
-            tc::bulk_commit();
-            stored = true;
-          }
-          if (ew == 0 && lane == 0) {
-            // The tile is complete in shared memory (barrier above): the
-            // exchange warps may copy it out while the next tile is computed.
-            if (args.num_peers > 0) mbar_arrive(&bars.xready[e]);
-            if (full_live) tc::bulk_wait_read0();
-            mbar_arrive(&bars.eempty[e]);
+          // The warps go on to the next tile independently; the store warp
+          // takes the tile once all four have arrived.
+          if (lane == 0) {
+            mbar_arrive(&bars.acc_empty[buf]);
+            mbar_arrive(&bars.xready[s]);
           }
         }
       }
     }
-    if (stored) tc::bulk_wait0();
     // Plain stores into the peers' y (short items) are ordered before
     // whatever this thread's kernel completion is followed by.
     if (args.num_peers > 0) __threadfence_system();
-  } else if (args.num_peers > 0) {
-    // ------------------------------------------------------ exchange ----
-    // Tensor parallel: every full 128 x 128 tile also goes to every other
-    // rank's y over NVLink, 256 contiguous bytes per row, 16 threads per row
-    // (rows of a short item were stored by the epilogue itself).  Each warp
-    // releases the y stage when its share of the copy is issued; the values
-    // are in registers by then, so the stage may be refilled.
+  } else if (args.num_peers > 0 || warp == 6) {
+    // ------------------------------------------------ store / exchange ----
+    // Warp 6 lane 0 TMA-stores each finished full tile from its slot, waits
+    // until the store has read the slot and releases it, so the epilogue
+    // never waits on a store.  Tensor parallel: warps 6-9 also copy the tile
+    // into every other rank's y over NVLink, 128 contiguous bytes per row
+    // and box (rows of a short item were stored by the epilogue itself).
     const int xw = warp - 6;
-    uint32_t ge = 0;
+    const bool tp = args.num_peers > 0;
+    const bool leader = xw == 0 && lane == 0;
+    bool stored = false;
+    uint32_t g = 0, xphase = 0;  // bit s: parity of the next xready[s] phase
     for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
       const int4 it = pv.items[item];
       const int row0 = it.y, count = it.z;
-      for (int t = 0; t < nn; ++t, ++ge) {
-        const int e = ge % kEStages;
-        const bool ok = tc_wait(&bars.xready[e], (ge / kEStages) & 1, args.err, abort);
-        if (ok && count == kTcRows && !*reinterpret_cast<volatile int*>(abort)) {
-          const uint32_t ybase = smem_u32(ering + e * C::kEBytes);
-          const int64_t col = args.n0 + t * kTcNT;
-#pragma unroll 4
-          for (int i = 0; i < (kTcRows * 16) / (kXchWarps * 32); ++i) {
-            const int idx = (xw * 32 + lane) + i * (kXchWarps * 32);
-            const int r = idx >> 4, c16 = idx & 15, box = c16 >> 3, cb = c16 & 7;
-            const uint4 val = lds128(ybase + box * C::kYBox + r * 128 + ((cb ^ (r & 7)) << 4));
-            const int64_t off = (static_cast<int64_t>(row0) + r) * args.ldy + col + c16 * 8;
-            for (int q = 0; q < args.num_peers; ++q) *reinterpret_cast<uint4*>(args.peers[q] + off) = val;
+      g += nk;
+      for (int t = 0; t < nn; ++t, ++g) {
+        const int s = g % kSlots;
+        const bool ok = tc_wait(&bars.xready[s], (xphase >> s) & 1u, args.err, abort);
+        xphase ^= 1u << s;
+        tc::fence_after_sync();
+        const bool full_live = ok && count == kTcRows && !*reinterpret_cast<volatile int*>(abort);
+        const uint32_t ybase = smem_u32(ring + s * C::kSlotBytes);
+        const int64_t col = args.n0 + t * kTcNT;
+        const int nbox = min(kBoxes, (args.N - t * kTcNT) / kBoxCols);
+        if (leader && full_live) {
+          for (int b = 0; b < nbox; ++b)
+            tc::tma_store_2d(&tmY, ring + s * C::kSlotBytes + b * C::kBoxBytes, static_cast<int>(col) + b * kBoxCols,
+                             row0);
+          tc::bulk_commit();
+          stored = true;
+        }
+        if (tp && full_live) {
+          for (int b = 0; b < nbox; ++b) {
+#pragma unroll
+            for (int i = 0; i < (kTcRows * 8) / (kXchWarps * 32); ++i) {
+              const int idx = (xw * 32 + lane) + i * (kXchWarps * 32);
+              const int r = idx >> 3, c16 = idx & 7;
+              const uint4 val = lds128(ybase + b * C::kBoxBytes + r * 128 + ((c16 ^ (r & 7)) << 4));
+              const int64_t off = (static_cast<int64_t>(row0) + r) * args.ldy + col + b * kBoxCols + c16 * 8;
+              for (int q = 0; q < args.num_peers; ++q) *reinterpret_cast<uint4*>(args.peers[q] + off) = val;
+            }
           }
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&bars.eempty[e]);
+        if (leader && full_live) tc::bulk_wait_read0();
+        if (tp)
+          named_sync(kXchBar, kXchWarps * 32);
+        else
+          __syncwarp();
+        if (leader) mbar_arrive(&bars.empty[s]);
       }
     }
-    __threadfence_system();
+    if (stored) tc::bulk_wait0();
+    if (tp) __threadfence_system();
   }
   tc::fence_before_sync();
   __syncthreads();

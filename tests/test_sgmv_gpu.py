@@ -1,4 +1,4 @@
-"""SGMV on the tensor-core path (ranks 16 / 32, K % 64 == 0, N % 128 == 0)
+"""SGMV on the tensor-core path (ranks 16 / 32, K % 64 == 0, N % 64 == 0)
 against the oracle: ragged segments that straddle the 128-row items, holes,
 slot -1 segments, both 16-bit types, strided y, and the C ABI."""
 
@@ -68,6 +68,9 @@ CASES = [
     ([128, 300, 37, 0, 256, 1], 512, 256),
     ([5, 129, 127, 640], 1024, 384),
     ([128] * 3, 192, 128),
+    ([200, 57], 128, 192),  # N a multiple of 64, not of 128
+    ([64], 64, 64),
+    ([130] * 160, 128, 128),  # 320 items: more than one per SM, the ring wraps across items
 ]
 
 
