@@ -55,9 +55,11 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["mixed_decode", "sgmv_prefill", "decode_set"],
+    ap.add_argument("--workload", choices=["mixed_decode", "sgmv_prefill", "decode_set", "e2e_decode"],
                     default="mixed_decode",
-                    help="mixed_decode is the headline; the others print their own line (1 GPU)")
+                    help="mixed_decode is the headline; the others print their own line")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="e2e_decode: rows per GPU (default 8 on one GPU, 64 per replica on several)")
     ap.add_argument("--only", default=None,
                     help="restrict to one projection (e.g. gate_proj), for profiling a small case")
     return ap.parse_args()
@@ -783,12 +785,105 @@ def run_sgmv_tp(args):
     return 0
 
 
+def run_e2e(args):
+    """Config 5: mixed-adapter greedy decode on a random-init Mistral-7B
+    architecture (32 layers, NF4 base linears, rank-16 adapters on all seven
+    projections), one adapter per row, prompts of 128 random token ids, 128
+    new tokens per row.  One GPU: batch 8 with 8 adapters; several GPUs:
+    data-parallel replicas (one process per GPU, no collective on the data
+    path) with batch 64 and 64 adapters each.  A step is one whole generation
+    (prefill + 127 graph-replayed decode steps), timed with CUDA events on
+    each rank, max over ranks; value = all ranks' new tokens / that time."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from persona import ops
+    from persona.adapter_pool import AdapterPool
+    from persona.engine import Request, StaticBatchEngine
+    from persona.mistral import MistralConfig, MistralLoRAModel
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
+    B = args.batch or (8 if world == 1 else 64)
+    D, prompt, new = B, 128, 128
+    cfg = MistralConfig()
+    pool = AdapterPool(max_slots=D, r=16, device=dev)
+    g = torch.Generator(device=dev)
+    g.manual_seed(SEED * 100 + rank)
+    for i in range(D):
+        pool.load_random_adapter(f"persona{i}", generator=g)
+    model = MistralLoRAModel(cfg, pool, dev, seed=SEED + rank)
+    eng = StaticBatchEngine(model, pool, max_batch=B, max_seq_len=prompt + new)
+    gen = torch.Generator().manual_seed(SEED * 10 + rank)
+    reqs = [Request(f"r{i}", f"persona{i % D}", torch.randint(0, cfg.vocab, (prompt,), generator=gen).tolist(),
+                    slot=pool.name_to_slot[f"persona{i % D}"]) for i in range(B)]
+    # a step is a whole generation (~0.3 s): at most 10 timed, 3 to 20 warm-up
+    warm, steps = min(max(3, args.warmup), 20), min(max(1, args.steps), 10)
+    for _ in range(warm):
+        eng.run_static_generate(reqs, max_new_tokens=new)
+    if world > 1:
+        dist.barrier(device_ids=[local])
+    torch.cuda.synchronize()
+    runs = [eng.run_static_generate(reqs, max_new_tokens=new) for _ in range(steps)]
+    ops.check_errors(dev)
+    ms = sum(r["prefill_ms"] + r["decode_ms"] for r in runs) / steps
+    pre = sum(r["prefill_ms"] for r in runs) / steps
+    dec = sum(r["decode_ms"] for r in runs) / steps
+    t = torch.tensor([ms, pre, dec], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, pre, dec = (float(v) for v in t.tolist())
+    # bytes one decode step must stream: the NF4 base weights and the LM head,
+    # the adapters the batch uses (all 7 projections, 32 layers) and the KV
+    # cache at the mean length
+    per_step = model.base_bytes()
+    r = 16
+    lora_per_adapter = sum(r * (k + n) * 2 for k, n in (
+        (cfg.hidden, cfg.q_dim), (cfg.hidden, cfg.kv_dim), (cfg.hidden, cfg.kv_dim), (cfg.q_dim, cfg.hidden),
+        (cfg.hidden, cfg.intermediate), (cfg.hidden, cfg.intermediate), (cfg.intermediate, cfg.hidden)))
+    per_step += lora_per_adapter * cfg.num_layers * len({q.slot for q in reqs})
+    per_step += B * cfg.num_layers * 2 * cfg.kv_dim * 2 * (prompt + new / 2)
+    step_ms = dec / (new - 1)
+    peak, _ = load_peaks()
+    if rank == 0:
+        print(json.dumps({
+            "workload": "e2e_decode", "metric": "mixed-adapter decode tokens/s",
+            "value": world * B * new / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world, "steps": steps,
+            "warmup": warm, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "dtype": "f16 (NF4 base weights)", "data": "synthetic: random-init weights and adapters, random ids",
+            "config": {"workload": "Mistral-7B architecture, 32 layers, NF4 base, rank-16 adapters on q/k/v/o/"
+                                   "gate/up/down, greedy", "batch_per_gpu": B, "adapters": D,
+                       "prompt_tokens": prompt, "new_tokens": new,
+                       "parallelism": f"dp{world} replicas" if world > 1 else "1 GPU"},
+            "prefill_ms": pre, "decode_ms": dec, "decode_ms_per_token_step": step_ms,
+            "roofline": {"bound": "hbm", "bytes_per_decode_step": per_step,
+                         "achieved": per_step / (step_ms * 1e-3) / 1e9, "peak": peak, "unit": "GB/s",
+                         "frac": per_step / (step_ms * 1e-3) / 1e9 / peak},
+            "gpu_launches_per_decode_step": 13 * cfg.num_layers + 5,
+        }), flush=True)
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     global ONLY
     args = parse_args()
     ONLY = args.only
     if args.impl == "reference":
         return run_reference(args)
+    if args.workload == "e2e_decode":
+        return run_e2e(args)
     if args.workload == "sgmv_prefill" and args.gpus > 1:
         return run_sgmv_tp(args)
     if args.workload != "mixed_decode":

@@ -222,6 +222,70 @@ int persona_ipc_export(const void* ptr, void* handle, size_t* offset);
 int persona_ipc_import(const void* handle, size_t offset, void** ptr, void** base);
 int persona_ipc_close(void* base);
 
+/* ---- NF4 base linears ------------------------------------------------------
+ * The base weights under the LoRA layers of the end-to-end decode.  The
+ * reference runs them through bitsandbytes' Linear4bit (reference
+ * bench/e2e.py:70-90: nf4, blocksize 64, double-quantised scales, fp16
+ * compute) as MultiLoRALinear.base (persona/lora_layer.py:30-45); these entry
+ * points replace that layer.  fp16 only; N and K multiples of 128.
+ *
+ * Storage, per 128 x 128 tile of W[N, K], tiles of a row of tiles adjacent:
+ * PERSONA_NF4_CHUNK_BYTES bytes = 8192 bytes of 4-bit codes in the A-fragment
+ * order of mma.m16n8k16, 256 int8 scale codes (one per 64 weights of a row),
+ * an fp32 scale step s127 and 12 zero bytes.  A block's scale is
+ * f32(code) * s127 + offset, offset one fp32 per matrix in device memory.  */
+#define PERSONA_NF4_CHUNK_BYTES 8464
+#define PERSONA_NF4_MAX_PROBLEMS 4
+size_t persona_nf4_packed_bytes(int64_t N, int64_t K);
+size_t persona_nf4_quantize_workspace_size(int64_t N, int64_t K);
+/* w: fp16 [N, K], row stride ldw (a multiple of 8), 16-byte aligned;
+ * packed: persona_nf4_packed_bytes(N, K); offset: one device float.         */
+int persona_nf4_quantize(const void* w, int64_t ldw, int64_t N, int64_t K, void* packed, float* offset,
+                         void* workspace, size_t workspace_bytes, cudaStream_t stream);
+/* W[n, k] = fp16(fp32(NF4 value) * scale) into w (row stride ldw).          */
+int persona_nf4_dequantize(const void* packed, const float* offset, int64_t N, int64_t K, void* w, int64_t ldw,
+                           cudaStream_t stream);
+/* One base linear of a launch: y[M, N] = x[M, K] W^T, fp32 accumulate, one
+ * rounding to fp16.  x rows 16-byte aligned (ldx a multiple of 8).          */
+typedef struct persona_nf4_problem {
+  const void* packed;
+  const float* offset;
+  const void* x;
+  int64_t ldx;
+  void* y;
+  int64_t ldy;
+  int64_t N;
+  int64_t K;
+} persona_nf4_problem;
+/* Workspace of persona_nf4_linear: zero-filled before its first use (calls
+ * leave its counters at zero again); one launch at a time per workspace.    */
+size_t persona_nf4_linear_workspace_size(const persona_nf4_problem* problems, int num_problems);
+/* Up to PERSONA_NF4_MAX_PROBLEMS linears in one launch (e.g. q / k / v on the
+ * same x); any M (launches of at most 64 rows each).                        */
+int persona_nf4_linear(const persona_nf4_problem* problems, int num_problems, int64_t M, void* workspace,
+                       size_t workspace_bytes, int32_t* dev_err, cudaStream_t stream);
+
+/* ---- end-to-end decode helpers -------------------------------------------
+ * Fused elementwise steps of the Mistral-7B decoder around the LoRA layers,
+ * where the reference runs Hugging Face's modules (reference
+ * persona/engine.py:101-107 calls model.generate).  fp16, head dim 128.
+ * add_rmsnorm: h += delta (delta may be NULL), out = w * fp16(h / rms(h)),
+ *   rows of D (a multiple of 8) elements.
+ * rope_cache: rows r = b * per_seq + i of q [rows, Hq, 128], k, v [rows, Hkv,
+ *   128] are at position *start + i of sequence b: rotate q and k in place
+ *   (rotate-half, base theta) and store k, v into the caches [B, Hkv, L, 128].
+ * silu_mul: out = fp16(silu(g)) * u over n elements (a multiple of 8).
+ * decode_attention: one new token per sequence, softmax(q K^T scale) V over
+ *   the first *len cache positions; q, out [B, Hq, 128], Hq / Hkv <= 8.      */
+int persona_add_rmsnorm(void* h, const void* delta, const void* w, void* out, int64_t rows, int64_t D, float eps,
+                        cudaStream_t stream);
+int persona_rope_cache(void* q, void* k, const void* v, void* k_cache, void* v_cache, const int32_t* start,
+                       int64_t rows, int64_t per_seq, int64_t Hq, int64_t Hkv, int64_t L, float theta,
+                       cudaStream_t stream);
+int persona_silu_mul(const void* g, const void* u, void* out, int64_t n, cudaStream_t stream);
+int persona_decode_attention(const void* q, const void* k_cache, const void* v_cache, const int32_t* len, void* out,
+                             int64_t B, int64_t Hq, int64_t Hkv, int64_t L, float scale, cudaStream_t stream);
+
 /* ---- warm-up GEMV ---------------------------------------------------------
  * y[n] = W[n, :] @ x (fp16, fp32 accumulate).  Replaces
  * persona::gemv_fp16_cuda (csrc/gemv_fp16.cu:33-50), kept so that

@@ -193,11 +193,6 @@ __device__ void plan_units(SplitShared& sh, const SplitArgs& a, int n_items, int
   sh.units = s_units + e_units;
 }
 
-__device__ __forceinline__ uint16_t lds16(uint32_t addr) {
-  uint16_t v;
-  asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(addr));
-  return v;
-}
 __device__ __forceinline__ void sts32(uint32_t addr, uint32_t v) {
   asm volatile("st.shared.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
 }

@@ -460,6 +460,172 @@ void sgmv_fused_op(const at::Tensor& x, const at::Tensor& a_pool, const at::Tens
 }
 }  // namespace
 
+namespace {
+// ------------------------------------------------------------------ NF4 ---
+// Base linears of the end-to-end decode (persona_nf4_* in the C ABI).
+std::tuple<at::Tensor, at::Tensor> nf4_quantize_op(const at::Tensor& w) {
+  const char* op = "nf4_quantize";
+  TORCH_CHECK(w.is_cuda() && w.dim() == 2 && w.stride(1) == 1, op, ": w must be a CUDA [N, K] matrix");
+  TORCH_CHECK(w.scalar_type() == at::kHalf, op, ": w must be float16");
+  const int64_t N = w.size(0), K = w.size(1);
+  TORCH_CHECK(N % 128 == 0 && K % 128 == 0 && N > 0 && K > 0, op, ": N and K must be multiples of 128");
+  const at::cuda::OptionalCUDAGuard guard(w.device());
+  auto u8 = w.options().dtype(at::kByte);
+  at::Tensor packed = at::empty({N / 128, K / 128, PERSONA_NF4_CHUNK_BYTES}, u8);
+  at::Tensor offset = at::empty({1}, w.options().dtype(at::kFloat));
+  at::Tensor ws = at::empty({static_cast<int64_t>(persona_nf4_quantize_workspace_size(N, K))}, u8);
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  check_status(persona_nf4_quantize(w.data_ptr(), row_stride(w), N, K, packed.data_ptr(), offset.data_ptr<float>(),
+                                    ws.data_ptr(), ws.numel(), stream),
+               op);
+  after_launch(w.get_device(), op, stream);
+  return {packed, offset};
+}
+
+void check_nf4_weight(const at::Tensor& packed, const at::Tensor& offset, int64_t N, int64_t K, const char* op) {
+  TORCH_CHECK(packed.is_cuda() && offset.is_cuda(), op, ": tensors must be CUDA");
+  TORCH_CHECK(packed.scalar_type() == at::kByte && packed.is_contiguous() && packed.dim() == 3 &&
+                  packed.size(0) * 128 == N && packed.size(1) * 128 == K && packed.size(2) == PERSONA_NF4_CHUNK_BYTES,
+              op, ": packed must be uint8 [N/128, K/128, ", PERSONA_NF4_CHUNK_BYTES, "]");
+  TORCH_CHECK(offset.scalar_type() == at::kFloat && offset.numel() == 1, op, ": offset must be one float32");
+}
+
+at::Tensor nf4_dequantize_op(const at::Tensor& packed, const at::Tensor& offset, int64_t N, int64_t K) {
+  const char* op = "nf4_dequantize";
+  check_nf4_weight(packed, offset, N, K, op);
+  const at::cuda::OptionalCUDAGuard guard(packed.device());
+  at::Tensor w = at::empty({N, K}, packed.options().dtype(at::kHalf));
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  check_status(persona_nf4_dequantize(packed.data_ptr(), offset.data_ptr<float>(), N, K, w.data_ptr(), K, stream),
+               op);
+  after_launch(packed.get_device(), op, stream);
+  return w;
+}
+
+// Per-device workspace of the NF4 linear: zero-filled when made or grown
+// (its counters must start at zero; the kernel leaves them at zero).
+at::Tensor nf4_workspace(size_t bytes, const at::Tensor& like) {
+  static std::mutex mu;
+  static std::vector<at::Tensor> cache(64);
+  const int dev = like.get_device();
+  TORCH_CHECK(dev >= 0 && dev < 64, "nf4_linear: device index out of range");
+  std::lock_guard<std::mutex> lock(mu);
+  at::Tensor& t = cache[dev];
+  if (!t.defined() || static_cast<size_t>(t.numel()) < bytes)
+    t = at::zeros({static_cast<int64_t>(bytes)}, like.options().dtype(at::kByte));
+  return t;
+}
+
+void nf4_linear_op(const at::Tensor& x, at::TensorList packed, at::TensorList offsets, at::TensorList ys) {
+  const char* op = "nf4_linear";
+  const int n = static_cast<int>(packed.size());
+  TORCH_CHECK(n >= 1 && n <= PERSONA_NF4_MAX_PROBLEMS, op, ": 1 to ", PERSONA_NF4_MAX_PROBLEMS, " weights");
+  TORCH_CHECK(static_cast<int>(offsets.size()) == n && static_cast<int>(ys.size()) == n, op,
+              ": one offset and one y per weight");
+  TORCH_CHECK(x.is_cuda() && x.dim() == 2 && x.stride(1) == 1 && x.scalar_type() == at::kHalf, op,
+              ": x must be a CUDA float16 [M, K] matrix with unit inner stride");
+  const int64_t M = x.size(0), K = x.size(1);
+  persona_nf4_problem probs[PERSONA_NF4_MAX_PROBLEMS];
+  for (int i = 0; i < n; ++i) {
+    const at::Tensor& y = ys[i];
+    TORCH_CHECK(y.is_cuda() && y.dim() == 2 && y.stride(1) == 1 && y.scalar_type() == at::kHalf && y.size(0) == M,
+                op, ": y must be a CUDA float16 [M, N] matrix with unit inner stride");
+    const int64_t N = y.size(1);
+    check_nf4_weight(packed[i], offsets[i], N, K, op);
+    TORCH_CHECK(packed[i].get_device() == x.get_device() && y.get_device() == x.get_device(), op,
+                ": tensors must be on one device");
+    probs[i] = persona_nf4_problem{packed[i].data_ptr(), offsets[i].data_ptr<float>(), x.data_ptr(), row_stride(x),
+                                   y.data_ptr(), row_stride(y), N, K};
+  }
+  const at::cuda::OptionalCUDAGuard guard(x.device());
+  const int dev = x.get_device();
+  raise_pending(dev, op);
+  if (M == 0) return;
+  at::Tensor ws = nf4_workspace(persona_nf4_linear_workspace_size(probs, n), x);
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  check_status(persona_nf4_linear(probs, n, M, ws.data_ptr(), ws.numel(), error_word_device(dev), stream), op);
+  after_launch(dev, op, stream);
+}
+}  // namespace
+
+namespace {
+// ---------------------------------------------------- decode helpers ----
+void check_half_cuda(const at::Tensor& t, const char* op) {
+  TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kHalf && t.is_contiguous(), op,
+              ": tensors must be contiguous CUDA float16");
+}
+
+void add_rmsnorm_op(at::Tensor& h, const c10::optional<at::Tensor>& delta, const at::Tensor& w, at::Tensor& out,
+                    double eps) {
+  const char* op = "add_rmsnorm";
+  check_half_cuda(h, op);
+  check_half_cuda(w, op);
+  check_half_cuda(out, op);
+  const int64_t D = h.size(-1), rows = h.numel() / D;
+  TORCH_CHECK(w.numel() == D && out.numel() == h.numel(), op, ": shape mismatch");
+  if (delta.has_value()) {
+    check_half_cuda(*delta, op);
+    TORCH_CHECK(delta->numel() == h.numel(), op, ": delta shape mismatch");
+  }
+  const at::cuda::OptionalCUDAGuard guard(h.device());
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  check_status(persona_add_rmsnorm(h.data_ptr(), delta.has_value() ? delta->data_ptr() : nullptr, w.data_ptr(),
+                                   out.data_ptr(), rows, D, static_cast<float>(eps), stream),
+               op);
+}
+
+void rope_cache_op(at::Tensor& q, at::Tensor& k, const at::Tensor& v, at::Tensor& k_cache, at::Tensor& v_cache,
+                   const at::Tensor& start, int64_t per_seq, double theta) {
+  const char* op = "rope_cache";
+  for (const at::Tensor* t : std::initializer_list<const at::Tensor*>{&q, &k, &v, &k_cache, &v_cache})
+    check_half_cuda(*t, op);
+  TORCH_CHECK(q.dim() == 3 && k.dim() == 3 && v.sizes() == k.sizes() && q.size(2) == 128 && k.size(2) == 128 &&
+                  q.size(0) == k.size(0),
+              op, ": q [rows, Hq, 128], k / v [rows, Hkv, 128]");
+  TORCH_CHECK(k_cache.dim() == 4 && v_cache.sizes() == k_cache.sizes() && k_cache.size(1) == k.size(1) &&
+                  k_cache.size(3) == 128 && k_cache.size(0) * per_seq == q.size(0),
+              op, ": caches [B, Hkv, L, 128] with B * per_seq rows");
+  TORCH_CHECK(start.is_cuda() && start.scalar_type() == at::kInt && start.numel() >= 1, op,
+              ": start must be a CUDA int32 scalar");
+  const at::cuda::OptionalCUDAGuard guard(q.device());
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  check_status(persona_rope_cache(q.data_ptr(), k.data_ptr(), v.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
+                                  start.data_ptr<int32_t>(), q.size(0), per_seq, q.size(1), k.size(1),
+                                  k_cache.size(2), static_cast<float>(theta), stream),
+               op);
+}
+
+void silu_mul_op(const at::Tensor& g, const at::Tensor& u, at::Tensor& out) {
+  const char* op = "silu_mul";
+  check_half_cuda(g, op);
+  check_half_cuda(u, op);
+  check_half_cuda(out, op);
+  TORCH_CHECK(g.numel() == u.numel() && out.numel() == g.numel(), op, ": shape mismatch");
+  const at::cuda::OptionalCUDAGuard guard(g.device());
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  check_status(persona_silu_mul(g.data_ptr(), u.data_ptr(), out.data_ptr(), g.numel(), stream), op);
+}
+
+void decode_attention_op(const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& v_cache,
+                         const at::Tensor& len, at::Tensor& out, double scale) {
+  const char* op = "decode_attention";
+  for (const at::Tensor* t : std::initializer_list<const at::Tensor*>{&q, &k_cache, &v_cache, &out})
+    check_half_cuda(*t, op);
+  TORCH_CHECK(q.dim() == 3 && q.size(2) == 128 && out.sizes() == q.sizes(), op, ": q, out [B, Hq, 128]");
+  TORCH_CHECK(k_cache.dim() == 4 && v_cache.sizes() == k_cache.sizes() && k_cache.size(0) == q.size(0) &&
+                  k_cache.size(3) == 128,
+              op, ": caches [B, Hkv, L, 128]");
+  TORCH_CHECK(len.is_cuda() && len.scalar_type() == at::kInt && len.numel() >= 1, op,
+              ": len must be a CUDA int32 scalar");
+  const at::cuda::OptionalCUDAGuard guard(q.device());
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  check_status(persona_decode_attention(q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), len.data_ptr<int32_t>(),
+                                        out.data_ptr(), q.size(0), q.size(1), k_cache.size(1), k_cache.size(2),
+                                        static_cast<float>(scale), stream),
+               op);
+}
+}  // namespace
+
 TORCH_LIBRARY(persona, m) {
   // Reference schemas, unchanged (csrc/bindings.cpp:19-23).
   m.def("bgmv_shrink(Tensor x, Tensor a_pool, Tensor slots, Tensor(a!) v) -> ()");
@@ -478,9 +644,24 @@ TORCH_LIBRARY(persona, m) {
   m.def("sgmv_expand(Tensor v, Tensor b_pool, Tensor seg_indptr, Tensor seg_slots, Tensor(a!) y) -> ()");
   m.def("sgmv_fused(Tensor x, Tensor a_pool, Tensor b_pool, Tensor seg_indptr, Tensor seg_slots, "
         "Tensor(a!) y) -> ()");
+  m.def("nf4_quantize(Tensor w) -> (Tensor, Tensor)");
+  m.def("nf4_dequantize(Tensor packed, Tensor offset, int N, int K) -> Tensor");
+  m.def("nf4_linear(Tensor x, Tensor[] packed, Tensor[] offsets, Tensor(a!)[] ys) -> ()");
+  m.def("add_rmsnorm(Tensor(a!) h, Tensor? delta, Tensor w, Tensor(b!) out, float eps) -> ()");
+  m.def("rope_cache(Tensor(a!) q, Tensor(b!) k, Tensor v, Tensor(c!) k_cache, Tensor(d!) v_cache, Tensor start, "
+        "int per_seq, float theta) -> ()");
+  m.def("silu_mul(Tensor g, Tensor u, Tensor(a!) out) -> ()");
+  m.def("decode_attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor len, Tensor(a!) out, float scale) -> ()");
 }
 
 TORCH_LIBRARY_IMPL(persona, CUDA, m) {
+  m.impl("nf4_quantize", &nf4_quantize_op);
+  m.impl("nf4_dequantize", &nf4_dequantize_op);
+  m.impl("nf4_linear", &nf4_linear_op);
+  m.impl("add_rmsnorm", &add_rmsnorm_op);
+  m.impl("rope_cache", &rope_cache_op);
+  m.impl("silu_mul", &silu_mul_op);
+  m.impl("decode_attention", &decode_attention_op);
   m.impl("bgmv_shrink", &bgmv_shrink_cuda);
   m.impl("bgmv_expand", &bgmv_expand_cuda);
   m.impl("gemv_fp16", &persona::gemv_fp16_cuda);

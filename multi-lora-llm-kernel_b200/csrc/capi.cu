@@ -7,12 +7,15 @@
 // Nothing here synchronises with the device or allocates device memory.
 #include <cudaTypedefs.h>
 
+#include <cmath>
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
 
 #include "bgmv_args.h"
 #include "common.cuh"
+#include "decode_args.h"
+#include "nf4_args.h"
 #include "plan_layout.h"
 
 namespace persona {
@@ -595,6 +598,217 @@ int persona_sgmv_fused(const void* x, int64_t ldx, const void* a_pool, int64_t a
   return persona_bgmv_fused(x, ldx, a_pool, a_slot_stride, a_row_stride, b_pool, b_slot_stride, row_slots, y, ldy,
                             T, K, N, R, S, dtype, workspace, persona::bgmv_ws_bytes(T), PERSONA_REUSE_PLAN, dev_err,
                             stream);
+}
+
+}  // extern "C"
+
+// ------------------------------------------------------------------ NF4 ---
+namespace {
+struct Nf4Plan {
+  persona::Nf4GemmArgs args;
+  size_t counter_bytes;
+  size_t partial_bytes;
+};
+
+// Splits so that the launch has about four units per SM, at least four
+// chunks (512 of K) per unit.
+int nf4_plan(const persona_nf4_problem* probs, int n, Nf4Plan* out) {
+  using namespace persona;
+  if (n < 1 || n > kNf4MaxProblems || probs == nullptr) return PERSONA_ERR_INVALID_ARG;
+  int64_t chunks = 0, tiles = 0;
+  for (int i = 0; i < n; ++i) {
+    const persona_nf4_problem& p = probs[i];
+    if (p.N <= 0 || p.K <= 0 || p.N % kNf4Tile || p.K % kNf4Tile || p.N > (int64_t{1} << 24) ||
+        p.K > (int64_t{1} << 24))
+      return PERSONA_ERR_SHAPE;
+    chunks += (p.N / kNf4Tile) * (p.K / kNf4Tile);
+    tiles += p.N / kNf4Tile;
+  }
+  int sms = nf4_sm_count();
+  if (sms <= 0) sms = 148;
+  int64_t per = (chunks + 4 * sms - 1) / (4 * sms);
+  if (per < 4) per = 4;
+  Nf4GemmArgs& a = out->args;
+  std::memset(&a, 0, sizeof(a));
+  a.num_problems = n;
+  int64_t units = 0, ctr = 0;
+  for (int i = 0; i < n; ++i) {
+    const int kt = static_cast<int>(probs[i].K / kNf4Tile), nt = static_cast<int>(probs[i].N / kNf4Tile);
+    int splits = static_cast<int>((kt + per - 1) / per);
+    const int cps = (kt + splits - 1) / splits;
+    splits = (kt + cps - 1) / cps;
+    Nf4Problem& q = a.prob[i];
+    q.N = static_cast<int>(probs[i].N);
+    q.K = static_cast<int>(probs[i].K);
+    q.splits = splits;
+    q.chunks_per_split = cps;
+    q.unit_base = static_cast<int>(units);
+    q.counter_base = static_cast<int>(ctr);
+    units += static_cast<int64_t>(nt) * splits;
+    ctr += nt;
+  }
+  if (units > kI32Max) return PERSONA_ERR_SHAPE;
+  a.units = static_cast<int>(units);
+  out->counter_bytes = (static_cast<size_t>(tiles) * 4 + 255) & ~size_t(255);
+  out->partial_bytes = static_cast<size_t>(units) * kNf4Tile * kNf4MaxRows * 4;
+  return PERSONA_OK;
+}
+}  // namespace
+
+extern "C" {
+
+size_t persona_nf4_packed_bytes(int64_t N, int64_t K) {
+  if (N <= 0 || K <= 0 || N % 128 || K % 128) return 0;
+  return static_cast<size_t>(N / 128) * static_cast<size_t>(K / 128) * persona::kNf4ChunkBytes;
+}
+
+size_t persona_nf4_quantize_workspace_size(int64_t N, int64_t K) {
+  if (N <= 0 || K <= 0 || N % 128 || K % 128) return 0;
+  return 256 + static_cast<size_t>(N) * static_cast<size_t>(K / 64) * 4;
+}
+
+int persona_nf4_quantize(const void* w, int64_t ldw, int64_t N, int64_t K, void* packed, float* offset,
+                         void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  using namespace persona;
+  if (w == nullptr || packed == nullptr || offset == nullptr) return PERSONA_ERR_INVALID_ARG;
+  if (N <= 0 || K <= 0 || N % 128 || K % 128 || ldw < K || N > (int64_t{1} << 24) || K > (int64_t{1} << 24))
+    return PERSONA_ERR_SHAPE;
+  if (!aligned16(w) || ldw % 8 || !aligned16(packed) || (reinterpret_cast<uintptr_t>(offset) & 3))
+    return PERSONA_ERR_ALIGNMENT;
+  if (workspace == nullptr || workspace_bytes < persona_nf4_quantize_workspace_size(N, K))
+    return PERSONA_ERR_WORKSPACE;
+  if (!aligned16(workspace)) return PERSONA_ERR_ALIGNMENT;
+  uint32_t* minmax = static_cast<uint32_t*>(workspace);
+  float* absmax = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + 256);
+  if (launch_nf4_absmax(static_cast<const uint16_t*>(w), ldw, static_cast<int>(N), static_cast<int>(K), absmax,
+                        minmax, stream) != cudaSuccess)
+    return PERSONA_ERR_CUDA;
+  if (launch_nf4_pack(static_cast<const uint16_t*>(w), ldw, static_cast<int>(N), static_cast<int>(K), absmax, minmax,
+                      static_cast<uint8_t*>(packed), offset, stream) != cudaSuccess)
+    return PERSONA_ERR_CUDA;
+  return PERSONA_OK;
+}
+
+int persona_nf4_dequantize(const void* packed, const float* offset, int64_t N, int64_t K, void* w, int64_t ldw,
+                           cudaStream_t stream) {
+  using namespace persona;
+  if (packed == nullptr || offset == nullptr || w == nullptr) return PERSONA_ERR_INVALID_ARG;
+  if (N <= 0 || K <= 0 || N % 128 || K % 128 || ldw < K || N > (int64_t{1} << 24) || K > (int64_t{1} << 24))
+    return PERSONA_ERR_SHAPE;
+  if (!aligned16(packed) || !aligned16(w) || ldw % 8) return PERSONA_ERR_ALIGNMENT;
+  return launch_nf4_dequant(static_cast<const uint8_t*>(packed), offset, static_cast<int>(N), static_cast<int>(K),
+                            static_cast<uint16_t*>(w), ldw, stream) == cudaSuccess
+             ? PERSONA_OK
+             : PERSONA_ERR_CUDA;
+}
+
+size_t persona_nf4_linear_workspace_size(const persona_nf4_problem* problems, int num_problems) {
+  Nf4Plan plan;
+  if (nf4_plan(problems, num_problems, &plan) != PERSONA_OK) return 0;
+  return plan.counter_bytes + plan.partial_bytes;
+}
+
+int persona_nf4_linear(const persona_nf4_problem* problems, int num_problems, int64_t M, void* workspace,
+                       size_t workspace_bytes, int32_t* dev_err, cudaStream_t stream) {
+  using namespace persona;
+  Nf4Plan plan;
+  int st = nf4_plan(problems, num_problems, &plan);
+  if (st != PERSONA_OK) return st;
+  if (M < 0 || M > (int64_t{1} << 30)) return PERSONA_ERR_SHAPE;
+  for (int i = 0; i < num_problems; ++i) {
+    const persona_nf4_problem& p = problems[i];
+    if (p.packed == nullptr || p.offset == nullptr || p.x == nullptr || p.y == nullptr)
+      return PERSONA_ERR_INVALID_ARG;
+    if (p.ldx < p.K || p.ldy < p.N) return PERSONA_ERR_SHAPE;
+    if (!aligned16(p.packed) || !aligned16(p.x) || p.ldx % 8 || (reinterpret_cast<uintptr_t>(p.y) & 1) ||
+        (reinterpret_cast<uintptr_t>(p.offset) & 3))
+      return PERSONA_ERR_ALIGNMENT;
+  }
+  if (M == 0) return PERSONA_OK;
+  if (workspace == nullptr || workspace_bytes < plan.counter_bytes + plan.partial_bytes)
+    return PERSONA_ERR_WORKSPACE;
+  if (!aligned16(workspace)) return PERSONA_ERR_ALIGNMENT;
+  Nf4GemmArgs& a = plan.args;
+  a.counters = static_cast<int*>(workspace);
+  a.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + plan.counter_bytes);
+  a.err = dev_err;
+  for (int64_t m0 = 0; m0 < M; m0 += kNf4MaxRows) {
+    const int mc = static_cast<int>(M - m0 < kNf4MaxRows ? M - m0 : kNf4MaxRows);
+    const int m_pad = mc <= 8 ? 8 : mc <= 16 ? 16 : mc <= 32 ? 32 : 64;
+    Nf4Maps maps;
+    std::memset(&maps, 0, sizeof(maps));
+    for (int i = 0; i < num_problems; ++i) {
+      const persona_nf4_problem& p = problems[i];
+      const uint16_t* x = static_cast<const uint16_t*>(p.x) + m0 * p.ldx;
+      if ((st = encode_2d_map(&maps.x[i], x, PERSONA_DTYPE_F16, p.K, mc, p.ldx, 64, m_pad)) != PERSONA_OK) return st;
+      a.prob[i].w = static_cast<const uint8_t*>(p.packed);
+      a.prob[i].offset = p.offset;
+      a.prob[i].y = static_cast<uint16_t*>(p.y) + m0 * p.ldy;
+      a.prob[i].ldy = p.ldy;
+    }
+    a.M = mc;
+    if (launch_nf4_gemm(maps, a, m_pad, stream) != cudaSuccess) return PERSONA_ERR_CUDA;
+  }
+  return PERSONA_OK;
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------- decode helpers ----
+extern "C" {
+
+int persona_add_rmsnorm(void* h, const void* delta, const void* w, void* out, int64_t rows, int64_t D, float eps,
+                        cudaStream_t stream) {
+  if (h == nullptr || w == nullptr || out == nullptr) return PERSONA_ERR_INVALID_ARG;
+  if (rows < 0 || rows > kI32Max || D <= 0 || D % 8 || D > (1 << 20)) return PERSONA_ERR_SHAPE;
+  if (!aligned16(h) || !aligned16(w) || !aligned16(out) || (delta != nullptr && !aligned16(delta)))
+    return PERSONA_ERR_ALIGNMENT;
+  if (rows == 0) return PERSONA_OK;
+  return persona::launch_add_rmsnorm(h, delta, w, out, static_cast<int>(rows), static_cast<int>(D), eps, stream) ==
+                 cudaSuccess
+             ? PERSONA_OK
+             : PERSONA_ERR_CUDA;
+}
+
+int persona_rope_cache(void* q, void* k, const void* v, void* k_cache, void* v_cache, const int32_t* start,
+                       int64_t rows, int64_t per_seq, int64_t Hq, int64_t Hkv, int64_t L, float theta,
+                       cudaStream_t stream) {
+  if (q == nullptr || k == nullptr || v == nullptr || k_cache == nullptr || v_cache == nullptr || start == nullptr)
+    return PERSONA_ERR_INVALID_ARG;
+  if (rows < 0 || rows > kI32Max || per_seq <= 0 || Hq <= 0 || Hkv <= 0 || Hq > 256 || Hkv > 256 || L <= 0 ||
+      L > kI32Max || !(theta > 1.f))
+    return PERSONA_ERR_SHAPE;
+  if (rows == 0) return PERSONA_OK;
+  return persona::launch_rope_cache(q, k, v, k_cache, v_cache, start, static_cast<int>(rows),
+                                    static_cast<int>(per_seq), static_cast<int>(Hq), static_cast<int>(Hkv),
+                                    static_cast<int>(L), std::log2(theta), stream) == cudaSuccess
+             ? PERSONA_OK
+             : PERSONA_ERR_CUDA;
+}
+
+int persona_silu_mul(const void* g, const void* u, void* out, int64_t n, cudaStream_t stream) {
+  if (g == nullptr || u == nullptr || out == nullptr) return PERSONA_ERR_INVALID_ARG;
+  if (n < 0 || n % 8) return PERSONA_ERR_SHAPE;
+  if (!aligned16(g) || !aligned16(u) || !aligned16(out)) return PERSONA_ERR_ALIGNMENT;
+  if (n == 0) return PERSONA_OK;
+  return persona::launch_silu_mul(g, u, out, n, stream) == cudaSuccess ? PERSONA_OK : PERSONA_ERR_CUDA;
+}
+
+int persona_decode_attention(const void* q, const void* k_cache, const void* v_cache, const int32_t* len, void* out,
+                             int64_t B, int64_t Hq, int64_t Hkv, int64_t L, float scale, cudaStream_t stream) {
+  if (q == nullptr || k_cache == nullptr || v_cache == nullptr || len == nullptr || out == nullptr)
+    return PERSONA_ERR_INVALID_ARG;
+  if (B < 0 || B > 65535 || Hkv <= 0 || Hq <= 0 || Hq % Hkv || Hq / Hkv > 8 || Hkv > 65535 || L <= 0 ||
+      L > kI32Max)
+    return PERSONA_ERR_SHAPE;
+  if ((reinterpret_cast<uintptr_t>(k_cache) & 3) || (reinterpret_cast<uintptr_t>(v_cache) & 3) ||
+      (reinterpret_cast<uintptr_t>(q) & 1) || (reinterpret_cast<uintptr_t>(out) & 1))
+    return PERSONA_ERR_ALIGNMENT;
+  if (B == 0) return PERSONA_OK;
+  return persona::launch_decode_attention(q, k_cache, v_cache, len, out, static_cast<int>(B), static_cast<int>(Hq),
+                                          static_cast<int>(Hkv), static_cast<int>(L), scale, stream) == cudaSuccess
+             ? PERSONA_OK
+             : PERSONA_ERR_CUDA;
 }
 
 }  // extern "C"

@@ -1,0 +1,468 @@
+// NF4 base linears for B200 (sm_100a): the quantiser, the dequantiser and
+// the decode GEMM y[M, N] = x[M, K] W^T with W in the tiled NF4 format
+// (nf4_table.h) and M <= 64 rows of x.
+//
+// The reference runs its base linears through bitsandbytes' Linear4bit
+// (reference bench/e2e.py:70-90: nf4, blocksize 64, double-quantised
+// scales, fp16 compute) under MultiLoRALinear.base (persona/lora_layer.py).
+//
+// GEMM design.  At decode sizes the op streams 0.52 bytes per weight from
+// HBM and does 2 M flops per weight, so it is bound by HBM and by the
+// instructions that turn 4-bit codes into tensor-core operands.  The codes
+// are stored in the A-fragment order of mma.sync.m16n8k16, so one 32-bit
+// word of codes is exactly one thread's A fragment for one k-step: four
+// bytes, each mapped by a 256-entry table to the two fp16 NF4 values it
+// holds.  The table sits in shared memory once per lane (entry b of lane l at
+// word 32 b + l), so every lookup is free of bank conflicts.  The fragments
+// never go through shared memory, and the per-block scale is applied to the
+// fp32 partial sum of each 64-wide block (two per 128-wide chunk), not to
+// every weight.  x (M rows, fp16) is the B operand, TMA-loaded per chunk
+// with a 128-byte swizzle so that the B-fragment loads are conflict-free.
+// Tensor-core work per weight is tiny at M <= 64, well inside what the
+// warp-level MMA delivers; staging dequantised tiles in shared memory for
+// tcgen05 would instead cost 4 bytes of shared-memory traffic per weight.
+//
+// Work units: (problem, tile of 128 output rows, split of the K chunks).
+// One CTA per SM, persistent over units (static round robin): a producer
+// warp bulk-copies each 8464-byte chunk and TMA-loads the x chunk into a
+// 6-slot ring; eight compute warps each own 16 rows of the tile.  A split
+// unit writes its fp32 partial tile to the workspace; the last unit of a
+// tile (per-tile counter) sums the partials in split order, so the result
+// does not depend on scheduling, writes y and resets the counter.
+#include <cuda_fp16.h>
+
+#include "common.cuh"
+#include "nf4_args.h"
+#include "tcgen05.cuh"
+
+namespace persona {
+namespace {
+
+constexpr int kNf4Warps = 8;
+constexpr int kNf4Threads = (kNf4Warps + 1) * 32;
+constexpr int kNf4Slots = 6;
+constexpr int kNf4RawPad = 9216;  // chunk area of a slot, padded to 1 KB
+constexpr int kNf4XBox = kNf4MaxRows * 128;
+constexpr int kNf4SlotBytes = kNf4RawPad + 2 * kNf4XBox;
+constexpr int kNf4LutBytes = 256 * 32 * 4;
+constexpr int kNf4Smem = kNf4Slots * kNf4SlotBytes + kNf4LutBytes + 1024;
+constexpr int kNf4EpiBar = 1;
+static_assert(kNf4ChunkBytes % 16 == 0 && kNf4RawPad >= kNf4ChunkBytes, "chunk layout");
+
+__device__ __forceinline__ float h2f(uint32_t bits) { return __half2float(__ushort_as_half(static_cast<uint16_t>(bits))); }
+
+__device__ __forceinline__ int nf4_index(float v, float am) {
+  const float r = am > 0.f ? __fdiv_rn(v, am) : 0.f;
+  int idx = 0;
+#pragma unroll
+  for (int i = 0; i < 15; ++i) idx += r > __uint_as_float(kNf4Mid[i]) ? 1 : 0;
+  return idx;
+}
+
+__device__ __forceinline__ uint32_t nf4_half_bits(int i) {
+  uint32_t h = 0;
+#pragma unroll
+  for (int k = 0; k < 16; ++k) h = i == k ? kNf4Half[k] : h;
+  return h;
+}
+
+// (row, column) of the first of the two weights in code byte q of a chunk.
+__device__ __forceinline__ void nf4_byte_pos(int q, int& row, int& col) {
+  const int j = q & 3, ks = (q >> 2) & 3, lane = (q >> 4) & 31, kh = (q >> 9) & 1, wt = q >> 10;
+  const int g = lane >> 2, t = lane & 3;
+  row = 16 * wt + g + 8 * (j & 1);
+  col = 64 * kh + 16 * ks + 2 * t + 8 * (j >> 1);
+}
+
+// ------------------------------------------------------------ quantiser ----
+__global__ void nf4_minmax_init_kernel(uint32_t* minmax) {
+  if (threadIdx.x == 0) {
+    minmax[0] = 0x7f800000u;  // +inf: no block seen yet
+    minmax[1] = 0u;
+  }
+}
+
+__global__ void nf4_absmax_kernel(const uint16_t* __restrict__ w, int64_t ldw, int N, int K,
+                                  float* __restrict__ absmax, uint32_t* __restrict__ minmax) {
+  const int nb = K / kNf4Block;
+  const int64_t total = static_cast<int64_t>(N) * nb;
+  uint32_t lmin = 0x7f800000u, lmax = 0u;  // absmax >= 0 orders like its bits
+  for (int64_t b = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; b < total;
+       b += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t row = b / nb;
+    const int kb = static_cast<int>(b - row * nb);
+    const uint4* p = reinterpret_cast<const uint4*>(w + row * ldw + kb * kNf4Block);
+    float m = 0.f;
+#pragma unroll
+    for (int i = 0; i < kNf4Block / 8; ++i) {
+      const uint4 q = p[i];
+      const uint32_t v[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) m = fmaxf(m, fmaxf(fabsf(h2f(v[k] & 0xffffu)), fabsf(h2f(v[k] >> 16))));
+    }
+    absmax[b] = m;
+    lmin = min(lmin, __float_as_uint(m));
+    lmax = max(lmax, __float_as_uint(m));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    lmin = min(lmin, __shfl_xor_sync(0xffffffffu, lmin, o));
+    lmax = max(lmax, __shfl_xor_sync(0xffffffffu, lmax, o));
+  }
+  if ((threadIdx.x & 31) == 0) {
+    atomicMin(&minmax[0], lmin);
+    atomicMax(&minmax[1], lmax);
+  }
+}
+
+// One CTA of 256 threads per 128 x 128 tile.
+__global__ void __launch_bounds__(256) nf4_pack_kernel(const uint16_t* __restrict__ w, int64_t ldw, int N, int K,
+                                                       const float* __restrict__ absmax,
+                                                       const uint32_t* __restrict__ minmax,
+                                                       uint8_t* __restrict__ packed, float* __restrict__ offset_out) {
+  const int kc = blockIdx.x, nt = blockIdx.y, kt = K / kNf4Tile;
+  uint8_t* chunk = packed + (static_cast<int64_t>(nt) * kt + kc) * kNf4ChunkBytes;
+  const float off = __fmul_rn(__fadd_rn(__uint_as_float(minmax[0]), __uint_as_float(minmax[1])), 0.5f);
+  const int tid = threadIdx.x;
+  if (kc == 0 && nt == 0 && tid == 0) *offset_out = off;
+  __shared__ float s_am[2 * kNf4Tile];
+  __shared__ float s_red[8];
+  {
+    const int r = tid >> 1, kh = tid & 1;
+    const float a = absmax[static_cast<int64_t>(nt * kNf4Tile + r) * (K / kNf4Block) + kc * 2 + kh];
+    s_am[tid] = a;
+    const float d = __fsub_rn(a, off);
+    float m = fabsf(d);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if ((tid & 31) == 0) s_red[tid >> 5] = m;
+    __syncthreads();
+    float scale = s_red[0];
+#pragma unroll
+    for (int i = 1; i < 8; ++i) scale = fmaxf(scale, s_red[i]);
+    const float s127 = __fdiv_rn(scale, 127.f);
+    int q = 0;
+    if (s127 > 0.f) q = min(127, max(-127, __float2int_rn(__fdiv_rn(d, s127))));
+    chunk[kNf4ScaleOff + tid] = static_cast<uint8_t>(static_cast<int8_t>(q));
+    if (tid < 4) reinterpret_cast<float*>(chunk + kNf4S127Off)[tid] = tid == 0 ? s127 : 0.f;
+  }
+  __syncthreads();
+  const uint16_t* wt = w + static_cast<int64_t>(nt) * kNf4Tile * ldw + kc * kNf4Tile;
+  for (int q = tid; q < kNf4CodeBytes; q += 256) {
+    int row, col;
+    nf4_byte_pos(q, row, col);
+    const float am = s_am[row * 2 + (col >> 6)];
+    const uint32_t pair = *reinterpret_cast<const uint32_t*>(wt + static_cast<int64_t>(row) * ldw + col);
+    const int hi = nf4_index(h2f(pair & 0xffffu), am), lo = nf4_index(h2f(pair >> 16), am);
+    chunk[q] = static_cast<uint8_t>((hi << 4) | lo);
+  }
+}
+
+// ---------------------------------------------------------- dequantiser ----
+// One CTA of 256 threads per tile: fp16(fp32(NF4) * absmax_q) into W.
+__global__ void __launch_bounds__(256) nf4_dequant_kernel(const uint8_t* __restrict__ packed,
+                                                          const float* __restrict__ offset, int N, int K,
+                                                          uint16_t* __restrict__ w, int64_t ldw) {
+  const int kc = blockIdx.x, nt = blockIdx.y, kt = K / kNf4Tile;
+  const uint8_t* chunk = packed + (static_cast<int64_t>(nt) * kt + kc) * kNf4ChunkBytes;
+  constexpr int kPitch = kNf4Tile + 8;  // halves; rows stay 16-byte aligned
+  __shared__ __align__(16) uint16_t tile[kNf4Tile * kPitch];
+  __shared__ float s_am[2 * kNf4Tile];
+  __shared__ float s_val[16];
+  const int tid = threadIdx.x;
+  if (tid < 16) s_val[tid] = h2f(nf4_half_bits(tid));
+  {
+    const float s127 = *reinterpret_cast<const float*>(chunk + kNf4S127Off);
+    const float code = static_cast<float>(static_cast<int8_t>(chunk[kNf4ScaleOff + tid]));
+    s_am[tid] = __fadd_rn(__fmul_rn(code, s127), *offset);
+  }
+  __syncthreads();
+  for (int q = tid; q < kNf4CodeBytes; q += 256) {
+    int row, col;
+    nf4_byte_pos(q, row, col);
+    const uint32_t b = chunk[q];
+    const float am = s_am[row * 2 + (col >> 6)];
+    const __half h0 = __float2half_rn(__fmul_rn(s_val[b >> 4], am));
+    const __half h1 = __float2half_rn(__fmul_rn(s_val[b & 15], am));
+    tile[row * kPitch + col] = __half_as_ushort(h0);
+    tile[row * kPitch + col + 1] = __half_as_ushort(h1);
+  }
+  __syncthreads();
+  uint16_t* dst = w + static_cast<int64_t>(nt) * kNf4Tile * ldw + kc * kNf4Tile;
+  for (int c = tid; c < kNf4Tile * 16; c += 256) {
+    const int row = c >> 4, c8 = c & 15;
+    *reinterpret_cast<uint4*>(dst + static_cast<int64_t>(row) * ldw + c8 * 8) =
+        *reinterpret_cast<const uint4*>(tile + row * kPitch + c8 * 8);
+  }
+}
+
+// ------------------------------------------------------------------ GEMM ----
+struct UnitPos {
+  int p, tile, split, kc0, kc1;
+};
+
+__device__ __forceinline__ UnitPos unit_pos(const Nf4GemmArgs& a, int u) {
+  int p = 0;
+#pragma unroll
+  for (int i = 1; i < kNf4MaxProblems; ++i)
+    if (i < a.num_problems && u >= a.prob[i].unit_base) p = i;
+  const Nf4Problem& pr = a.prob[p];
+  const int lu = u - pr.unit_base;
+  UnitPos r;
+  r.p = p;
+  r.tile = lu / pr.splits;
+  r.split = lu - r.tile * pr.splits;
+  r.kc0 = r.split * pr.chunks_per_split;
+  r.kc1 = min(pr.K / kNf4Tile, r.kc0 + pr.chunks_per_split);
+  return r;
+}
+
+__device__ __forceinline__ void store_y(uint16_t* y, int64_t ldy, int M, int n0, int m0, float v0, float v1,
+                                        float v2, float v3) {
+  // v0 / v1: rows m0 / m0 + 1 of column n0; v2 / v3: the same of column n0 + 8
+  if (m0 < M) {
+    y[static_cast<int64_t>(m0) * ldy + n0] = __half_as_ushort(__float2half_rn(v0));
+    y[static_cast<int64_t>(m0) * ldy + n0 + 8] = __half_as_ushort(__float2half_rn(v2));
+  }
+  if (m0 + 1 < M) {
+    y[static_cast<int64_t>(m0 + 1) * ldy + n0] = __half_as_ushort(__float2half_rn(v1));
+    y[static_cast<int64_t>(m0 + 1) * ldy + n0 + 8] = __half_as_ushort(__float2half_rn(v3));
+  }
+}
+
+template <int MT>
+__global__ void __launch_bounds__(kNf4Threads, 1)
+    nf4_gemm_kernel(const __grid_constant__ Nf4Maps maps, const Nf4GemmArgs args) {
+  constexpr int MP = 8 * MT;  // rows of x per TMA box (zero past M)
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* ring = base;
+  uint32_t* lut = reinterpret_cast<uint32_t*>(base + kNf4Slots * kNf4SlotBytes);
+  __shared__ uint64_t full[kNf4Slots], empty[kNf4Slots];
+  __shared__ uint32_t lut1[256];
+  __shared__ int s_fin;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+  if (tid < 256) lut1[tid] = nf4_half_bits(tid >> 4) | (nf4_half_bits(tid & 15) << 16);
+  if (tid == 0) {
+    for (int s = 0; s < kNf4Slots; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kNf4Warps);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  // the compute warps spread the table to one copy per lane while the
+  // producer already streams the first chunks
+  if (warp < kNf4Warps) {
+    for (int i = tid; i < 256 * 32; i += kNf4Warps * 32) lut[i] = lut1[i >> 5];
+    named_sync(kNf4EpiBar, kNf4Warps * 32);
+  }
+
+  if (warp == kNf4Warps) {
+    // -------------------------------------------------------- producer ----
+    if (lane == 0) {
+      for (int p = 0; p < args.num_problems; ++p) tma_prefetch_desc(&maps.x[p]);
+      uint32_t g = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; ok && u < args.units; u += gridDim.x) {
+        const UnitPos up = unit_pos(args, u);
+        const Nf4Problem& pr = args.prob[up.p];
+        const int kt = pr.K / kNf4Tile;
+        for (int kc = up.kc0; kc < up.kc1; ++kc, ++g) {
+          const int s = static_cast<int>(g % kNf4Slots);
+          if (g >= static_cast<uint32_t>(kNf4Slots) &&
+              !mbar_wait(&empty[s], ((g / kNf4Slots) - 1) & 1, args.err)) {
+            ok = false;
+            break;
+          }
+          uint8_t* st = ring + s * kNf4SlotBytes;
+          mbar_arrive_expect_tx(&full[s], kNf4ChunkBytes + 2 * MP * 128);
+          bulk_load(st, pr.w + (static_cast<int64_t>(up.tile) * kt + kc) * kNf4ChunkBytes, kNf4ChunkBytes,
+                    &full[s]);
+          tc::tma_load_2d(st + kNf4RawPad, &maps.x[up.p], &full[s], kc * kNf4Tile, 0);
+          tc::tma_load_2d(st + kNf4RawPad + MP * 128, &maps.x[up.p], &full[s], kc * kNf4Tile + 64, 0);
+        }
+      }
+      // every copy this thread issued lands before the CTA exits
+      for (int s = 0; s < kNf4Slots; ++s)
+        if (g > static_cast<uint32_t>(s)) mbar_wait(&full[s], ((g - 1 - s) / kNf4Slots) & 1, args.err);
+    }
+    __syncwarp();
+  } else {
+    // ---------------------------------------------------------- compute ----
+    const int g8 = lane >> 2, t = lane & 3;
+    const uint32_t lut_lane = smem_u32(lut) + lane * 4;
+    uint32_t g = 0;
+    for (int u = blockIdx.x; u < args.units; u += gridDim.x) {
+      const UnitPos up = unit_pos(args, u);
+      const Nf4Problem& pr = args.prob[up.p];
+      const float off = *pr.offset;
+      float acc[MT][4];
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt) acc[mt][0] = acc[mt][1] = acc[mt][2] = acc[mt][3] = 0.f;
+      for (int kc = up.kc0; kc < up.kc1; ++kc, ++g) {
+        const int s = static_cast<int>(g % kNf4Slots);
+        mbar_wait(&full[s], (g / kNf4Slots) & 1, args.err);
+        const uint32_t st = smem_u32(ring + s * kNf4SlotBytes);
+        const uint4 c0 = lds128(st + ((warp * 2 + 0) * 32 + lane) * 16);
+        const uint4 c1 = lds128(st + ((warp * 2 + 1) * 32 + lane) * 16);
+        const float s127 = __uint_as_float(lds32(st + kNf4S127Off));
+        const int r0 = 16 * warp + g8;
+        // scale codes of rows r0 and r0 + 8: (kh 0, kh 1) in the low / high byte
+        const uint32_t s0 = lds16(st + kNf4ScaleOff + r0 * 2);
+        const uint32_t s1 = lds16(st + kNf4ScaleOff + (r0 + 8) * 2);
+        float am[2][2];
+#pragma unroll
+        for (int kh = 0; kh < 2; ++kh) {
+          am[kh][0] = __fadd_rn(__fmul_rn(static_cast<float>(static_cast<int8_t>((s0 >> (8 * kh)) & 0xffu)), s127), off);
+          am[kh][1] = __fadd_rn(__fmul_rn(static_cast<float>(static_cast<int8_t>((s1 >> (8 * kh)) & 0xffu)), s127), off);
+        }
+#pragma unroll
+        for (int kh = 0; kh < 2; ++kh) {
+          const uint4 cw = kh ? c1 : c0;
+          const uint32_t words[4] = {cw.x, cw.y, cw.z, cw.w};
+          const uint32_t xb = st + kNf4RawPad + kh * MP * 128;
+          float part[MT][4];
+#pragma unroll
+          for (int mt = 0; mt < MT; ++mt) part[mt][0] = part[mt][1] = part[mt][2] = part[mt][3] = 0.f;
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks) {
+            uint32_t a[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) a[j] = lds32(lut_lane + ((words[ks] >> (8 * j)) & 0xffu) * 128u);
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt) {
+              const int row = 8 * mt + g8;
+              const uint32_t rb = xb + row * 128 + t * 4;
+              uint32_t b[2];
+              b[0] = lds32(rb + (((2 * ks) ^ (row & 7)) << 4));
+              b[1] = lds32(rb + (((2 * ks + 1) ^ (row & 7)) << 4));
+              Mma<__half>::k16(part[mt], a, b);
+            }
+          }
+#pragma unroll
+          for (int mt = 0; mt < MT; ++mt) {
+            acc[mt][0] = fmaf(am[kh][0], part[mt][0], acc[mt][0]);
+            acc[mt][1] = fmaf(am[kh][0], part[mt][1], acc[mt][1]);
+            acc[mt][2] = fmaf(am[kh][1], part[mt][2], acc[mt][2]);
+            acc[mt][3] = fmaf(am[kh][1], part[mt][3], acc[mt][3]);
+          }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+      }
+      // D fragment: rows n0 = tile*128 + 16 warp + g8 (acc 0, 1) and n0 + 8
+      // (acc 2, 3); x rows 8 mt + 2t and + 1.
+      const int nl = 16 * warp + g8;
+      const int n0 = up.tile * kNf4Tile + nl;
+      if (pr.splits == 1) {
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt)
+          store_y(pr.y, pr.ldy, args.M, n0, 8 * mt + 2 * t, acc[mt][0], acc[mt][1], acc[mt][2], acc[mt][3]);
+      } else {
+        float* part = args.partials + static_cast<int64_t>(u) * kNf4Tile * MP;
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt) {
+          *reinterpret_cast<float2*>(part + nl * MP + 8 * mt + 2 * t) = make_float2(acc[mt][0], acc[mt][1]);
+          *reinterpret_cast<float2*>(part + (nl + 8) * MP + 8 * mt + 2 * t) = make_float2(acc[mt][2], acc[mt][3]);
+        }
+        __threadfence();
+        named_sync(kNf4EpiBar, kNf4Warps * 32);
+        int* cnt = args.counters + pr.counter_base + up.tile;
+        if (tid == 0) {
+          const int old = atomicAdd(cnt, 1);
+          s_fin = old == pr.splits - 1;
+          if (s_fin) __threadfence();
+        }
+        named_sync(kNf4EpiBar, kNf4Warps * 32);
+        if (s_fin) {
+          const float* p0 = args.partials + static_cast<int64_t>(pr.unit_base + up.tile * pr.splits) * kNf4Tile * MP;
+#pragma unroll
+          for (int mt = 0; mt < MT; ++mt) {
+            float v[4] = {0.f, 0.f, 0.f, 0.f};
+            for (int sp = 0; sp < pr.splits; ++sp) {
+              const float* q = p0 + static_cast<int64_t>(sp) * kNf4Tile * MP;
+              const float2 a = __ldcg(reinterpret_cast<const float2*>(q + nl * MP + 8 * mt + 2 * t));
+              const float2 b = __ldcg(reinterpret_cast<const float2*>(q + (nl + 8) * MP + 8 * mt + 2 * t));
+              v[0] += a.x;
+              v[1] += a.y;
+              v[2] += b.x;
+              v[3] += b.y;
+            }
+            store_y(pr.y, pr.ldy, args.M, n0, 8 * mt + 2 * t, v[0], v[1], v[2], v[3]);
+          }
+          named_sync(kNf4EpiBar, kNf4Warps * 32);
+          if (tid == 0) *cnt = 0;  // every split has counted: ready for the next launch
+        }
+      }
+    }
+  }
+  __syncthreads();
+}
+
+}  // namespace
+
+int nf4_sm_count() {
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
+  return sms;
+}
+
+cudaError_t launch_nf4_absmax(const uint16_t* w, int64_t ldw, int N, int K, float* absmax, uint32_t* minmax,
+                              cudaStream_t st) {
+  nf4_minmax_init_kernel<<<1, 32, 0, st>>>(minmax);
+  const int64_t blocks = static_cast<int64_t>(N) * (K / kNf4Block);
+  int grid = static_cast<int>((blocks + 255) / 256);
+  const int cap = 8 * (nf4_sm_count() > 0 ? nf4_sm_count() : 148);
+  if (grid > cap) grid = cap;
+  if (grid < 1) grid = 1;
+  nf4_absmax_kernel<<<grid, 256, 0, st>>>(w, ldw, N, K, absmax, minmax);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_nf4_pack(const uint16_t* w, int64_t ldw, int N, int K, const float* absmax,
+                            const uint32_t* minmax, uint8_t* packed, float* offset, cudaStream_t st) {
+  nf4_pack_kernel<<<dim3(K / kNf4Tile, N / kNf4Tile), 256, 0, st>>>(w, ldw, N, K, absmax, minmax, packed, offset);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_nf4_dequant(const uint8_t* packed, const float* offset, int N, int K, uint16_t* w, int64_t ldw,
+                               cudaStream_t st) {
+  nf4_dequant_kernel<<<dim3(K / kNf4Tile, N / kNf4Tile), 256, 0, st>>>(packed, offset, N, K, w, ldw);
+  return cudaGetLastError();
+}
+
+template <int MT>
+static cudaError_t gemm_launch(const Nf4Maps& maps, const Nf4GemmArgs& args, cudaStream_t st) {
+  auto kern = nf4_gemm_kernel<MT>;
+  constexpr int kMaxDev = 64;
+  static bool configured[kMaxDev] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kMaxDev) return cudaErrorInvalidDevice;
+  if (!configured[dev]) {
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kNf4Smem);
+    if (e != cudaSuccess) return e;
+    configured[dev] = true;
+  }
+  const int sms = nf4_sm_count();
+  int grid = sms < args.units ? sms : args.units;
+  if (grid < 1) grid = 1;
+  kern<<<grid, kNf4Threads, kNf4Smem, st>>>(maps, args);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_nf4_gemm(const Nf4Maps& maps, const Nf4GemmArgs& args, int m_pad, cudaStream_t st) {
+  switch (m_pad) {
+    case 8: return gemm_launch<1>(maps, args, st);
+    case 16: return gemm_launch<2>(maps, args, st);
+    case 32: return gemm_launch<4>(maps, args, st);
+    case 64: return gemm_launch<8>(maps, args, st);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace persona

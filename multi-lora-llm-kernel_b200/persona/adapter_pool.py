@@ -156,12 +156,16 @@ class LayerPools:
     B_down: torch.Tensor
 
 
-def pool_shapes(slots: int, r: int) -> Dict[str, Tuple[int, int, int]]:
+def pool_shapes(slots: int, r: int, geometry: Tuple[int, int, int] = (HIDDEN, KV_OUT, MLP_INTER)
+                ) -> Dict[str, Tuple[int, int, int]]:
+    """Pool shapes for ``geometry`` = (hidden, k/v output, MLP intermediate);
+    Mistral-7B by default.  q and o keep the hidden width."""
+    h, kv, inter = geometry
     return {
-        "A_qkv": (slots, 3 * r, HIDDEN), "B_q": (slots, HIDDEN, r), "B_k": (slots, KV_OUT, r),
-        "B_v": (slots, KV_OUT, r), "A_o": (slots, r, HIDDEN), "B_o": (slots, HIDDEN, r),
-        "A_gu": (slots, 2 * r, HIDDEN), "B_gate": (slots, MLP_INTER, r), "B_up": (slots, MLP_INTER, r),
-        "A_down": (slots, r, MLP_INTER), "B_down": (slots, HIDDEN, r),
+        "A_qkv": (slots, 3 * r, h), "B_q": (slots, h, r), "B_k": (slots, kv, r),
+        "B_v": (slots, kv, r), "A_o": (slots, r, h), "B_o": (slots, h, r),
+        "A_gu": (slots, 2 * r, h), "B_gate": (slots, inter, r), "B_up": (slots, inter, r),
+        "A_down": (slots, r, inter), "B_down": (slots, h, r),
     }
 
 
@@ -169,10 +173,11 @@ def _align(n: int, a: int = 128) -> int:
     return (n + a - 1) // a * a
 
 
-def _empty_layer_pools(slots: int, r: int, device: torch.device, dtype: torch.dtype) -> LayerPools:
+def _empty_layer_pools(slots: int, r: int, device: torch.device, dtype: torch.dtype,
+                       geometry: Tuple[int, int, int] = (HIDDEN, KV_OUT, MLP_INTER)) -> LayerPools:
     """Zeroed pools of one layer, carved out of a single allocation; every
     pool starts on a 256-byte boundary (TMA wants 16)."""
-    shapes = pool_shapes(slots, r)
+    shapes = pool_shapes(slots, r, geometry)
     sizes = {k: s[0] * s[1] * s[2] for k, s in shapes.items()}
     total = sum(_align(n) for n in sizes.values())
     slab = torch.zeros(total, dtype=dtype, device=device)
@@ -187,16 +192,19 @@ def _empty_layer_pools(slots: int, r: int, device: torch.device, dtype: torch.dt
 class AdapterPool:
     """All adapters resident in HBM; a slot table without paging (reference
     ``persona/adapter_pool.py:150-282``).  ``num_layers`` defaults to the
-    Mistral-7B 32 and exists so small models and tests can use fewer."""
+    Mistral-7B 32 and exists so small models and tests can use fewer;
+    ``geometry`` (hidden, k/v output, MLP intermediate) likewise defaults to
+    Mistral-7B."""
 
     def __init__(self, max_slots: int, r: int, device: torch.device, dtype: torch.dtype = torch.float16,
-                 num_layers: int = NUM_LAYERS):
+                 num_layers: int = NUM_LAYERS, geometry: Tuple[int, int, int] = (HIDDEN, KV_OUT, MLP_INTER)):
         self.max_slots = max_slots
         self.r = r
         self.device = torch.device(device)
         self.dtype = dtype
         self.num_layers = num_layers
-        self.layers: List[LayerPools] = [_empty_layer_pools(max_slots, r, self.device, dtype)
+        self.geometry = tuple(geometry)
+        self.layers: List[LayerPools] = [_empty_layer_pools(max_slots, r, self.device, dtype, self.geometry)
                                          for _ in range(num_layers)]
         self.slot_to_name: Dict[int, str] = {}
         self.name_to_slot: Dict[str, int] = {}

@@ -38,7 +38,19 @@ SIGNATURES = {
                                    _p, _p]),
     "persona_sgmv_fused": (_i32, [_p, _i64, _p, _i64, _i64, _p, _i64, _p, _p, _i64, _p, _i64, _i64, _i64, _i64,
                                   _i64, _i64, _i32, _p, _sz, _p, _p]),
+    "persona_nf4_packed_bytes": (_sz, [_i64, _i64]),
+    "persona_nf4_quantize_workspace_size": (_sz, [_i64, _i64]),
+    "persona_nf4_quantize": (_i32, [_p, _i64, _i64, _i64, _p, _p, _p, _sz, _p]),
+    "persona_nf4_dequantize": (_i32, [_p, _p, _i64, _i64, _p, _i64, _p]),
+    "persona_nf4_linear_workspace_size": (_sz, [_p, _i32]),
+    "persona_nf4_linear": (_i32, [_p, _i32, _i64, _p, _sz, _p, _p]),
 }
+
+
+class Nf4Problem(ctypes.Structure):
+    """persona_nf4_problem (include/persona_bgmv.h)."""
+    _fields_ = [("packed", _p), ("offset", _p), ("x", _p), ("ldx", _i64), ("y", _p), ("ldy", _i64), ("N", _i64),
+                ("K", _i64)]
 
 
 class Problem(ctypes.Structure):
