@@ -56,6 +56,12 @@ extern "C" {
 
 /* Flags of the BGMV ops. */
 #define PERSONA_REUSE_PLAN 1 /* workspace already holds the plan of these slots */
+#define PERSONA_SPLIT_ONLY 2 /* fused ops: always the split kernels, also at decode sizes */
+/* Fused ops on at most PERSONA_SMALL_MAX_ROWS rows (K <= 32768) run a kernel
+ * without cross-CTA steps: each CTA recomputes its row's v and writes one
+ * column slice.  Larger batches, or PERSONA_SPLIT_ONLY, use the split
+ * kernels.  Both leave the plan in the workspace when REUSE_PLAN is unset.  */
+#define PERSONA_SMALL_MAX_ROWS 64
 
 const char* persona_status_string(int status);
 int persona_abi_version(void);

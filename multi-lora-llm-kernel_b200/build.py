@@ -34,7 +34,7 @@ NVCC = str(CUDA_HOME / "bin" / "nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 CU_SOURCES = ["capi.cu", "bgmv_plan.cu", "bgmv_split.cu", "sgmv_tcgen05.cu", "simple_kernels.cu",
-              "noalloc.cu", "nf4.cu", "decode_ops.cu"]
+              "noalloc.cu", "nf4.cu", "decode_ops.cu", "bgmv_small.cu"]
 LIB = OUT / "libpersona_bgmv.so"
 EXT = OUT / ("_C" + sysconfig.get_config_var("EXT_SUFFIX"))
 

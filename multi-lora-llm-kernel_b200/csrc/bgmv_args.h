@@ -53,6 +53,29 @@ cudaError_t launch_bgmv_split(int mode, int dtype, int R, const SplitMaps& maps,
                               cudaStream_t st);
 
 // Segmented tensor-core kernels (sgmv_tcgen05.cu).
+// One projection of a decode-sized fused launch (bgmv_small.cu).
+struct SmallProblem {
+  const void* x;
+  const void* a;
+  const void* b;
+  void* y;
+  int64_t ldx, a_slot_stride, a_row_stride, b_slot_stride, ldy;
+  int K, N;
+  int slices;   // column slices per row (set by the launcher)
+  int x_bytes;  // shared-memory bytes of one x row (set by the launcher)
+};
+
+struct SmallArgs {
+  SmallProblem prob[kMaxProblems];
+  int unit_base[kMaxProblems];  // first CTA of each problem (set by the launcher)
+  const int32_t* slots;
+  int32_t* err;
+  int num_problems;
+  int S;
+};
+
+cudaError_t launch_bgmv_small(int dtype, int R, SmallArgs& a, int T, cudaStream_t st);
+
 constexpr int kMaxTpPeers = 7;  // other ranks a tensor-parallel launch writes to
 // Width of one tensor-core SGMV fill: the shrink's K chunk and the expand's
 // output tile (MMA N); x, y and A move as 64-element boxes side by side.

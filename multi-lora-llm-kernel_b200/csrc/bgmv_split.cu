@@ -570,8 +570,17 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
           if (finisher) {
             const float* p0 = wv.parts + static_cast<int64_t>(gg.p_base + item * gg.nks) * kPartFloats;
             for (int e = tid; e < E; e += kConsumers) {
+              // eight slices' loads in flight at a time, summed in slice order
               float sum = 0.f;
-              for (int q = 0; q < gg.nks; ++q) sum += __ldcg(p0 + q * kPartFloats + e);
+              int q = 0;
+              for (; q + 8 <= gg.nks; q += 8) {
+                float pv8[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) pv8[i] = __ldcg(p0 + (q + i) * kPartFloats + e);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) sum += pv8[i];
+              }
+              for (; q < gg.nks; ++q) sum += __ldcg(p0 + q * kPartFloats + e);
               sm.pv[e] = sum;
             }
           }

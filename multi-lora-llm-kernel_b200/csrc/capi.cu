@@ -155,6 +155,41 @@ int run_split(int mode, int dtype, int64_t R, const SplitMaps& maps, SplitArgs& 
                                                                                              : PERSONA_ERR_CUDA;
 }
 
+// Decode-sized fused launches: the kernel without cross-CTA steps.
+bool small_path(int64_t T, int flags, const int64_t* Ks, int n) {
+  if (T > PERSONA_SMALL_MAX_ROWS || (flags & PERSONA_SPLIT_ONLY)) return false;
+  for (int i = 0; i < n; ++i)
+    if (Ks[i] > 32768) return false;
+  return true;
+}
+
+int run_small(const persona_bgmv_problem* probs, int n, const int32_t* slots, int64_t T, int64_t R, int64_t S,
+              int dtype, int32_t* dev_err, cudaStream_t stream) {
+  SmallArgs a = {};
+  for (int i = 0; i < n; ++i) {
+    const persona_bgmv_problem& q = probs[i];
+    SmallProblem& p = a.prob[i];
+    p.x = q.x;
+    p.a = q.a_pool;
+    p.b = q.b_pool;
+    p.y = q.y;
+    p.ldx = q.ldx;
+    p.a_slot_stride = q.a_slot_stride;
+    p.a_row_stride = q.a_row_stride;
+    p.b_slot_stride = q.b_slot_stride;
+    p.ldy = q.ldy;
+    p.K = static_cast<int>(q.K);
+    p.N = static_cast<int>(q.N);
+  }
+  a.slots = slots;
+  a.err = dev_err;
+  a.num_problems = n;
+  a.S = static_cast<int>(S);
+  return launch_bgmv_small(dtype, static_cast<int>(R), a, static_cast<int>(T), stream) == cudaSuccess
+             ? PERSONA_OK
+             : PERSONA_ERR_CUDA;
+}
+
 int plan_if_needed(const int32_t* slots, int64_t T, int64_t S, void* ws, int flags,
                    int32_t* dev_err, cudaStream_t st) {
   if (flags & PERSONA_REUSE_PLAN) return PERSONA_OK;
@@ -285,7 +320,7 @@ int persona_bgmv_fused(const void* x, int64_t ldx, const void* a_pool, int64_t a
                        int64_t N, int64_t R, int64_t S, int dtype, void* workspace,
                        size_t workspace_bytes, int flags, int32_t* dev_err,
                        cudaStream_t stream) {
-  if (flags & ~PERSONA_REUSE_PLAN) return PERSONA_ERR_INVALID_ARG;
+  if (flags & ~(PERSONA_REUSE_PLAN | PERSONA_SPLIT_ONLY)) return PERSONA_ERR_INVALID_ARG;
   int st = check_common(T, S, dtype, workspace, workspace_bytes, slots);
   if (st != PERSONA_OK) return st;
   if (!rank_supported(R)) return PERSONA_ERR_RANK;
@@ -293,6 +328,12 @@ int persona_bgmv_fused(const void* x, int64_t ldx, const void* a_pool, int64_t a
   if ((st = check_a(x, ldx, a_pool, a_slot_stride, a_row_stride, K, R, S)) != PERSONA_OK) return st;
   if ((st = check_b(b_pool, b_slot_stride, y, ldy, N, R)) != PERSONA_OK) return st;
   if (K < 64) return PERSONA_ERR_SHAPE;
+  if (small_path(T, flags, &K, 1)) {
+    if ((st = plan_if_needed(slots, T, S, workspace, flags, dev_err, stream)) != PERSONA_OK) return st;
+    const persona_bgmv_problem one = {x, ldx, a_pool, a_slot_stride, a_row_stride, b_pool, b_slot_stride,
+                                      y, ldy, K, N};
+    return run_small(&one, 1, slots, T, R, S, dtype, dev_err, stream);
+  }
   SplitArgs a = {};
   SplitMaps maps;
   std::memset(&maps, 0, sizeof(maps));
@@ -324,7 +365,7 @@ size_t persona_bgmv_multi_workspace_size(int64_t T, int num_problems) {
 int persona_bgmv_fused_multi(const persona_bgmv_problem* problems, int num_problems, const int32_t* slots,
                              int64_t T, int64_t R, int64_t S, int dtype, void* workspace, size_t workspace_bytes,
                              int flags, int32_t* dev_err, cudaStream_t stream) {
-  if (flags & ~PERSONA_REUSE_PLAN) return PERSONA_ERR_INVALID_ARG;
+  if (flags & ~(PERSONA_REUSE_PLAN | PERSONA_SPLIT_ONLY)) return PERSONA_ERR_INVALID_ARG;
   if (problems == nullptr || num_problems < 1 || num_problems > PERSONA_MAX_PROBLEMS) return PERSONA_ERR_INVALID_ARG;
   int st = check_common(T, S, dtype, workspace, workspace_bytes, slots);
   if (st != PERSONA_OK) return st;
@@ -347,6 +388,12 @@ int persona_bgmv_fused_multi(const persona_bgmv_problem* problems, int num_probl
     a.prob[p].n_box = b_box_rows(q.N, R);
   }
   if (T == 0) return PERSONA_OK;
+  int64_t Ks[PERSONA_MAX_PROBLEMS];
+  for (int p = 0; p < num_problems; ++p) Ks[p] = problems[p].K;
+  if (small_path(T, flags, Ks, num_problems)) {
+    if ((st = plan_if_needed(slots, T, S, workspace, flags, dev_err, stream)) != PERSONA_OK) return st;
+    return run_small(problems, num_problems, slots, T, R, S, dtype, dev_err, stream);
+  }
   for (int p = 0; p < num_problems; ++p) {
     const persona_bgmv_problem& q = problems[p];
     if ((st = encode_a_map(&maps.a[p], q.a_pool, dtype, q.K, R, S, q.a_row_stride, q.a_slot_stride)) != PERSONA_OK)
@@ -801,8 +848,8 @@ int persona_decode_attention(const void* q, const void* k_cache, const void* v_c
   if (B < 0 || B > 65535 || Hkv <= 0 || Hq <= 0 || Hq % Hkv || Hq / Hkv > 8 || Hkv > 65535 || L <= 0 ||
       L > kI32Max)
     return PERSONA_ERR_SHAPE;
-  if ((reinterpret_cast<uintptr_t>(k_cache) & 3) || (reinterpret_cast<uintptr_t>(v_cache) & 3) ||
-      (reinterpret_cast<uintptr_t>(q) & 1) || (reinterpret_cast<uintptr_t>(out) & 1))
+  if (!aligned16(k_cache) || !aligned16(v_cache) || (reinterpret_cast<uintptr_t>(q) & 1) ||
+      (reinterpret_cast<uintptr_t>(out) & 1))
     return PERSONA_ERR_ALIGNMENT;
   if (B == 0) return PERSONA_OK;
   return persona::launch_decode_attention(q, k_cache, v_cache, len, out, static_cast<int>(B), static_cast<int>(Hq),

@@ -22,6 +22,7 @@ __device__ __forceinline__ float h2f(__half h) { return __half2float(h); }
 __global__ void __launch_bounds__(256) add_rmsnorm_kernel(__half* __restrict__ h, const __half* __restrict__ delta,
                                                           const __half* __restrict__ w, __half* __restrict__ out,
                                                           int D, float eps) {
+  asm volatile("griddepcontrol.launch_dependents;");  // a dependent NF4 GEMM may start streaming weights
   const int r = blockIdx.x;
   __half* hr = h + static_cast<int64_t>(r) * D;
   const __half* dr = delta ? delta + static_cast<int64_t>(r) * D : nullptr;
@@ -102,6 +103,7 @@ __global__ void rope_cache_kernel(__half* __restrict__ q, __half* __restrict__ k
 // out = fp16(fp16(silu(g)) * u), n a multiple of 8.
 __global__ void silu_mul_kernel(const __half* __restrict__ g, const __half* __restrict__ u, __half* __restrict__ out,
                                 int64_t n) {
+  asm volatile("griddepcontrol.launch_dependents;");
   for (int64_t i = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) * 8; i < n;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x * 8) {
     const uint4 gv = *reinterpret_cast<const uint4*>(g + i);
@@ -121,88 +123,121 @@ __global__ void silu_mul_kernel(const __half* __restrict__ g, const __half* __re
 }
 
 // One new token per sequence: out[b, h] = softmax(q[b, h] K[b, h / G]^T *
-// scale) V[b, h / G] over positions [0, *len).  One CTA per (sequence, kv
-// head), one warp per query head of the group (G = Hq / Hkv <= 8); the
-// cache is staged 32 positions at a time, rows padded to 65 words so that a
-// lane per position reads without bank conflicts.
-constexpr int kAttnChunk = 32;
-constexpr int kAttnPitch = 130;  // halves per staged row (65 words)
+// scale) V[b, h / G] over positions [0, *len).  One CTA of 128 threads per
+// (sequence, kv head) computes the G = Hq / Hkv <= 8 query heads that share
+// the cache rows, so K and V are read once.  Scores: a thread per position,
+// 16-byte loads of its K row, G dot products (q in shared memory).  P V:
+// threads as 8 position groups x 16 column chunks of 8 dims, 16-byte V
+// loads eight positions at a time, then a sum over the groups in shared
+// memory.  Dynamic shared memory: G * L scores + 8 * G * 128 partial sums +
+// G * 128 query values, all fp32.
+constexpr int kAttnThreads = 128;
 
-__global__ void decode_attention_kernel(const __half* __restrict__ q, const __half* __restrict__ kc,
-                                        const __half* __restrict__ vc, const int* __restrict__ len_ptr,
-                                        __half* __restrict__ out, int Hq, int Hkv, int L, float scale) {
+__global__ void __launch_bounds__(kAttnThreads) decode_attention_kernel(
+    const __half* __restrict__ q, const __half* __restrict__ kc, const __half* __restrict__ vc,
+    const int* __restrict__ len_ptr, __half* __restrict__ out, int Hq, int Hkv, int L, float scale) {
   constexpr int D = 128;
-  const int b = blockIdx.x, kh = blockIdx.y;
+  asm volatile("griddepcontrol.launch_dependents;");
+  const int b = blockIdx.x, kh = blockIdx.y, tid = threadIdx.x;
   const int G = Hq / Hkv;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int h = kh * G + warp;
   const int len = min(*len_ptr, L);
-  __shared__ __half ks[kAttnChunk * kAttnPitch];
-  __shared__ __half vs[kAttnChunk * kAttnPitch];
-  __shared__ float qs[8][D];
-  if (warp < G)
-    for (int d = lane; d < D; d += 32) qs[warp][d] = h2f(q[(static_cast<int64_t>(b) * Hq + h) * D + d]);
+  extern __shared__ float attn_smem[];
+  float* sc = attn_smem;                 // [G][L]
+  float* part = sc + G * L;              // [8][G][D]
+  float* qs = part + 8 * G * D;          // [G][D]
+  __shared__ float s_inv[8];
+  for (int i = tid; i < G * D; i += kAttnThreads)
+    qs[i] = __half2float(q[(static_cast<int64_t>(b) * Hq + kh * G) * D + i]);
+  __syncthreads();
   const __half* kb = kc + (static_cast<int64_t>(b) * Hkv + kh) * L * D;
   const __half* vb = vc + (static_cast<int64_t>(b) * Hkv + kh) * L * D;
-  float m = -INFINITY, l = 0.f;
-  float acc[4] = {0.f, 0.f, 0.f, 0.f};  // dims 4 lane .. 4 lane + 3
-  for (int p0 = 0; p0 < len; p0 += kAttnChunk) {
-    const int n = min(kAttnChunk, len - p0);
-    __syncthreads();
-    for (int e = threadIdx.x; e < kAttnChunk * (D / 2); e += blockDim.x) {
-      const int pr = e / (D / 2), c2 = e - pr * (D / 2);
-      uint32_t kv = 0, vv = 0;
-      if (pr < n) {
-        kv = reinterpret_cast<const uint32_t*>(kb + static_cast<int64_t>(p0 + pr) * D)[c2];
-        vv = reinterpret_cast<const uint32_t*>(vb + static_cast<int64_t>(p0 + pr) * D)[c2];
-      }
-      reinterpret_cast<uint32_t*>(ks + pr * kAttnPitch)[c2] = kv;
-      reinterpret_cast<uint32_t*>(vs + pr * kAttnPitch)[c2] = vv;
-    }
-    __syncthreads();
-    if (warp < G) {
-      float sc = -INFINITY;
-      if (lane < n) {
-        const __half* kr = ks + lane * kAttnPitch;
-        float dot = 0.f;
-#pragma unroll 8
-        for (int d = 0; d < D; d += 2) {
-          const float2 kf = __half22float2(*reinterpret_cast<const __half2*>(kr + d));
-          dot = fmaf(qs[warp][d], kf.x, dot);
-          dot = fmaf(qs[warp][d + 1], kf.y, dot);
+  // scores
+  for (int p = tid; p < len; p += kAttnThreads) {
+    const uint4* kr = reinterpret_cast<const uint4*>(kb + static_cast<int64_t>(p) * D);
+    uint4 kv[D / 8];
+#pragma unroll
+    for (int i = 0; i < D / 8; ++i) kv[i] = kr[i];
+    for (int h = 0; h < G; ++h) {
+      const float* qh = qs + h * D;
+      float dot = 0.f;
+#pragma unroll
+      for (int i = 0; i < D / 8; ++i) {
+        const __half2* k2 = reinterpret_cast<const __half2*>(&kv[i]);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 kf = __half22float2(k2[j]);
+          dot = fmaf(qh[8 * i + 2 * j], kf.x, dot);
+          dot = fmaf(qh[8 * i + 2 * j + 1], kf.y, dot);
         }
-        sc = dot * scale;
       }
-      float mx = sc;
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-      const float m_new = fmaxf(m, mx);
-      const float corr = __expf(m - m_new);
-      const float pw = lane < n ? __expf(sc - m_new) : 0.f;
-      float ps = pw;
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
-      l = l * corr + ps;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) acc[i] *= corr;
-      for (int pr = 0; pr < n; ++pr) {
-        const float wgt = __shfl_sync(0xffffffffu, pw, pr);
-        const __half* vr = vs + pr * kAttnPitch + 4 * lane;
-        const float2 v0 = __half22float2(*reinterpret_cast<const __half2*>(vr));
-        const float2 v1 = __half22float2(*reinterpret_cast<const __half2*>(vr + 2));
-        acc[0] = fmaf(wgt, v0.x, acc[0]);
-        acc[1] = fmaf(wgt, v0.y, acc[1]);
-        acc[2] = fmaf(wgt, v1.x, acc[2]);
-        acc[3] = fmaf(wgt, v1.y, acc[3]);
-      }
-      m = m_new;
+      sc[h * L + p] = dot * scale;
     }
   }
-  if (warp < G) {
-    const float inv = l > 0.f ? 1.f / l : 0.f;
-    __half* o = out + (static_cast<int64_t>(b) * Hq + h) * D + 4 * lane;
+  __syncthreads();
+  // softmax statistics per head: warp w reduces heads w, w + 4
+  const int warp = tid >> 5, lane = tid & 31;
+  for (int h = warp; h < G; h += kAttnThreads / 32) {
+    float m = -INFINITY;
+    for (int p = lane; p < len; p += 32) m = fmaxf(m, sc[h * L + p]);
 #pragma unroll
-    for (int i = 0; i < 4; ++i) o[i] = __float2half_rn(acc[i] * inv);
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float l = 0.f;
+    for (int p = lane; p < len; p += 32) {
+      const float e = __expf(sc[h * L + p] - m);
+      sc[h * L + p] = e;
+      l += e;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+    if (lane == 0) s_inv[h] = l > 0.f ? 1.f / l : 0.f;
+  }
+  __syncthreads();
+  // P V: position group pg, 8-dim column chunk dc
+  const int pg = tid >> 4, dc = tid & 15;
+  float acc[8][8];
+#pragma unroll
+  for (int h = 0; h < 8; ++h)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[h][j] = 0.f;
+  for (int p0 = pg; p0 < len; p0 += 8 * 8) {
+    uint4 vv[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int p = p0 + 8 * i;
+      vv[i] = p < len ? reinterpret_cast<const uint4*>(vb + static_cast<int64_t>(p) * D)[dc] : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int p = p0 + 8 * i;
+      if (p < len) {
+        const __half2* v2 = reinterpret_cast<const __half2*>(&vv[i]);
+#pragma unroll
+        for (int h = 0; h < 8; ++h) {
+          if (h < G) {
+            const float w = sc[h * L + p];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const float2 vf = __half22float2(v2[j]);
+              acc[h][2 * j] = fmaf(w, vf.x, acc[h][2 * j]);
+              acc[h][2 * j + 1] = fmaf(w, vf.y, acc[h][2 * j + 1]);
+            }
+          }
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int h = 0; h < 8; ++h)
+    if (h < G)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) part[(pg * G + h) * D + 8 * dc + j] = acc[h][j];
+  __syncthreads();
+  for (int i = tid; i < G * D; i += kAttnThreads) {
+    const int h = i / D;
+    float sum = 0.f;
+#pragma unroll
+    for (int g = 0; g < 8; ++g) sum += part[g * G * D + i];
+    out[(static_cast<int64_t>(b) * Hq + kh * G) * D + i] = __float2half_rn(sum * s_inv[h]);
   }
 }
 
@@ -234,7 +269,15 @@ cudaError_t launch_silu_mul(const void* g, const void* u, void* out, int64_t n, 
 
 cudaError_t launch_decode_attention(const void* q, const void* kc, const void* vc, const int* len, void* out, int B,
                                     int Hq, int Hkv, int L, float scale, cudaStream_t st) {
-  decode_attention_kernel<<<dim3(B, Hkv), 32 * (Hq / Hkv), 0, st>>>(
+  const int G = Hq / Hkv;
+  const size_t smem = (static_cast<size_t>(G) * L + 8 * G * 128 + G * 128) * sizeof(float);
+  if (smem > 227 * 1024) return cudaErrorInvalidValue;
+  if (smem > 48 * 1024) {
+    const cudaError_t e =
+        cudaFuncSetAttribute(decode_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+  }
+  decode_attention_kernel<<<dim3(B, Hkv), kAttnThreads, smem, st>>>(
       static_cast<const __half*>(q), static_cast<const __half*>(kc), static_cast<const __half*>(vc), len,
       static_cast<__half*>(out), Hq, Hkv, L, scale);
   return cudaGetLastError();

@@ -42,10 +42,17 @@ constexpr int kNf4Warps = 8;
 constexpr int kNf4Threads = (kNf4Warps + 1) * 32;
 constexpr int kNf4Slots = 6;
 constexpr int kNf4RawPad = 9216;  // chunk area of a slot, padded to 1 KB
-constexpr int kNf4XBox = kNf4MaxRows * 128;
-constexpr int kNf4SlotBytes = kNf4RawPad + 2 * kNf4XBox;
 constexpr int kNf4LutBytes = 256 * 32 * 4;
-constexpr int kNf4Smem = kNf4Slots * kNf4SlotBytes + kNf4LutBytes + 1024;
+
+// A slot holds one chunk and the two x boxes (8 MT rows each); at MT = 1 two
+// CTAs fit on an SM, which doubles the warps that hide the load and MMA
+// latencies.
+template <int MT>
+struct Nf4Cfg {
+  static constexpr int kSlotBytes = kNf4RawPad + 2 * 8 * MT * 128;
+  static constexpr int kSmem = kNf4Slots * kSlotBytes + kNf4LutBytes + 1024;
+  static_assert(kSlotBytes % 1024 == 0, "slot alignment");
+};
 constexpr int kNf4EpiBar = 1;
 static_assert(kNf4ChunkBytes % 16 == 0 && kNf4RawPad >= kNf4ChunkBytes, "chunk layout");
 
@@ -234,10 +241,11 @@ template <int MT>
 __global__ void __launch_bounds__(kNf4Threads, 1)
     nf4_gemm_kernel(const __grid_constant__ Nf4Maps maps, const Nf4GemmArgs args) {
   constexpr int MP = 8 * MT;  // rows of x per TMA box (zero past M)
+  constexpr int kSlotBytes = Nf4Cfg<MT>::kSlotBytes;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* ring = base;
-  uint32_t* lut = reinterpret_cast<uint32_t*>(base + kNf4Slots * kNf4SlotBytes);
+  uint32_t* lut = reinterpret_cast<uint32_t*>(base + kNf4Slots * kSlotBytes);
   __shared__ uint64_t full[kNf4Slots], empty[kNf4Slots];
   __shared__ uint32_t lut1[256];
   __shared__ int s_fin;
@@ -263,6 +271,20 @@ __global__ void __launch_bounds__(kNf4Threads, 1)
     // -------------------------------------------------------- producer ----
     if (lane == 0) {
       for (int p = 0; p < args.num_problems; ++p) tma_prefetch_desc(&maps.x[p]);
+      // Launched as a programmatic dependent of the kernel that writes x:
+      // the weight chunks of the first kNf4Slots fills do not depend on it
+      // and are requested at once; their x boxes wait for that kernel.
+      int pend_kc[kNf4Slots], pend_p[kNf4Slots], n_pend = 0;
+      bool waited = false;
+      auto flush = [&]() {
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+        for (int i = 0; i < n_pend; ++i) {
+          uint8_t* st = ring + i * kSlotBytes;
+          tc::tma_load_2d(st + kNf4RawPad, &maps.x[pend_p[i]], &full[i], pend_kc[i] * kNf4Tile, 0);
+          tc::tma_load_2d(st + kNf4RawPad + MP * 128, &maps.x[pend_p[i]], &full[i], pend_kc[i] * kNf4Tile + 64, 0);
+        }
+        waited = true;
+      };
       uint32_t g = 0;
       bool ok = true;
       for (int u = blockIdx.x; ok && u < args.units; u += gridDim.x) {
@@ -271,19 +293,28 @@ __global__ void __launch_bounds__(kNf4Threads, 1)
         const int kt = pr.K / kNf4Tile;
         for (int kc = up.kc0; kc < up.kc1; ++kc, ++g) {
           const int s = static_cast<int>(g % kNf4Slots);
-          if (g >= static_cast<uint32_t>(kNf4Slots) &&
-              !mbar_wait(&empty[s], ((g / kNf4Slots) - 1) & 1, args.err)) {
-            ok = false;
-            break;
+          if (g >= static_cast<uint32_t>(kNf4Slots)) {
+            if (!waited) flush();
+            if (!mbar_wait(&empty[s], ((g / kNf4Slots) - 1) & 1, args.err)) {
+              ok = false;
+              break;
+            }
           }
-          uint8_t* st = ring + s * kNf4SlotBytes;
+          uint8_t* st = ring + s * kSlotBytes;
           mbar_arrive_expect_tx(&full[s], kNf4ChunkBytes + 2 * MP * 128);
           bulk_load(st, pr.w + (static_cast<int64_t>(up.tile) * kt + kc) * kNf4ChunkBytes, kNf4ChunkBytes,
                     &full[s]);
-          tc::tma_load_2d(st + kNf4RawPad, &maps.x[up.p], &full[s], kc * kNf4Tile, 0);
-          tc::tma_load_2d(st + kNf4RawPad + MP * 128, &maps.x[up.p], &full[s], kc * kNf4Tile + 64, 0);
+          if (waited) {
+            tc::tma_load_2d(st + kNf4RawPad, &maps.x[up.p], &full[s], kc * kNf4Tile, 0);
+            tc::tma_load_2d(st + kNf4RawPad + MP * 128, &maps.x[up.p], &full[s], kc * kNf4Tile + 64, 0);
+          } else {
+            pend_kc[n_pend] = kc;
+            pend_p[n_pend] = up.p;
+            ++n_pend;
+          }
         }
       }
+      if (!waited) flush();
       // every copy this thread issued lands before the CTA exits
       for (int s = 0; s < kNf4Slots; ++s)
         if (g > static_cast<uint32_t>(s)) mbar_wait(&full[s], ((g - 1 - s) / kNf4Slots) & 1, args.err);
@@ -304,7 +335,7 @@ __global__ void __launch_bounds__(kNf4Threads, 1)
       for (int kc = up.kc0; kc < up.kc1; ++kc, ++g) {
         const int s = static_cast<int>(g % kNf4Slots);
         mbar_wait(&full[s], (g / kNf4Slots) & 1, args.err);
-        const uint32_t st = smem_u32(ring + s * kNf4SlotBytes);
+        const uint32_t st = smem_u32(ring + s * kSlotBytes);
         const uint4 c0 = lds128(st + ((warp * 2 + 0) * 32 + lane) * 16);
         const uint4 c1 = lds128(st + ((warp * 2 + 1) * 32 + lane) * 16);
         const float s127 = __uint_as_float(lds32(st + kNf4S127Off));
@@ -326,6 +357,16 @@ __global__ void __launch_bounds__(kNf4Threads, 1)
           float part[MT][4];
 #pragma unroll
           for (int mt = 0; mt < MT; ++mt) part[mt][0] = part[mt][1] = part[mt][2] = part[mt][3] = 0.f;
+          // B fragments of the four k-steps: ldmatrix.x4 gives two k-steps
+          // (four 8 x 8 tiles: 16-byte chunks 4h .. 4h + 3 of rows 8 mt ..)
+          uint32_t bf[MT][2][4];
+#pragma unroll
+          for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const int row = 8 * mt + (lane & 7), c = 4 * h + (lane >> 3);
+              ldsm_x4(xb + row * 128 + ((c ^ (row & 7)) << 4), bf[mt][h]);
+            }
 #pragma unroll
           for (int ks = 0; ks < 4; ++ks) {
             uint32_t a[4];
@@ -333,11 +374,7 @@ __global__ void __launch_bounds__(kNf4Threads, 1)
             for (int j = 0; j < 4; ++j) a[j] = lds32(lut_lane + ((words[ks] >> (8 * j)) & 0xffu) * 128u);
 #pragma unroll
             for (int mt = 0; mt < MT; ++mt) {
-              const int row = 8 * mt + g8;
-              const uint32_t rb = xb + row * 128 + t * 4;
-              uint32_t b[2];
-              b[0] = lds32(rb + (((2 * ks) ^ (row & 7)) << 4));
-              b[1] = lds32(rb + (((2 * ks + 1) ^ (row & 7)) << 4));
+              const uint32_t b[2] = {bf[mt][ks >> 1][(ks & 1) * 2], bf[mt][ks >> 1][(ks & 1) * 2 + 1]};
               Mma<__half>::k16(part[mt], a, b);
             }
           }
@@ -367,10 +404,12 @@ __global__ void __launch_bounds__(kNf4Threads, 1)
           *reinterpret_cast<float2*>(part + nl * MP + 8 * mt + 2 * t) = make_float2(acc[mt][0], acc[mt][1]);
           *reinterpret_cast<float2*>(part + (nl + 8) * MP + 8 * mt + 2 * t) = make_float2(acc[mt][2], acc[mt][3]);
         }
-        __threadfence();
+        // one cumulative fence after the barrier orders every warp's
+        // partial stores before the count
         named_sync(kNf4EpiBar, kNf4Warps * 32);
         int* cnt = args.counters + pr.counter_base + up.tile;
         if (tid == 0) {
+          __threadfence();
           const int old = atomicAdd(cnt, 1);
           s_fin = old == pr.splits - 1;
           if (s_fin) __threadfence();
@@ -381,14 +420,26 @@ __global__ void __launch_bounds__(kNf4Threads, 1)
 #pragma unroll
           for (int mt = 0; mt < MT; ++mt) {
             float v[4] = {0.f, 0.f, 0.f, 0.f};
-            for (int sp = 0; sp < pr.splits; ++sp) {
-              const float* q = p0 + static_cast<int64_t>(sp) * kNf4Tile * MP;
-              const float2 a = __ldcg(reinterpret_cast<const float2*>(q + nl * MP + 8 * mt + 2 * t));
-              const float2 b = __ldcg(reinterpret_cast<const float2*>(q + (nl + 8) * MP + 8 * mt + 2 * t));
-              v[0] += a.x;
-              v[1] += a.y;
-              v[2] += b.x;
-              v[3] += b.y;
+            // four splits' loads in flight at a time, summed in split order
+            for (int sp0 = 0; sp0 < pr.splits; sp0 += 4) {
+              float2 a[4], b[4];
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                if (sp0 + q < pr.splits) {
+                  const float* src = p0 + static_cast<int64_t>(sp0 + q) * kNf4Tile * MP;
+                  a[q] = __ldcg(reinterpret_cast<const float2*>(src + nl * MP + 8 * mt + 2 * t));
+                  b[q] = __ldcg(reinterpret_cast<const float2*>(src + (nl + 8) * MP + 8 * mt + 2 * t));
+                }
+              }
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                if (sp0 + q < pr.splits) {
+                  v[0] += a[q].x;
+                  v[1] += a[q].y;
+                  v[2] += b[q].x;
+                  v[3] += b[q].y;
+                }
+              }
             }
             store_y(pr.y, pr.ldy, args.M, n0, 8 * mt + 2 * t, v[0], v[1], v[2], v[3]);
           }
@@ -437,21 +488,38 @@ cudaError_t launch_nf4_dequant(const uint8_t* packed, const float* offset, int N
 template <int MT>
 static cudaError_t gemm_launch(const Nf4Maps& maps, const Nf4GemmArgs& args, cudaStream_t st) {
   auto kern = nf4_gemm_kernel<MT>;
+  constexpr int smem = Nf4Cfg<MT>::kSmem;
   constexpr int kMaxDev = 64;
-  static bool configured[kMaxDev] = {};
+  static int per_sm[kMaxDev] = {};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= kMaxDev) return cudaErrorInvalidDevice;
-  if (!configured[dev]) {
-    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kNf4Smem);
+  if (per_sm[dev] == 0) {
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
-    configured[dev] = true;
+    int occ = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kNf4Threads, smem);
+    if (e != cudaSuccess) return e;
+    per_sm[dev] = occ > 0 ? occ : 1;
   }
-  const int sms = nf4_sm_count();
-  int grid = sms < args.units ? sms : args.units;
+  const int ctas = per_sm[dev] * nf4_sm_count();
+  int grid = ctas < args.units ? ctas : args.units;
   if (grid < 1) grid = 1;
-  kern<<<grid, kNf4Threads, kNf4Smem, st>>>(maps, args);
+  // programmatic dependent launch: the weight streaming of this kernel may
+  // start while the kernel before it on the stream finishes
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kNf4Threads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, kern, maps, args);
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 

@@ -15,7 +15,7 @@ package's kernels:
   up, one each for o and down);
 * LoRA: ``ops.bgmv_fused_multi`` / ``ops.bgmv_fused`` on a plan computed once
   per batch at decode, ``ops.sgmv_fused`` per request segment at prefill;
-* the rest: ``torch.ops.persona.add_rmsnorm`` (residual add fused into the
+* the rest: ``ops.add_rmsnorm`` (residual add fused into the
   next norm), ``rope_cache`` (rotary embedding + KV-cache write),
   ``decode_attention``, ``silu_mul``; the LM head and the prefill attention
   are library calls (cuBLAS, scaled_dot_product_attention).
@@ -170,12 +170,12 @@ class MistralLoRAModel:
         delta = None
         for li, lw in enumerate(self.layers):
             lora = self._lora[li]
-            torch.ops.persona.add_rmsnorm(h, delta, lw.in_norm, xn, cfg.rms_eps)
+            ops.add_rmsnorm(h, delta, lw.in_norm, xn, cfg.rms_eps)
             q, k, v = nf4.linear(xn, [lw.q, lw.k, lw.v])
             for name, y in (("q_proj", q), ("k_proj", k), ("v_proj", v)):
                 ops.sgmv_fused(xn, *lora[name], indptr, st.slots, y)
             q3, k3, v3 = (t.view(R, -1, 128) for t in (q, k, v))
-            torch.ops.persona.rope_cache(q3, k3, v3, st.k_cache[li], st.v_cache[li], start, T, cfg.rope_theta)
+            ops.rope_cache(q3, k3, v3, st.k_cache[li], st.v_cache[li], start, T, cfg.rope_theta)
             qa = q3.view(B, T, cfg.n_heads, 128).transpose(1, 2)
             ka = k3.view(B, T, cfg.n_kv_heads, 128).transpose(1, 2)
             va = v3.view(B, T, cfg.n_kv_heads, 128).transpose(1, 2)
@@ -183,16 +183,16 @@ class MistralLoRAModel:
             attn = attn.transpose(1, 2).reshape(R, cfg.q_dim).contiguous()
             o = nf4.linear(attn, [lw.o])[0]
             ops.sgmv_fused(attn, *lora["o_proj"], indptr, st.slots, o)
-            torch.ops.persona.add_rmsnorm(h, o, lw.post_norm, xn, cfg.rms_eps)
+            ops.add_rmsnorm(h, o, lw.post_norm, xn, cfg.rms_eps)
             g_, u_ = nf4.linear(xn, [lw.gate, lw.up])
             ops.sgmv_fused(xn, *lora["gate_proj"], indptr, st.slots, g_)
             ops.sgmv_fused(xn, *lora["up_proj"], indptr, st.slots, u_)
             act = torch.empty_like(g_)
-            torch.ops.persona.silu_mul(g_, u_, act)
+            ops.silu_mul(g_, u_, act)
             dn = nf4.linear(act, [lw.down])[0]
             ops.sgmv_fused(act, *lora["down_proj"], indptr, st.slots, dn)
             delta = dn
-        torch.ops.persona.add_rmsnorm(h, delta, self.final_norm, xn, cfg.rms_eps)
+        ops.add_rmsnorm(h, delta, self.final_norm, xn, cfg.rms_eps)
         last = xn.view(B, T, cfg.hidden)[:, -1, :]
         logits = torch.matmul(last, self.lm_head.t())
         st.pos.fill_(T)
@@ -208,28 +208,28 @@ class MistralLoRAModel:
         delta = None
         for li, lw in enumerate(self.layers):
             lora = self._lora[li]
-            torch.ops.persona.add_rmsnorm(b["h"], delta, lw.in_norm, b["xn"], cfg.rms_eps)
+            ops.add_rmsnorm(b["h"], delta, lw.in_norm, b["xn"], cfg.rms_eps)
             nf4.linear(b["xn"], [lw.q, lw.k, lw.v], outs=[b["q"], b["k"], b["v"]])
             ops.bgmv_fused_multi([b["xn"]] * 3, [lora[m][0] for m in ("q_proj", "k_proj", "v_proj")],
                                  [lora[m][1] for m in ("q_proj", "k_proj", "v_proj")], st.slots,
                                  [b["q"], b["k"], b["v"]], plan=st.plan)
             q3 = b["q"].view(B, cfg.n_heads, 128)
-            torch.ops.persona.rope_cache(q3, b["k"].view(B, cfg.n_kv_heads, 128), b["v"].view(B, cfg.n_kv_heads, 128),
+            ops.rope_cache(q3, b["k"].view(B, cfg.n_kv_heads, 128), b["v"].view(B, cfg.n_kv_heads, 128),
                                          st.k_cache[li], st.v_cache[li], st.pos, 1, cfg.rope_theta)
-            torch.ops.persona.decode_attention(q3, st.k_cache[li], st.v_cache[li], st.length,
+            ops.decode_attention(q3, st.k_cache[li], st.v_cache[li], st.length,
                                                b["attn"].view(B, cfg.n_heads, 128), scale)
             nf4.linear(b["attn"], [lw.o], outs=[b["o"]])
             ops.bgmv_fused(b["attn"], *lora["o_proj"], st.slots, b["o"], plan=st.plan)
-            torch.ops.persona.add_rmsnorm(b["h"], b["o"], lw.post_norm, b["xn"], cfg.rms_eps)
+            ops.add_rmsnorm(b["h"], b["o"], lw.post_norm, b["xn"], cfg.rms_eps)
             nf4.linear(b["xn"], [lw.gate, lw.up], outs=[b["g"], b["u"]])
             ops.bgmv_fused_multi([b["xn"]] * 2, [lora[m][0] for m in ("gate_proj", "up_proj")],
                                  [lora[m][1] for m in ("gate_proj", "up_proj")], st.slots, [b["g"], b["u"]],
                                  plan=st.plan)
-            torch.ops.persona.silu_mul(b["g"], b["u"], b["act"])
+            ops.silu_mul(b["g"], b["u"], b["act"])
             nf4.linear(b["act"], [lw.down], outs=[b["d"]])
             ops.bgmv_fused(b["act"], *lora["down_proj"], st.slots, b["d"], plan=st.plan)
             delta = b["d"]
-        torch.ops.persona.add_rmsnorm(b["h"], delta, self.final_norm, b["xn"], cfg.rms_eps)
+        ops.add_rmsnorm(b["h"], delta, self.final_norm, b["xn"], cfg.rms_eps)
         torch.matmul(b["xn"], self.lm_head.t(), out=b["logits"])
         st.tok.copy_(torch.argmax(b["logits"], dim=-1))
         st.pos.add_(1)

@@ -179,3 +179,33 @@ def check_errors(device: Optional[torch.device] = None, synchronize: bool = True
         if bits & 4:
             what.append("invalid segment table")
         raise RuntimeError(f"persona: device error 0x{bits:x}: {', '.join(what)}")
+
+
+# ---- fused steps of the end-to-end decode (persona_add_rmsnorm & co.) ------
+def add_rmsnorm(h: torch.Tensor, delta: Optional[torch.Tensor], w: torch.Tensor, out: torch.Tensor,
+                eps: float) -> torch.Tensor:
+    """``h += delta`` (if given) and ``out = w * fp16(h / rms(h))`` per row."""
+    _require_cuda("add_rmsnorm", h, w, out)
+    torch.ops.persona.add_rmsnorm(h, delta, w, out, float(eps))
+    return out
+
+
+def rope_cache(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+               start: torch.Tensor, per_seq: int, theta: float) -> None:
+    """Rotary embedding of q and k in place and the k / v cache write."""
+    _require_cuda("rope_cache", q, k, v, k_cache, v_cache, start)
+    torch.ops.persona.rope_cache(q, k, v, k_cache, v_cache, start, int(per_seq), float(theta))
+
+
+def silu_mul(g: torch.Tensor, u: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+    _require_cuda("silu_mul", g, u, out)
+    torch.ops.persona.silu_mul(g, u, out)
+    return out
+
+
+def decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, length: torch.Tensor,
+                     out: torch.Tensor, scale: float) -> torch.Tensor:
+    """One new token per sequence over the first ``length`` cache positions."""
+    _require_cuda("decode_attention", q, k_cache, v_cache, length, out)
+    torch.ops.persona.decode_attention(q, k_cache, v_cache, length, out, float(scale))
+    return out

@@ -44,11 +44,11 @@ def test_add_rmsnorm_matches_reference():
     hf = want_h.float()
     want = w.float() * (hf * torch.rsqrt(hf.pow(2).mean(-1, keepdim=True) + 1e-5)).half().float()
     out = torch.empty_like(h)
-    torch.ops.persona.add_rmsnorm(h, d, w, out, 1e-5)
+    ops.add_rmsnorm(h, d, w, out, 1e-5)
     assert torch.equal(h, want_h)
     torch.testing.assert_close(out.float(), want, rtol=2e-3, atol=2e-3)
     out2 = torch.empty_like(h)
-    torch.ops.persona.add_rmsnorm(h, None, w, out2, 1e-5)  # no delta: h unchanged
+    ops.add_rmsnorm(h, None, w, out2, 1e-5)  # no delta: h unchanged
     assert torch.equal(h, want_h) and torch.equal(out2, out)
 
 
@@ -64,7 +64,7 @@ def test_rope_cache_matches_reference_and_fills_the_cache():
     pos = (4 + torch.arange(B * T, device=_dev()) % T)
     q_want, k_want = _rope_ref(q, pos, 1e6), _rope_ref(k, pos, 1e6)
     q2, k2 = q.clone(), k.clone()
-    torch.ops.persona.rope_cache(q2, k2, v, kc, vc, start, T, 1e6)
+    ops.rope_cache(q2, k2, v, kc, vc, start, T, 1e6)
     torch.testing.assert_close(q2.float(), q_want, rtol=2e-3, atol=4e-3)
     torch.testing.assert_close(k2.float(), k_want, rtol=2e-3, atol=4e-3)
     for b in range(B):
@@ -78,7 +78,7 @@ def test_silu_mul_matches_reference():
     a = (3 * torch.randn(7, 1024, generator=g, device=_dev())).half()
     b = torch.randn(7, 1024, generator=g, device=_dev()).half()
     out = torch.empty_like(a)
-    torch.ops.persona.silu_mul(a, b, out)
+    ops.silu_mul(a, b, out)
     torch.testing.assert_close(out.float(), (F.silu(a.float()).half().float() * b.float()), rtol=2e-3, atol=2e-3)
 
 
@@ -91,7 +91,7 @@ def test_decode_attention_matches_reference(length):
     vc = torch.randn(B, Hkv, L, 128, generator=g, device=_dev()).half()
     out = torch.empty_like(q)
     ln = torch.tensor([length], dtype=torch.int32, device=_dev())
-    torch.ops.persona.decode_attention(q, kc, vc, ln, out, 1 / math.sqrt(128))
+    ops.decode_attention(q, kc, vc, ln, out, 1 / math.sqrt(128))
     kk = kc[:, :, :length].float().repeat_interleave(Hq // Hkv, dim=1)
     vv = vc[:, :, :length].float().repeat_interleave(Hq // Hkv, dim=1)
     p = torch.softmax(torch.einsum("bhd,bhld->bhl", q.float(), kk) / math.sqrt(128), dim=-1)

@@ -171,3 +171,59 @@ def test_multi_full_size_mixed_decode_layer():
         torch.testing.assert_close(ys[i].float(), y1.float(), **TOL)
         assert torch.equal(ys[i][null], y0[i][null])
     ops.check_errors(dev())
+
+
+@pytest.mark.parametrize("dtype", ["f16", "bf16"])
+@pytest.mark.parametrize("R", [8, 16, 32, 64])
+@pytest.mark.parametrize("T", [1, 5, 8, 64])
+def test_decode_sized_fused_matches_split_kernels_and_oracle(dtype, R, T):
+    """At most PERSONA_SMALL_MAX_ROWS rows run the kernel without cross-CTA
+    steps; it matches the oracle and the split kernels (PERSONA_SPLIT_ONLY)
+    on the same projections, rows without adapter stay untouched."""
+    lib = capi_lib.load()
+    S = 6
+    shapes = [(4096, 4096), (4096, 1024), (14336, 4096), (256, 392)]
+    slots, projs = layer_case(100 + T + R, T, R, S, dtype, names=shapes, null_frac=0.25)
+    sd = torch.from_numpy(slots).to(dev())
+    keep, probs = [], {}
+    outs = {}
+    for flag in (0, 2):  # 2 = PERSONA_SPLIT_ONLY
+        ps, ys = [], []
+        for p in projs:
+            K, N = p["K"], p["N"]
+            x, a, b, y = t16(p["x"], dtype), t16(p["a"], dtype), t16(p["b"], dtype), t16(p["y"], dtype)
+            keep += [x, a, b, y]
+            ys.append(y)
+            ps.append(capi_lib.Problem(x.data_ptr(), K, a.data_ptr(), R * K, K, b.data_ptr(), N * R, y.data_ptr(),
+                                       N, K, N))
+        arr = (capi_lib.Problem * len(ps))(*ps)
+        ws_bytes = lib.persona_bgmv_multi_workspace_size(T, len(ps))
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev())
+        err = torch.zeros(1, dtype=torch.int32, device=dev())
+        stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+        capi_lib.check(lib.persona_bgmv_fused_multi(arr, len(ps), sd.data_ptr(), T, R, S,
+                                                    capi_lib.BF16 if dtype == "bf16" else capi_lib.F16,
+                                                    ws.data_ptr(), ws_bytes, flag, err.data_ptr(), stream))
+        torch.cuda.synchronize()
+        assert int(err.item()) == 0
+        outs[flag] = ys
+        check_against_oracle(slots, projs, ys, dtype)
+    for a_, b_ in zip(outs[0], outs[2]):
+        np.testing.assert_allclose(f32(n16(a_, dtype), dtype), f32(n16(b_, dtype), dtype), **TOL)
+
+
+def test_decode_sized_fused_flags_out_of_range_slots():
+    dtype, T, R, S = "f16", 4, 16, 3
+    slots, projs = layer_case(77, T, R, S, dtype, names=[(512, 256)], null_frac=0.0)
+    slots[2] = 5  # out of range: the row is left alone and the slot error is raised
+    p = projs[0]
+    y = t16(p["y"], dtype)
+    ops.bgmv_fused(t16(p["x"], dtype), t16(p["a"], dtype), t16(p["b"], dtype), torch.from_numpy(slots).to(dev()), y)
+    with pytest.raises(RuntimeError, match="slot"):
+        ops.check_errors(dev())
+    got = n16(y, dtype)
+    assert np.array_equal(got[2], p["y"][2])
+    ok = np.array([0, 1, 3])
+    want = p["y"][ok].copy()
+    O.bgmv_forward_ref(p["x"][ok], p["a"], p["b"], slots[ok], dtype, y=want)
+    np.testing.assert_allclose(f32(got[ok], dtype), f32(want, dtype), **TOL)
