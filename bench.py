@@ -55,11 +55,12 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["mixed_decode", "sgmv_prefill", "decode_set", "e2e_decode"],
+    ap.add_argument("--workload", choices=["mixed_decode", "sgmv_prefill", "decode_set", "e2e_decode", "nf4_decode"],
                     default="mixed_decode",
                     help="mixed_decode is the headline; the others print their own line")
     ap.add_argument("--batch", type=int, default=None,
-                    help="e2e_decode: rows per GPU (default 8 on one GPU, 64 per replica on several)")
+                    help="e2e_decode: rows per GPU (default 8 on one GPU, 64 per replica on several); "
+                         "nf4_decode: rows of x (default 8)")
     ap.add_argument("--only", default=None,
                     help="restrict to one projection (e.g. gate_proj), for profiling a small case")
     return ap.parse_args()
@@ -876,6 +877,74 @@ def run_e2e(args):
     return 0
 
 
+def run_nf4(args):
+    """The seven NF4 base projections of a Mistral-7B decoder layer at decode
+    (8 rows of x by default), as the decode step launches them: q / k / v in
+    one launch, then o, gate / up, down.  Eight distinct layers (0.9 GB of
+    packed weights, more than L2) are cycled through a CUDA graph, so every
+    launch streams its weights from HBM.  Metric: packed-weight GB/s."""
+    import torch
+
+    from persona import nf4, ops
+    from persona.workloads import PROJECTIONS
+
+    if args.gpus != 1:
+        raise SystemExit("--workload nf4_decode runs on one GPU")
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    M = args.batch or 8
+    g = torch.Generator(device=dev)
+    g.manual_seed(SEED * 1000 + 41)
+    groups = [["q_proj", "k_proj", "v_proj"], ["o_proj"], ["gate_proj", "up_proj"], ["down_proj"]]
+    if ONLY is not None:
+        groups = [gr for gr in groups if ONLY in gr or ONLY == "+".join(gr)]
+    names = [n for gr in groups for n in gr]
+    layers = 8
+    qs = [{n: nf4.quantize((torch.randn(PROJECTIONS[n][1], PROJECTIONS[n][0], generator=g, device=dev) * 0.02)
+                           .half()) for n in names} for _ in range(layers)]
+    xs = {n: torch.randn(M, PROJECTIONS[n][0], generator=g, device=dev).half() for n in names}
+    ys = {n: torch.empty(M, PROJECTIONS[n][1], dtype=torch.float16, device=dev) for n in names}
+
+    def body():
+        for lq in qs:
+            for gr in groups:
+                nf4.linear(xs[gr[0]], [lq[n] for n in gr], outs=[ys[n] for n in gr])
+
+    s = torch.cuda.Stream(dev)
+    s.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(s):
+        body()  # makes the workspace outside the capture
+    torch.cuda.current_stream(dev).wait_stream(s)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        body()
+    warm, steps = max(3, args.warmup), max(1, min(args.steps, 200))
+    for _ in range(warm):
+        graph.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    ops.check_errors(dev)
+    ms = e0.elapsed_time(e1) / steps / layers  # one layer's launches
+    byts = sum(qs[0][n].nbytes for n in names)
+    peak, _ = load_peaks()
+    print(json.dumps({
+        "workload": "nf4_decode", "metric": "NF4 base linear GB/s (packed weights streamed)",
+        "value": byts / (ms * 1e-3) / 1e9, "unit": "GB/s", "n_gpus": 1, "steps": steps, "warmup": warm,
+        "ms_per_step": ms, "dtype": "f16 x, NF4 weights", "data": "synthetic",
+        "config": {"workload": f"Mistral-7B layer base projections, {M} rows", "groups": ["+".join(gr) for gr in groups],
+                   "l2": "8 distinct layers cycled (0.9 GB > L2)"},
+        "roofline": {"bound": "hbm", "achieved": byts / (ms * 1e-3) / 1e9, "peak": peak, "unit": "GB/s",
+                     "frac": byts / (ms * 1e-3) / 1e9 / peak},
+        "gpu_launches": steps * layers * len(groups),
+    }), flush=True)
+    return 0
+
+
 def main():
     global ONLY
     args = parse_args()
@@ -884,6 +953,8 @@ def main():
         return run_reference(args)
     if args.workload == "e2e_decode":
         return run_e2e(args)
+    if args.workload == "nf4_decode":
+        return run_nf4(args)
     if args.workload == "sgmv_prefill" and args.gpus > 1:
         return run_sgmv_tp(args)
     if args.workload != "mixed_decode":

@@ -40,6 +40,32 @@ __global__ void __launch_bounds__(kSmallThreads) bgmv_small_kernel(const SmallAr
     if (i < args.num_problems && u >= args.unit_base[i]) p = i;
   const SmallProblem& pr = args.prob[p];
   const int row = u - args.unit_base[p];
+  const int K = pr.K, N = pr.N, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // this CTA's K range (eighths rounded to 8 values) and column range
+  const int kper = ((K + kSmallCluster * 8 - 1) / (kSmallCluster * 8)) * 8;
+  const int k0 = min(K, rank * kper), k1 = min(K, k0 + kper);
+  const int nper = (N + kSmallCluster - 1) / kSmallCluster;
+  const int n0 = min(N, rank * nper), n1 = min(N, n0 + nper);
+  {
+    // Launched as a programmatic dependent of the kernel before it (at
+    // decode: the base GEMM that writes y): pull this CTA's A and B lines
+    // into L2 while that kernel finishes.  Only a prefetch reads the slot
+    // here (it may not be final yet), and only for a slot in range.
+    const int sp = args.slots[row];
+    if (sp >= 0 && sp < args.S) {
+      const char* ab = static_cast<const char*>(pr.a) + static_cast<int64_t>(sp) * pr.a_slot_stride * 2;
+      const int lines_a = (2 * (k1 - k0) + 127) / 128;
+      for (int i = tid; i < R * lines_a; i += kSmallThreads) {
+        const char* q = ab + (static_cast<int64_t>(i / lines_a) * pr.a_row_stride + k0) * 2 + (i % lines_a) * 128;
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(q));
+      }
+      const char* bb = static_cast<const char*>(pr.b) + (static_cast<int64_t>(sp) * pr.b_slot_stride +
+                                                          static_cast<int64_t>(n0) * R) * 2;
+      for (int i = tid; i < ((n1 - n0) * R * 2 + 127) / 128; i += kSmallThreads)
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(bb + static_cast<int64_t>(i) * 128));
+    }
+  }
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int s = args.slots[row];
   // the whole cluster takes the same exit, so the barriers below stay matched
   if (s < 0) return;
@@ -47,10 +73,6 @@ __global__ void __launch_bounds__(kSmallThreads) bgmv_small_kernel(const SmallAr
     if (threadIdx.x == 0 && rank == 0 && p == 0) raise_error(args.err, PERSONA_DEV_ERR_SLOT);
     return;
   }
-  const int K = pr.K, N = pr.N, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  // this CTA's K range: eighths rounded to 8 values
-  const int kper = ((K + kSmallCluster * 8 - 1) / (kSmallCluster * 8)) * 8;
-  const int k0 = min(K, rank * kper), k1 = min(K, k0 + kper);
   uint16_t* xs = reinterpret_cast<uint16_t*>(small_smem);
   const uint16_t* xr = static_cast<const uint16_t*>(pr.x) + static_cast<int64_t>(row) * pr.ldx;
   for (int i = k0 + tid * 8; i < k1; i += kSmallThreads * 8)
@@ -91,8 +113,6 @@ __global__ void __launch_bounds__(kSmallThreads) bgmv_small_kernel(const SmallAr
 #pragma unroll
   for (int r = 0; r < R; ++r) v[r] = v_all[r];
   // expand: this CTA's eighth of the columns, one per thread
-  const int nper = (N + kSmallCluster - 1) / kSmallCluster;
-  const int n0 = min(N, rank * nper), n1 = min(N, n0 + nper);
   const uint16_t* bb = static_cast<const uint16_t*>(pr.b) + static_cast<int64_t>(s) * pr.b_slot_stride;
   uint16_t* yr = static_cast<uint16_t*>(pr.y) + static_cast<int64_t>(row) * pr.ldy;
 #pragma unroll 2
@@ -129,13 +149,15 @@ cudaError_t small_launch(const SmallArgs& a, int clusters, size_t smem, cudaStre
   cfg.blockDim = dim3(kSmallThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = kSmallCluster;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a);
   if (e != cudaSuccess) return e;
   return cudaGetLastError();

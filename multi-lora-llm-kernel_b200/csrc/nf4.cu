@@ -250,6 +250,8 @@ __global__ void __launch_bounds__(kNf4Threads, 1)
   __shared__ uint32_t lut1[256];
   __shared__ int s_fin;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // the LoRA kernel after this one may start prefetching its weights
+  asm volatile("griddepcontrol.launch_dependents;");
 
   if (tid < 256) lut1[tid] = nf4_half_bits(tid >> 4) | (nf4_half_bits(tid & 15) << 16);
   if (tid == 0) {
