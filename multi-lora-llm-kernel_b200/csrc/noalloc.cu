@@ -4,8 +4,11 @@
 // The array is a file-scope __device__ variable, one copy per device, loaded
 // with the library's device code.  Its device address is looked up once per
 // device (cudaGetSymbolAddress with that device current) and then handed to
-// the same plan + split kernels persona_bgmv_fused runs.  Nothing here
-// calls cudaMalloc / cudaFree or any allocating routine.
+// persona_bgmv_fused as its workspace: the plan kernel writes the plan there,
+// then the split kernels use it for their partial sums and counters (at up to
+// PERSONA_SMALL_MAX_ROWS rows the decode-sized kernel runs instead and reads
+// nothing from it).  Nothing here calls cudaMalloc / cudaFree or any
+// allocating routine.
 //
 // The plan kernel rewrites every field the fused kernel reads (header, row
 // permutation, items) and resets the kernel's shared counters on each call,
