@@ -373,7 +373,8 @@ __global__ void __launch_bounds__(kNf4Threads, 1)
           for (int ks = 0; ks < 4; ++ks) {
             uint32_t a[4];
 #pragma unroll
-            for (int j = 0; j < 4; ++j) a[j] = lds32(lut_lane + ((words[ks] >> (8 * j)) & 0xffu) * 128u);
+            for (int j = 0; j < 4; ++j)  // byte j alone (one byte permute), then one shift-add
+              a[j] = lds32(lut_lane + (__byte_perm(words[ks], 0u, 0x4440u + j) << 7));
 #pragma unroll
             for (int mt = 0; mt < MT; ++mt) {
               const uint32_t b[2] = {bf[mt][ks >> 1][(ks & 1) * 2], bf[mt][ks >> 1][(ks & 1) * 2 + 1]};
