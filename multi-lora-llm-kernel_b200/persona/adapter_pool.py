@@ -276,6 +276,13 @@ class AdapterPool:
                                        generator=generator) * 0.01)
         return slot
 
+    def clear_slot(self, slot: int) -> None:
+        """Zero ``slot`` in every pool of every layer (a slot handed to a new
+        adapter must not keep modules of the one before)."""
+        for pools in self.layers:
+            for f in fields(LayerPools):
+                getattr(pools, f.name)[slot].zero_()
+
     def a_pool(self, layer_idx: int, module: str) -> torch.Tensor:
         """``[S, r, K]`` A view of one module (a rank block of a packed pool)."""
         a_name, block, _ = MODULE_POOLS[module]
@@ -287,6 +294,91 @@ class AdapterPool:
     def nbytes(self) -> int:
         return sum(getattr(lp, f.name).numel() * getattr(lp, f.name).element_size()
                    for lp in self.layers for f in fields(LayerPools))
+
+
+class AdapterCache:
+    """More adapters than the pool has slots: LRU paging of the GPU slots.
+
+    The reference's pool keeps every adapter resident ("Version 1 ... without
+    LRU paging", reference ``persona/adapter_pool.py:151``).  Here adapters
+    are registered by name (a PEFT directory, read once, or in-memory
+    ``{layer: {module: (A [r, in], B [out, r])}}`` tensors, scale already
+    folded); each keeps a pinned host copy, and ``acquire`` makes the
+    adapters of one batch resident: a miss takes a free slot or evicts the
+    least recently used adapter that the batch does not use, zeroes that slot
+    and copies the adapter in on the current stream (behind any work already
+    queued that still reads the old contents).
+    """
+
+    def __init__(self, pool: AdapterPool):
+        self.pool = pool
+        self._host: Dict[str, Dict[int, Dict[str, Tuple[torch.Tensor, torch.Tensor]]]] = {}
+        self._lru: List[str] = []  # resident adapters, least recently used first
+        self.hits = 0
+        self.misses = 0
+        self.evictions = 0
+
+    def register(self, name: str, adapter_dir: Optional[Path] = None,
+                 layers: Optional[Dict[int, Dict[str, Tuple[torch.Tensor, torch.Tensor]]]] = None) -> None:
+        if (adapter_dir is None) == (layers is None):
+            raise ValueError("register: give exactly one of adapter_dir and layers")
+        if adapter_dir is not None:
+            cfg, layers = load_peft_adapter_tensors(Path(adapter_dir), dtype=self.pool.dtype)
+            if cfg.r != self.pool.r:
+                raise ValueError(f"Adapter rank {cfg.r} != pool rank {self.pool.r}")
+        pin = self.pool.device.type == "cuda"
+        host = {}
+        for li, mods in layers.items():
+            if not 0 <= li < self.pool.num_layers:
+                raise ValueError(f"{name}: layer {li} outside the pool")
+            host[li] = {m: tuple((t.to(self.pool.dtype).contiguous().cpu().pin_memory() if pin
+                                  else t.to(self.pool.dtype).contiguous().cpu()) for t in ab)
+                        for m, ab in mods.items()}
+        self._host[name] = host
+        if name in self.pool.name_to_slot:  # re-registered while resident: refresh the slot
+            self._load(name, self.pool.name_to_slot[name])
+
+    @property
+    def registered(self) -> List[str]:
+        return list(self._host)
+
+    @property
+    def resident(self) -> List[str]:
+        """Resident adapters, least recently used first."""
+        return list(self._lru)
+
+    def acquire(self, names: Sequence[str]) -> List[int]:
+        """Slots of ``names`` (one batch; repeats allowed), loading misses."""
+        want = list(dict.fromkeys(names))
+        for n in want:
+            if n not in self._host:
+                raise KeyError(f"adapter {n!r} is not registered")
+        if len(want) > self.pool.max_slots:
+            raise RuntimeError(f"a batch of {len(want)} adapters does not fit {self.pool.max_slots} slots")
+        for n in want:
+            if n in self.pool.name_to_slot:
+                self.hits += 1
+                self._lru.remove(n)
+            else:
+                self.misses += 1
+                if not self.pool._free_slots:
+                    victims = [v for v in self._lru if v not in want]
+                    if not victims:
+                        raise RuntimeError("no slot can be freed: every slot holds an adapter of this batch or "
+                                           "one loaded into the pool directly")
+                    victim = victims[0]
+                    self._lru.remove(victim)
+                    self.pool.release_slot(victim)
+                    self.evictions += 1
+                slot = self.pool.acquire_slot(n)
+                self.pool.clear_slot(slot)
+                self._load(n, slot)
+            self._lru.append(n)
+        return [self.pool.name_to_slot[n] for n in names]
+
+    def _load(self, name: str, slot: int) -> None:
+        for li, mods in self._host[name].items():
+            self.pool.pack_layer(li, slot, mods)
 
 
 def validate_uniform_adapters(adapter_dirs: Sequence[Path]) -> AdapterConfig:

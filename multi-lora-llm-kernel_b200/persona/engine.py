@@ -14,11 +14,11 @@ Prompts are token ids: this build ships no tokenizer.
 from __future__ import annotations
 
 from dataclasses import dataclass, field
-from typing import List, Sequence
+from typing import List, Optional, Sequence
 
 import torch
 
-from persona.adapter_pool import AdapterPool
+from persona.adapter_pool import AdapterCache, AdapterPool
 from persona.mistral import MistralLoRAModel
 from persona.sampling import SamplingParams, sample_next_token
 
@@ -35,9 +35,16 @@ class Request:
 class StaticBatchEngine:
     """All requests of a batch share the prompt length and start together."""
 
-    def __init__(self, model: MistralLoRAModel, pool: AdapterPool, max_batch: int = 8, max_seq_len: int = 2048):
+    def __init__(self, model: MistralLoRAModel, pool: AdapterPool, max_batch: int = 8, max_seq_len: int = 2048,
+                 cache: Optional[AdapterCache] = None):
+        """With ``cache``, a request whose ``persona_name`` is registered there
+        gets its slot from ``cache.acquire`` (its adapter paged in if needed);
+        other requests keep the slot they carry."""
+        if cache is not None and cache.pool is not pool:
+            raise ValueError("the adapter cache must page this engine's pool")
         self.model = model
         self.pool = pool
+        self.cache = cache
         self.max_batch = max_batch
         self.max_seq_len = max_seq_len
         self.device = model.device
@@ -48,6 +55,12 @@ class StaticBatchEngine:
     def plan_batch(self, requests: Sequence[Request]) -> torch.Tensor:
         if len(requests) > self.max_batch:
             raise ValueError("Static batch exceeds max_batch")
+        if self.cache is not None:
+            names = [r.persona_name for r in requests if r.persona_name in self.cache.registered]
+            slots = iter(self.cache.acquire(names))
+            for r in requests:
+                if r.persona_name in self.cache.registered:
+                    r.slot = next(slots)
         return torch.tensor([r.slot for r in requests], dtype=torch.int32, device=self.device)
 
     @torch.inference_mode()
@@ -56,7 +69,7 @@ class StaticBatchEngine:
         """Generate ``max_new_tokens`` per request; returns the new token ids
         [batch, max_new_tokens] (CPU) and the device time of the prefill and of
         the decode loop (CUDA events)."""
-        slots = self.plan_batch(requests)
+        slots = self.plan_batch(requests)  # fills r.slot from the cache first
         lens = {len(r.prompt) for r in requests}
         if len(lens) != 1:
             raise ValueError("static batching needs prompts of one length")

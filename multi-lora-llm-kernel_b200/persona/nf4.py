@@ -13,6 +13,7 @@ inputs (prefill) the weight is expanded to fp16 by
 
 from __future__ import annotations
 
+import os
 from dataclasses import dataclass
 from typing import List, Optional, Sequence
 
@@ -22,8 +23,8 @@ import torch.nn as nn
 from persona import ops
 
 # Rows of x up to which the streaming kernel is used; above it the weight is
-# dequantised and multiplied densely.
-DENSE_ABOVE_ROWS = 64
+# dequantised and multiplied densely.  PERSONA_NF4_DENSE_ABOVE overrides it.
+DENSE_ABOVE_ROWS = int(os.environ.get("PERSONA_NF4_DENSE_ABOVE", "64"))
 
 
 @dataclass
@@ -56,13 +57,15 @@ def dequantize(q: NF4Weight) -> torch.Tensor:
 
 
 def linear(x: torch.Tensor, weights: Sequence[NF4Weight], outs: Optional[Sequence[torch.Tensor]] = None,
-           dense_above: int = DENSE_ABOVE_ROWS) -> List[torch.Tensor]:
+           dense_above: Optional[int] = None) -> List[torch.Tensor]:
     """``y_i = x @ W_i^T`` for up to four weights that share x ([M, K] fp16,
     unit inner stride); one launch at decode sizes."""
     ops._load()
     if x.dim() != 2:
         raise ValueError("nf4.linear: x must be [M, K]")
     M = x.shape[0]
+    if dense_above is None:
+        dense_above = DENSE_ABOVE_ROWS
     if outs is None:
         outs = [torch.empty(M, w.N, dtype=torch.float16, device=x.device) for w in weights]
     if M > dense_above:

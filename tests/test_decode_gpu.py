@@ -191,3 +191,36 @@ def test_engine_graph_and_eager_generate_the_same_tokens():
     assert a["tok_per_s"] > 0
     with pytest.raises(ValueError):
         eng.run_static_generate(reqs + reqs[:2], max_new_tokens=4)
+
+
+def test_engine_pages_adapters_through_the_cache():
+    """Three adapters, two slots: the second batch evicts one adapter; each
+    row's tokens equal those of the same adapter in a fresh pool (rows are
+    computed independently)."""
+    from persona.adapter_pool import AdapterCache
+
+    geom = (CFG.hidden, CFG.kv_dim, CFG.intermediate)
+    dims = {"q_proj": (CFG.hidden, CFG.q_dim), "k_proj": (CFG.hidden, CFG.kv_dim), "v_proj": (CFG.hidden, CFG.kv_dim),
+            "o_proj": (CFG.q_dim, CFG.hidden), "gate_proj": (CFG.hidden, CFG.intermediate),
+            "up_proj": (CFG.hidden, CFG.intermediate), "down_proj": (CFG.intermediate, CFG.hidden)}
+    g = torch.Generator().manual_seed(4)
+    ads = {f"c{i}": {li: {m: ((torch.randn(16, k, generator=g) * 0.02).half(), (torch.randn(n, 16, generator=g) * 0.02)
+                              .half()) for m, (k, n) in dims.items()} for li in range(CFG.num_layers)} for i in range(3)}
+    prompt = torch.randint(0, CFG.vocab, (10,), generator=g).tolist()
+
+    def engine(names):
+        pool = AdapterPool(max_slots=2, r=16, device=_dev(), num_layers=CFG.num_layers, geometry=geom)
+        cache = AdapterCache(pool)
+        for n in names:
+            cache.register(n, layers=ads[n])
+        model = MistralLoRAModel(CFG, pool, _dev(), seed=5)
+        return cache, StaticBatchEngine(model, pool, max_batch=2, max_seq_len=64, cache=cache)
+
+    cache, eng = engine(["c0", "c1", "c2"])
+    out1 = eng.run_static_generate([Request("r0", "c0", prompt), Request("r1", "c1", prompt)], max_new_tokens=6)
+    out2 = eng.run_static_generate([Request("r2", "c2", prompt), Request("r0", "c0", prompt)], max_new_tokens=6)
+    assert cache.evictions == 1 and "c1" not in cache.resident
+    assert torch.equal(out1["tokens"][0], out2["tokens"][1])
+    _, fresh = engine(["c2"])
+    out3 = fresh.run_static_generate([Request("r2", "c2", prompt), Request("x", "c2", prompt)], max_new_tokens=6)
+    assert torch.equal(out3["tokens"][0], out2["tokens"][0])
