@@ -435,7 +435,7 @@ def run_ours(args):
         achieved = step_bytes / (fused_ms_per_step * 1e-3) / 1e9
         traffic = None
         tf = ROOT / "profiles" / "bgmv_fused_mixed_batch_traffic.json"
-        if tf.exists():
+        if tf.exists() and world == 1:  # captured on the one-GPU launch (512 rows)
             traffic = json.loads(tf.read_text()).get("traffic_bytes_per_launch")
         line = {
             "metric": METRIC,
