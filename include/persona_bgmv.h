@@ -137,6 +137,14 @@ typedef struct persona_bgmv_problem {
   int64_t K;
   int64_t N;
 } persona_bgmv_problem;
+/* LoRA term alone at decode sizes (T <= PERSONA_SMALL_MAX_ROWS):
+ * deltas[i][t, n] = (B_i[s] (A_i[s] x_i[t]))[n] in fp32, 0 for rows without an
+ * adapter; the problems' y / ldy are ignored.  Same math as the fused op
+ * (reference persona/ops.py:12-56) without the add into y, for callers that
+ * fold the term into the base projection's output (persona_nf4_linear_add). */
+int persona_bgmv_lora_delta_multi(const persona_bgmv_problem* problems, int num_problems, float* const* deltas,
+                                  const int64_t* ld_deltas, const int32_t* slots, int64_t T, int64_t R, int64_t S,
+                                  int dtype, int32_t* dev_err, cudaStream_t stream);
 size_t persona_bgmv_multi_workspace_size(int64_t T, int num_problems);
 int persona_bgmv_fused_multi(const persona_bgmv_problem* problems, int num_problems, const int32_t* slots,
                              int64_t T, int64_t R, int64_t S, int dtype, void* workspace, size_t workspace_bytes,
@@ -270,6 +278,16 @@ size_t persona_nf4_linear_workspace_size(const persona_nf4_problem* problems, in
  * same x); any M (launches of at most 64 rows each).                        */
 int persona_nf4_linear(const persona_nf4_problem* problems, int num_problems, int64_t M, void* workspace,
                        size_t workspace_bytes, int32_t* dev_err, cudaStream_t stream);
+/* The same with an fp32 addend per problem (addends[i] may be NULL):
+ * y = fp16(x W^T + addend), one rounding.  With the LoRA delta below as the
+ * addend this is the patched projection base(x) + B[s] A[s] x of the
+ * reference's MultiLoRALinear (persona/lora_layer.py:30-57) with one rounding
+ * instead of two.  Launched as a programmatic dependent of the kernel before
+ * it on the stream: its weight streaming starts while that kernel (which
+ * writes x or the addend) finishes.                                         */
+int persona_nf4_linear_add(const persona_nf4_problem* problems, int num_problems, const float* const* addends,
+                           const int64_t* ld_addends, int64_t M, void* workspace, size_t workspace_bytes,
+                           int32_t* dev_err, cudaStream_t stream);
 
 /* ---- end-to-end decode helpers -------------------------------------------
  * Fused elementwise steps of the Mistral-7B decoder around the LoRA layers,

@@ -63,6 +63,8 @@ struct SmallProblem {
   int K, N;
   int slices;   // column slices per row (set by the launcher)
   int x_bytes;  // shared-memory bytes of one x row (set by the launcher)
+  float* delta;      // non-null: write B[s] (A[s] x) here (fp32, 0 for rows
+  int64_t ld_delta;  // without adapter) instead of adding it into y
 };
 
 struct SmallArgs {

@@ -27,6 +27,8 @@ constexpr int kSmallCluster = 8;
 
 template <typename DT, int R>
 __global__ void __launch_bounds__(kSmallThreads) bgmv_small_kernel(const SmallArgs args) {
+  // a base GEMM launched after this kernel may start streaming its weights
+  asm volatile("griddepcontrol.launch_dependents;");
   extern __shared__ __align__(16) uint8_t small_smem[];
   __shared__ float v_part[R];
   __shared__ float v_all[R];
@@ -67,10 +69,12 @@ __global__ void __launch_bounds__(kSmallThreads) bgmv_small_kernel(const SmallAr
   }
   asm volatile("griddepcontrol.wait;" ::: "memory");
   const int s = args.slots[row];
-  // the whole cluster takes the same exit, so the barriers below stay matched
-  if (s < 0) return;
-  if (s >= args.S) {
-    if (threadIdx.x == 0 && rank == 0 && p == 0) raise_error(args.err, PERSONA_DEV_ERR_SLOT);
+  // the whole cluster takes the same exit, so the barriers below stay matched;
+  // a row without adapter adds nothing (a zero delta)
+  if (s < 0 || s >= args.S) {
+    if (s >= args.S && threadIdx.x == 0 && rank == 0 && p == 0) raise_error(args.err, PERSONA_DEV_ERR_SLOT);
+    if (pr.delta)
+      for (int n = n0 + tid; n < n1; n += kSmallThreads) pr.delta[static_cast<int64_t>(row) * pr.ld_delta + n] = 0.f;
     return;
   }
   uint16_t* xs = reinterpret_cast<uint16_t*>(small_smem);
@@ -121,7 +125,7 @@ __global__ void __launch_bounds__(kSmallThreads) bgmv_small_kernel(const SmallAr
     uint4 bv[R / 8];
 #pragma unroll
     for (int c = 0; c < R / 8; ++c) bv[c] = br[c];
-    const uint16_t yo = yr[n];
+    const uint16_t yo = pr.delta ? uint16_t(0) : yr[n];
     float acc = 0.f;
 #pragma unroll
     for (int c = 0; c < R / 8; ++c) {
@@ -133,7 +137,10 @@ __global__ void __launch_bounds__(kSmallThreads) bgmv_small_kernel(const SmallAr
         acc = fmaf(bf.y, v[8 * c + 2 * j + 1], acc);
       }
     }
-    yr[n] = Cvt<DT>::from1(Cvt<DT>::to1(yo) + acc);
+    if (pr.delta)
+      pr.delta[static_cast<int64_t>(row) * pr.ld_delta + n] = acc;
+    else
+      yr[n] = Cvt<DT>::from1(Cvt<DT>::to1(yo) + acc);
   }
 }
 

@@ -626,6 +626,96 @@ void decode_attention_op(const at::Tensor& q, const at::Tensor& k_cache, const a
 }
 }  // namespace
 
+namespace {
+// LoRA term alone at decode sizes (persona_bgmv_lora_delta_multi): deltas[i]
+// is fp32 [T, N_i]; the base projection adds it (nf4_linear_add).
+void lora_delta_multi_op(at::TensorList xs, at::TensorList a_pools, at::TensorList b_pools, const at::Tensor& slots,
+                         at::TensorList deltas) {
+  const char* op = "bgmv_lora_delta_multi";
+  const int P = static_cast<int>(xs.size());
+  TORCH_CHECK(P >= 1 && P <= PERSONA_MAX_PROBLEMS, op, ": 1 to ", PERSONA_MAX_PROBLEMS, " projections");
+  TORCH_CHECK(a_pools.size() == xs.size() && b_pools.size() == xs.size() && deltas.size() == xs.size(), op,
+              ": xs, a_pools, b_pools and deltas must have the same length");
+  TORCH_CHECK(slots.is_cuda() && slots.is_contiguous() && slots.dim() == 1 && slots.scalar_type() == at::kInt, op,
+              ": slots must be a contiguous int32 CUDA vector");
+  const int64_t T = slots.size(0);
+  const int64_t S = a_pools[0].size(0), R = a_pools[0].size(1);
+  const int dt = dtype_code(xs[0], op);
+  persona_bgmv_problem probs[PERSONA_MAX_PROBLEMS];
+  float* dptr[PERSONA_MAX_PROBLEMS];
+  int64_t dld[PERSONA_MAX_PROBLEMS];
+  for (int p = 0; p < P; ++p) {
+    const at::Tensor &x = xs[p], &a = a_pools[p], &b = b_pools[p], &d = deltas[p];
+    TORCH_CHECK(x.is_cuda() && a.is_cuda() && b.is_cuda() && d.is_cuda(), op, ": all tensors must be CUDA");
+    TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1 && d.dim() == 2 && d.stride(1) == 1, op,
+                ": tensors must be contiguous");
+    TORCH_CHECK(d.scalar_type() == at::kFloat, op, ": deltas must be float32");
+    check_pool_a(a, op);
+    check_pool_b(b, op);
+    TORCH_CHECK(x.size(0) == T && d.size(0) == T, op, ": x / delta rows must match slots");
+    TORCH_CHECK(a.size(0) == S && a.size(1) == R && a.size(2) == x.size(1), op, ": a_pool shape mismatch");
+    TORCH_CHECK(b.size(0) == S && b.size(2) == R && b.size(1) == d.size(1), op, ": b_pool shape mismatch");
+    TORCH_CHECK(x.scalar_type() == xs[0].scalar_type() && a.scalar_type() == x.scalar_type() &&
+                    b.scalar_type() == x.scalar_type(),
+                op, ": dtype mismatch");
+    probs[p] = persona_bgmv_problem{x.data_ptr(), row_stride(x), a.data_ptr(), a.stride(0), a.stride(1),
+                                    b.data_ptr(), b.stride(0),   nullptr,      0,            x.size(1),
+                                    d.size(1)};
+    dptr[p] = d.data_ptr<float>();
+    dld[p] = row_stride(d);
+  }
+  const at::cuda::OptionalCUDAGuard guard(slots.device());
+  const int dev = slots.get_device();
+  raise_pending(dev, op);
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  check_status(persona_bgmv_lora_delta_multi(probs, P, dptr, dld, slots.data_ptr<int32_t>(), T, R, S, dt,
+                                             error_word_device(dev), stream),
+               op);
+  after_launch(dev, op, stream);
+}
+
+void nf4_linear_add_op(const at::Tensor& x, at::TensorList packed, at::TensorList offsets, at::TensorList addends,
+                       at::TensorList ys) {
+  const char* op = "nf4_linear_add";
+  const int n = static_cast<int>(packed.size());
+  TORCH_CHECK(n >= 1 && n <= PERSONA_NF4_MAX_PROBLEMS, op, ": 1 to ", PERSONA_NF4_MAX_PROBLEMS, " weights");
+  TORCH_CHECK(static_cast<int>(offsets.size()) == n && static_cast<int>(ys.size()) == n &&
+                  static_cast<int>(addends.size()) == n,
+              op, ": one offset, one addend and one y per weight");
+  TORCH_CHECK(x.is_cuda() && x.dim() == 2 && x.stride(1) == 1 && x.scalar_type() == at::kHalf, op,
+              ": x must be a CUDA float16 [M, K] matrix with unit inner stride");
+  const int64_t M = x.size(0), K = x.size(1);
+  persona_nf4_problem probs[PERSONA_NF4_MAX_PROBLEMS];
+  const float* add[PERSONA_NF4_MAX_PROBLEMS];
+  int64_t ldadd[PERSONA_NF4_MAX_PROBLEMS];
+  for (int i = 0; i < n; ++i) {
+    const at::Tensor& y = ys[i];
+    const at::Tensor& d = addends[i];
+    TORCH_CHECK(y.is_cuda() && y.dim() == 2 && y.stride(1) == 1 && y.scalar_type() == at::kHalf && y.size(0) == M,
+                op, ": y must be a CUDA float16 [M, N] matrix with unit inner stride");
+    const int64_t N = y.size(1);
+    TORCH_CHECK(d.is_cuda() && d.dim() == 2 && d.stride(1) == 1 && d.scalar_type() == at::kFloat &&
+                    d.size(0) == M && d.size(1) == N,
+                op, ": addend must be a CUDA float32 [M, N] matrix with unit inner stride");
+    check_nf4_weight(packed[i], offsets[i], N, K, op);
+    probs[i] = persona_nf4_problem{packed[i].data_ptr(), offsets[i].data_ptr<float>(), x.data_ptr(), row_stride(x),
+                                   y.data_ptr(), row_stride(y), N, K};
+    add[i] = d.data_ptr<float>();
+    ldadd[i] = row_stride(d);
+  }
+  const at::cuda::OptionalCUDAGuard guard(x.device());
+  const int dev = x.get_device();
+  raise_pending(dev, op);
+  if (M == 0) return;
+  at::Tensor ws = nf4_workspace(persona_nf4_linear_workspace_size(probs, n), x);
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  check_status(persona_nf4_linear_add(probs, n, add, ldadd, M, ws.data_ptr(), ws.numel(), error_word_device(dev),
+                                      stream),
+               op);
+  after_launch(dev, op, stream);
+}
+}  // namespace
+
 TORCH_LIBRARY(persona, m) {
   // Reference schemas, unchanged (csrc/bindings.cpp:19-23).
   m.def("bgmv_shrink(Tensor x, Tensor a_pool, Tensor slots, Tensor(a!) v) -> ()");
@@ -647,6 +737,9 @@ TORCH_LIBRARY(persona, m) {
   m.def("nf4_quantize(Tensor w) -> (Tensor, Tensor)");
   m.def("nf4_dequantize(Tensor packed, Tensor offset, int N, int K) -> Tensor");
   m.def("nf4_linear(Tensor x, Tensor[] packed, Tensor[] offsets, Tensor(a!)[] ys) -> ()");
+  m.def("nf4_linear_add(Tensor x, Tensor[] packed, Tensor[] offsets, Tensor[] addends, Tensor(a!)[] ys) -> ()");
+  m.def("bgmv_lora_delta_multi(Tensor[] xs, Tensor[] a_pools, Tensor[] b_pools, Tensor slots, "
+        "Tensor(a!)[] deltas) -> ()");
   m.def("add_rmsnorm(Tensor(a!) h, Tensor? delta, Tensor w, Tensor(b!) out, float eps) -> ()");
   m.def("rope_cache(Tensor(a!) q, Tensor(b!) k, Tensor v, Tensor(c!) k_cache, Tensor(d!) v_cache, Tensor start, "
         "int per_seq, float theta) -> ()");
@@ -658,6 +751,8 @@ TORCH_LIBRARY_IMPL(persona, CUDA, m) {
   m.impl("nf4_quantize", &nf4_quantize_op);
   m.impl("nf4_dequantize", &nf4_dequantize_op);
   m.impl("nf4_linear", &nf4_linear_op);
+  m.impl("nf4_linear_add", &nf4_linear_add_op);
+  m.impl("bgmv_lora_delta_multi", &lora_delta_multi_op);
   m.impl("add_rmsnorm", &add_rmsnorm_op);
   m.impl("rope_cache", &rope_cache_op);
   m.impl("silu_mul", &silu_mul_op);

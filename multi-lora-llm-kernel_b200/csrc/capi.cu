@@ -651,6 +651,10 @@ int persona_sgmv_fused(const void* x, int64_t ldx, const void* a_pool, int64_t a
 
 // ------------------------------------------------------------------ NF4 ---
 namespace {
+int nf4_linear_impl(const persona_nf4_problem* problems, int num_problems, const float* const* addends,
+                    const int64_t* ld_addends, int64_t M, void* workspace, size_t workspace_bytes, int32_t* dev_err,
+                    cudaStream_t stream);
+
 struct Nf4Plan {
   persona::Nf4GemmArgs args;
   size_t counter_bytes;
@@ -757,6 +761,22 @@ size_t persona_nf4_linear_workspace_size(const persona_nf4_problem* problems, in
 
 int persona_nf4_linear(const persona_nf4_problem* problems, int num_problems, int64_t M, void* workspace,
                        size_t workspace_bytes, int32_t* dev_err, cudaStream_t stream) {
+  return nf4_linear_impl(problems, num_problems, nullptr, nullptr, M, workspace, workspace_bytes, dev_err, stream);
+}
+
+int persona_nf4_linear_add(const persona_nf4_problem* problems, int num_problems, const float* const* addends,
+                           const int64_t* ld_addends, int64_t M, void* workspace, size_t workspace_bytes,
+                           int32_t* dev_err, cudaStream_t stream) {
+  if (addends == nullptr || ld_addends == nullptr) return PERSONA_ERR_INVALID_ARG;
+  return nf4_linear_impl(problems, num_problems, addends, ld_addends, M, workspace, workspace_bytes, dev_err, stream);
+}
+
+}  // extern "C"
+
+namespace {
+int nf4_linear_impl(const persona_nf4_problem* problems, int num_problems, const float* const* addends,
+                    const int64_t* ld_addends, int64_t M, void* workspace, size_t workspace_bytes, int32_t* dev_err,
+                    cudaStream_t stream) {
   using namespace persona;
   Nf4Plan plan;
   int st = nf4_plan(problems, num_problems, &plan);
@@ -770,6 +790,10 @@ int persona_nf4_linear(const persona_nf4_problem* problems, int num_problems, in
     if (!aligned16(p.packed) || !aligned16(p.x) || p.ldx % 8 || (reinterpret_cast<uintptr_t>(p.y) & 1) ||
         (reinterpret_cast<uintptr_t>(p.offset) & 3))
       return PERSONA_ERR_ALIGNMENT;
+    if (addends != nullptr && addends[i] != nullptr) {
+      if (ld_addends[i] < p.N) return PERSONA_ERR_SHAPE;
+      if (reinterpret_cast<uintptr_t>(addends[i]) & 3) return PERSONA_ERR_ALIGNMENT;
+    }
   }
   if (M == 0) return PERSONA_OK;
   if (workspace == nullptr || workspace_bytes < plan.counter_bytes + plan.partial_bytes)
@@ -792,14 +816,18 @@ int persona_nf4_linear(const persona_nf4_problem* problems, int num_problems, in
       a.prob[i].offset = p.offset;
       a.prob[i].y = static_cast<uint16_t*>(p.y) + m0 * p.ldy;
       a.prob[i].ldy = p.ldy;
+      a.prob[i].addend = nullptr;
+      if (addends != nullptr && addends[i] != nullptr) {
+        a.prob[i].addend = addends[i] + m0 * ld_addends[i];
+        a.prob[i].ld_addend = ld_addends[i];
+      }
     }
     a.M = mc;
     if (launch_nf4_gemm(maps, a, m_pad, stream) != cudaSuccess) return PERSONA_ERR_CUDA;
   }
   return PERSONA_OK;
 }
-
-}  // extern "C"
+}  // namespace
 
 // ---------------------------------------------------- decode helpers ----
 extern "C" {
@@ -859,3 +887,47 @@ int persona_decode_attention(const void* q, const void* k_cache, const void* v_c
 }
 
 }  // extern "C"
+
+// ------------------------------------------------- LoRA delta at decode ---
+extern "C" int persona_bgmv_lora_delta_multi(const persona_bgmv_problem* problems, int num_problems,
+                                             float* const* deltas, const int64_t* ld_deltas, const int32_t* slots,
+                                             int64_t T, int64_t R, int64_t S, int dtype, int32_t* dev_err,
+                                             cudaStream_t stream) {
+  if (problems == nullptr || deltas == nullptr || ld_deltas == nullptr || num_problems < 1 ||
+      num_problems > PERSONA_MAX_PROBLEMS)
+    return PERSONA_ERR_INVALID_ARG;
+  if (dtype != PERSONA_DTYPE_F16 && dtype != PERSONA_DTYPE_BF16) return PERSONA_ERR_DTYPE;
+  if (T < 0 || S <= 0 || T > PERSONA_SMALL_MAX_ROWS) return PERSONA_ERR_SHAPE;
+  if (!rank_supported(R)) return PERSONA_ERR_RANK;
+  if (T > 0 && slots == nullptr) return PERSONA_ERR_INVALID_ARG;
+  SmallArgs a = {};
+  for (int i = 0; i < num_problems; ++i) {
+    const persona_bgmv_problem& q = problems[i];
+    int st = check_a(q.x, q.ldx, q.a_pool, q.a_slot_stride, q.a_row_stride, q.K, R, S);
+    if (st != PERSONA_OK) return st;
+    if ((st = check_b(q.b_pool, q.b_slot_stride, deltas[i], ld_deltas[i], q.N, R)) != PERSONA_OK) return st;
+    if (q.K < 64 || q.K > 32768) return PERSONA_ERR_SHAPE;
+    SmallProblem& p = a.prob[i];
+    p.x = q.x;
+    p.a = q.a_pool;
+    p.b = q.b_pool;
+    p.y = nullptr;
+    p.ldx = q.ldx;
+    p.a_slot_stride = q.a_slot_stride;
+    p.a_row_stride = q.a_row_stride;
+    p.b_slot_stride = q.b_slot_stride;
+    p.ldy = 0;
+    p.K = static_cast<int>(q.K);
+    p.N = static_cast<int>(q.N);
+    p.delta = deltas[i];
+    p.ld_delta = ld_deltas[i];
+  }
+  if (T == 0) return PERSONA_OK;
+  a.slots = slots;
+  a.err = dev_err;
+  a.num_problems = num_problems;
+  a.S = static_cast<int>(S);
+  return launch_bgmv_small(dtype, static_cast<int>(R), a, static_cast<int>(T), stream) == cudaSuccess
+             ? PERSONA_OK
+             : PERSONA_ERR_CUDA;
+}

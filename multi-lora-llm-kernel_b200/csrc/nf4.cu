@@ -224,14 +224,25 @@ __device__ __forceinline__ UnitPos unit_pos(const Nf4GemmArgs& a, int u) {
   return r;
 }
 
-__device__ __forceinline__ void store_y(uint16_t* y, int64_t ldy, int M, int n0, int m0, float v0, float v1,
-                                        float v2, float v3) {
-  // v0 / v1: rows m0 / m0 + 1 of column n0; v2 / v3: the same of column n0 + 8
+__device__ __forceinline__ void store_y(const Nf4Problem& pr, int M, int n0, int m0, float v0, float v1, float v2,
+                                        float v3) {
+  // v0 / v1: rows m0 / m0 + 1 of column n0; v2 / v3: the same of column n0 + 8.
+  // With an addend (the LoRA term) it joins before the one rounding.
+  uint16_t* y = pr.y;
+  const int64_t ldy = pr.ldy;
   if (m0 < M) {
+    if (pr.addend) {
+      v0 += pr.addend[static_cast<int64_t>(m0) * pr.ld_addend + n0];
+      v2 += pr.addend[static_cast<int64_t>(m0) * pr.ld_addend + n0 + 8];
+    }
     y[static_cast<int64_t>(m0) * ldy + n0] = __half_as_ushort(__float2half_rn(v0));
     y[static_cast<int64_t>(m0) * ldy + n0 + 8] = __half_as_ushort(__float2half_rn(v2));
   }
   if (m0 + 1 < M) {
+    if (pr.addend) {
+      v1 += pr.addend[static_cast<int64_t>(m0 + 1) * pr.ld_addend + n0];
+      v3 += pr.addend[static_cast<int64_t>(m0 + 1) * pr.ld_addend + n0 + 8];
+    }
     y[static_cast<int64_t>(m0 + 1) * ldy + n0] = __half_as_ushort(__float2half_rn(v1));
     y[static_cast<int64_t>(m0 + 1) * ldy + n0 + 8] = __half_as_ushort(__float2half_rn(v3));
   }
@@ -399,7 +410,7 @@ __global__ void __launch_bounds__(kNf4Threads, 1)
       if (pr.splits == 1) {
 #pragma unroll
         for (int mt = 0; mt < MT; ++mt)
-          store_y(pr.y, pr.ldy, args.M, n0, 8 * mt + 2 * t, acc[mt][0], acc[mt][1], acc[mt][2], acc[mt][3]);
+          store_y(pr, args.M, n0, 8 * mt + 2 * t, acc[mt][0], acc[mt][1], acc[mt][2], acc[mt][3]);
       } else {
         float* part = args.partials + static_cast<int64_t>(u) * kNf4Tile * MP;
 #pragma unroll
@@ -444,7 +455,7 @@ __global__ void __launch_bounds__(kNf4Threads, 1)
                 }
               }
             }
-            store_y(pr.y, pr.ldy, args.M, n0, 8 * mt + 2 * t, v[0], v[1], v[2], v[3]);
+            store_y(pr, args.M, n0, 8 * mt + 2 * t, v[0], v[1], v[2], v[3]);
           }
           named_sync(kNf4EpiBar, kNf4Warps * 32);
           if (tid == 0) *cnt = 0;  // every split has counted: ready for the next launch

@@ -17,6 +17,8 @@ struct Nf4Problem {
   const float* offset;  // device scalar written by the quantiser
   uint16_t* y;
   int64_t ldy;
+  const float* addend;  // non-null: y = fp16(x W^T + addend), fp32 [M, ld_addend]
+  int64_t ld_addend;
   int N, K;
   int splits;           // K splits per tile
   int chunks_per_split;

@@ -57,9 +57,11 @@ def dequantize(q: NF4Weight) -> torch.Tensor:
 
 
 def linear(x: torch.Tensor, weights: Sequence[NF4Weight], outs: Optional[Sequence[torch.Tensor]] = None,
-           dense_above: Optional[int] = None) -> List[torch.Tensor]:
-    """``y_i = x @ W_i^T`` for up to four weights that share x ([M, K] fp16,
-    unit inner stride); one launch at decode sizes."""
+           dense_above: Optional[int] = None,
+           addends: Optional[Sequence[torch.Tensor]] = None) -> List[torch.Tensor]:
+    """``y_i = x @ W_i^T`` (``+ addends[i]``, fp32 [M, N_i], before the one
+    rounding) for up to four weights that share x ([M, K] fp16, unit inner
+    stride); one launch at decode sizes."""
     ops._load()
     if x.dim() != 2:
         raise ValueError("nf4.linear: x must be [M, K]")
@@ -69,11 +71,18 @@ def linear(x: torch.Tensor, weights: Sequence[NF4Weight], outs: Optional[Sequenc
     if outs is None:
         outs = [torch.empty(M, w.N, dtype=torch.float16, device=x.device) for w in weights]
     if M > dense_above:
-        for w, y in zip(weights, outs):
-            torch.matmul(x, dequantize(w).t(), out=y)
+        for i, (w, y) in enumerate(zip(weights, outs)):
+            if addends is None:
+                torch.matmul(x, dequantize(w).t(), out=y)
+            else:
+                y.copy_(torch.matmul(x.float(), dequantize(w).float().t()) + addends[i])
         return list(outs)
     xc = x if x.stride(1) == 1 else x.contiguous()
-    torch.ops.persona.nf4_linear(xc, [w.packed for w in weights], [w.offset for w in weights], list(outs))
+    if addends is None:
+        torch.ops.persona.nf4_linear(xc, [w.packed for w in weights], [w.offset for w in weights], list(outs))
+    else:
+        torch.ops.persona.nf4_linear_add(xc, [w.packed for w in weights], [w.offset for w in weights],
+                                         list(addends), list(outs))
     return list(outs)
 
 

@@ -209,3 +209,12 @@ def decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tens
     _require_cuda("decode_attention", q, k_cache, v_cache, length, out)
     torch.ops.persona.decode_attention(q, k_cache, v_cache, length, out, float(scale))
     return out
+
+
+def bgmv_lora_delta_multi(xs, a_pools, b_pools, slots: torch.Tensor, deltas):
+    """``deltas[i][t] = B_i[s] @ (A_i[s] @ xs[i][t])`` in fp32 (0 for rows
+    without adapter), at most 64 rows: the LoRA term alone, for a base
+    projection that adds it (``nf4.linear(..., addends=...)``)."""
+    _require_cuda("bgmv_lora_delta_multi", slots, *xs, *a_pools, *b_pools, *deltas)
+    torch.ops.persona.bgmv_lora_delta_multi(list(xs), list(a_pools), list(b_pools), slots, list(deltas))
+    return deltas

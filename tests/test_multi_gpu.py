@@ -227,3 +227,30 @@ def test_decode_sized_fused_flags_out_of_range_slots():
     want = p["y"][ok].copy()
     O.bgmv_forward_ref(p["x"][ok], p["a"], p["b"], slots[ok], dtype, y=want)
     np.testing.assert_allclose(f32(got[ok], dtype), f32(want, dtype), **TOL)
+
+
+@pytest.mark.parametrize("dtype", ["f16", "bf16"])
+@pytest.mark.parametrize("T", [1, 8, 64])
+def test_lora_delta_matches_oracle(dtype, T):
+    """The LoRA term alone, fp32, at decode sizes: B[s] (A[s] x) per row, exact
+    zeros for rows without adapter."""
+    R, S = 16, 5
+    shapes = [(4096, 4096), (4096, 1024), (14336, 4096)]
+    slots, projs = layer_case(300 + T, T, R, S, dtype, names=shapes, null_frac=0.3)
+    sd = torch.from_numpy(slots).to(dev())
+    xs = [t16(p["x"], dtype) for p in projs]
+    a_s = [t16(p["a"], dtype) for p in projs]
+    b_s = [t16(p["b"], dtype) for p in projs]
+    ds = [torch.full((T, p["N"]), 7.0, dtype=torch.float32, device=dev()) for p in projs]
+    ops.bgmv_lora_delta_multi(xs, a_s, b_s, sd, ds)
+    ops.check_errors(dev())
+    for p, d in zip(projs, ds):
+        got = d.cpu().numpy()
+        v = O.bgmv_shrink_ref(p["x"], p["a"], slots, dtype).astype(np.float64)
+        b = f32(p["b"], dtype).astype(np.float64)
+        for t in range(T):
+            if slots[t] < 0:
+                assert np.all(got[t] == 0)
+            else:
+                want = b[slots[t]] @ v[t]
+                np.testing.assert_allclose(got[t], want, rtol=1e-3, atol=1e-3)

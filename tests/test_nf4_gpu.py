@@ -118,3 +118,19 @@ def test_c_abi_checks_arguments():
     assert lib.persona_nf4_linear(bad, 1, M, ws.data_ptr(), ws_bytes, err.data_ptr(), st) == 2
     assert lib.persona_nf4_packed_bytes(N, K) == (N // 128) * (K // 128) * 8464
     assert lib.persona_nf4_packed_bytes(100, K) == 0
+
+
+@pytest.mark.parametrize("M", [3, 8, 64])
+def test_linear_with_addend_matches_the_oracle(M):
+    """y = fp16(x W^T + addend): the addend joins before the one rounding,
+    on the split-K path (K 4096) and the unsplit one (K 256)."""
+    rng = np.random.default_rng(40 + M)
+    for N, K in ((1024, 4096), (384, 256)):
+        q = nf4.quantize(torch.from_numpy(_weights(M + K, N, K)).to(_dev()))
+        x = rng.standard_normal((M, K)).astype(np.float16)
+        add = rng.standard_normal((M, N)).astype(np.float32)
+        y = nf4.linear(torch.from_numpy(x).to(_dev()), [q], addends=[torch.from_numpy(add).to(_dev())])[0]
+        ops.check_errors(_dev())
+        w = Q.dequantize_f32(q.packed.cpu().numpy(), np.float32(q.offset.item()), N, K).astype(np.float64)
+        want = (x.astype(np.float64) @ w.T + add).astype(np.float16)
+        np.testing.assert_allclose(y.cpu().numpy().astype(np.float32), want.astype(np.float32), **TOL)
