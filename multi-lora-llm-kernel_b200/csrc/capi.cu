@@ -661,47 +661,38 @@ struct Nf4Plan {
   size_t partial_bytes;
 };
 
-// Splits so that the launch has about four units per SM, at least four
-// chunks (512 of K) per unit.
+// Every CTA of the launch gets an equal contiguous range of the problems'
+// chunks (tile-major, problem after problem).  A tile that one CTA covers
+// whole is written straight to y; a tile split between CTAs is summed from
+// their pieces, so the partial buffer holds two pieces (a CTA's first and
+// last tile) per CTA.
 int nf4_plan(const persona_nf4_problem* probs, int n, Nf4Plan* out) {
   using namespace persona;
   if (n < 1 || n > kNf4MaxProblems || probs == nullptr) return PERSONA_ERR_INVALID_ARG;
+  Nf4GemmArgs& a = out->args;
+  std::memset(&a, 0, sizeof(a));
+  a.num_problems = n;
   int64_t chunks = 0, tiles = 0;
   for (int i = 0; i < n; ++i) {
     const persona_nf4_problem& p = probs[i];
     if (p.N <= 0 || p.K <= 0 || p.N % kNf4Tile || p.K % kNf4Tile || p.N > (int64_t{1} << 24) ||
         p.K > (int64_t{1} << 24))
       return PERSONA_ERR_SHAPE;
+    Nf4Problem& q = a.prob[i];
+    q.N = static_cast<int>(p.N);
+    q.K = static_cast<int>(p.K);
+    q.chunk_base = chunks;
+    q.counter_base = static_cast<int>(tiles);
     chunks += (p.N / kNf4Tile) * (p.K / kNf4Tile);
     tiles += p.N / kNf4Tile;
   }
   int sms = nf4_sm_count();
   if (sms <= 0) sms = 148;
-  int64_t per = (chunks + 4 * sms - 1) / (4 * sms);
-  if (per < 4) per = 4;
-  Nf4GemmArgs& a = out->args;
-  std::memset(&a, 0, sizeof(a));
-  a.num_problems = n;
-  int64_t units = 0, ctr = 0;
-  for (int i = 0; i < n; ++i) {
-    const int kt = static_cast<int>(probs[i].K / kNf4Tile), nt = static_cast<int>(probs[i].N / kNf4Tile);
-    int splits = static_cast<int>((kt + per - 1) / per);
-    const int cps = (kt + splits - 1) / splits;
-    splits = (kt + cps - 1) / cps;
-    Nf4Problem& q = a.prob[i];
-    q.N = static_cast<int>(probs[i].N);
-    q.K = static_cast<int>(probs[i].K);
-    q.splits = splits;
-    q.chunks_per_split = cps;
-    q.unit_base = static_cast<int>(units);
-    q.counter_base = static_cast<int>(ctr);
-    units += static_cast<int64_t>(nt) * splits;
-    ctr += nt;
-  }
-  if (units > kI32Max) return PERSONA_ERR_SHAPE;
-  a.units = static_cast<int>(units);
+  const int64_t cap = static_cast<int64_t>(kNf4MaxCtasPerSm) * sms;
+  a.chunks = chunks;
+  a.max_ctas = static_cast<int>(chunks < cap ? chunks : cap);
   out->counter_bytes = (static_cast<size_t>(tiles) * 4 + 255) & ~size_t(255);
-  out->partial_bytes = static_cast<size_t>(units) * kNf4Tile * kNf4MaxRows * 4;
+  out->partial_bytes = static_cast<size_t>(a.max_ctas) * 2 * kNf4Tile * kNf4MaxRows * 4;
   return PERSONA_OK;
 }
 }  // namespace

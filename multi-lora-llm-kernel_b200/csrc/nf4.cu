@@ -13,7 +13,8 @@
 // word of codes is exactly one thread's A fragment for one k-step: four
 // bytes, each mapped by a 256-entry table to the two fp16 NF4 values it
 // holds.  The table sits in shared memory once per lane (entry b of lane l at
-// word 32 b + l), so every lookup is free of bank conflicts.  The fragments
+// byte 256 b + 4 l), so every lookup is free of bank conflicts and its offset
+// is one byte permute of the code word and 4 l.  The fragments
 // never go through shared memory, and the per-block scale is applied to the
 // fp32 partial sum of each 64-wide block (two per 128-wide chunk), not to
 // every weight.  x (M rows, fp16) is the B operand, TMA-loaded per chunk
@@ -22,13 +23,16 @@
 // warp-level MMA delivers; staging dequantised tiles in shared memory for
 // tcgen05 would instead cost 4 bytes of shared-memory traffic per weight.
 //
-// Work units: (problem, tile of 128 output rows, split of the K chunks).
-// One CTA per SM, persistent over units (static round robin): a producer
-// warp bulk-copies each 8464-byte chunk and TMA-loads the x chunk into a
-// 6-slot ring; eight compute warps each own 16 rows of the tile.  A split
-// unit writes its fp32 partial tile to the workspace; the last unit of a
-// tile (per-tile counter) sums the partials in split order, so the result
-// does not depend on scheduling, writes y and resets the counter.
+// Work: the launch's chunks (problem, tile of 128 output rows, 128-wide K
+// chunk) in one linear order, cut into equal contiguous ranges, one per CTA
+// (two CTAs per SM at 8 rows, one above), so every SM streams the same
+// number of bytes.  A producer warp bulk-copies each 8464-byte chunk and
+// TMA-loads the x chunk into a ring of 4 (8 rows) or 6 slots; eight compute
+// warps each own 16 rows of the tile.  A tile inside one range is written
+// straight to y.  A tile cut between ranges leaves one fp32 piece per CTA
+// (a CTA's first and last tile may be such pieces); the last piece to finish
+// (per-tile counter) sums them in CTA order, so the result does not depend
+// on scheduling, writes y and resets the counter.
 #include <cuda_fp16.h>
 
 #include "common.cuh"
@@ -40,21 +44,33 @@ namespace {
 
 constexpr int kNf4Warps = 8;
 constexpr int kNf4Threads = (kNf4Warps + 1) * 32;
-constexpr int kNf4Slots = 6;
-constexpr int kNf4RawPad = 9216;  // chunk area of a slot, padded to 1 KB
-constexpr int kNf4LutBytes = 256 * 32 * 4;
+constexpr int kNf4MaxSlots = 6;
 
-// A slot holds one chunk and the two x boxes (8 MT rows each); at MT = 1 two
-// CTAs fit on an SM, which doubles the warps that hide the load and MMA
-// latencies.
+// Dynamic shared memory: the lookup table at offset 0, then the slots' x
+// boxes (two per slot, 8 MT rows each, 1 KB aligned for the 128-byte
+// swizzle), then the slots' chunks (16-byte aligned, packed).
+//
+// The table holds entry b of lane l at byte kLutRow b + 4 l.  At MT = 1 a row
+// is 256 bytes (the upper 128 unused): one byte permute of the code word and
+// the lane's 4 l is then the whole offset of a lookup, which matters because
+// there the lookups are most of the instructions.  Above, every lookup feeds
+// MT MMAs and the rows are 128 bytes (a permute and a shift-add), which
+// leaves more of the SM's shared memory to L1.
+//
+// At MT = 1 four slots keep two CTAs on an SM, which doubles the warps that
+// hide the load and MMA latencies; at MT >= 2 one CTA fits and gets six.
 template <int MT>
 struct Nf4Cfg {
-  static constexpr int kSlotBytes = kNf4RawPad + 2 * 8 * MT * 128;
-  static constexpr int kSmem = kNf4Slots * kSlotBytes + kNf4LutBytes + 1024;
-  static_assert(kSlotBytes % 1024 == 0, "slot alignment");
+  static constexpr int kLutRow = MT == 1 ? 256 : 128;
+  static constexpr int kLutBytes = 256 * kLutRow;
+  static constexpr int kSlots = MT == 1 ? 4 : kNf4MaxSlots;
+  static constexpr int kXBytes = 2 * 8 * MT * 128;
+  static constexpr int kSmem = kLutBytes + 1024 + kSlots * (kXBytes + kNf4ChunkBytes);
+  static_assert(kXBytes % 1024 == 0, "x box alignment");
+  static_assert(kSlots <= kNf4MaxSlots, "slot count");
 };
 constexpr int kNf4EpiBar = 1;
-static_assert(kNf4ChunkBytes % 16 == 0 && kNf4RawPad >= kNf4ChunkBytes, "chunk layout");
+static_assert(kNf4ChunkBytes % 16 == 0, "chunk layout");
 
 __device__ __forceinline__ float h2f(uint32_t bits) { return __half2float(__ushort_as_half(static_cast<uint16_t>(bits))); }
 
@@ -204,23 +220,36 @@ __global__ void __launch_bounds__(256) nf4_dequant_kernel(const uint8_t* __restr
 }
 
 // ------------------------------------------------------------------ GEMM ----
-struct UnitPos {
-  int p, tile, split, kc0, kc1;
+// The launch's chunks in one linear order (problem, tile, K chunk); CTA g
+// owns [range_start(g), range_start(g + 1)).
+__device__ __forceinline__ int64_t range_start(int64_t chunks, int ctas, int g) {
+  return static_cast<int64_t>(g) * chunks / ctas;
+}
+
+// The CTA whose range holds chunk c.
+__device__ __forceinline__ int range_cta(int64_t chunks, int ctas, int64_t c) {
+  return static_cast<int>(((c + 1) * ctas - 1) / chunks);
+}
+
+// A run of chunks of one tile inside a CTA's range: K chunks [kc0, kc1).
+struct Nf4Seg {
+  int p, tile, kt, kc0, kc1;
 };
 
-__device__ __forceinline__ UnitPos unit_pos(const Nf4GemmArgs& a, int u) {
+__device__ __forceinline__ Nf4Seg seg_at(const Nf4GemmArgs& a, int64_t c, int64_t c_end) {
   int p = 0;
 #pragma unroll
   for (int i = 1; i < kNf4MaxProblems; ++i)
-    if (i < a.num_problems && u >= a.prob[i].unit_base) p = i;
+    if (i < a.num_problems && c >= a.prob[i].chunk_base) p = i;
   const Nf4Problem& pr = a.prob[p];
-  const int lu = u - pr.unit_base;
-  UnitPos r;
+  Nf4Seg r;
   r.p = p;
-  r.tile = lu / pr.splits;
-  r.split = lu - r.tile * pr.splits;
-  r.kc0 = r.split * pr.chunks_per_split;
-  r.kc1 = min(pr.K / kNf4Tile, r.kc0 + pr.chunks_per_split);
+  r.kt = pr.K / kNf4Tile;
+  const int64_t lc = c - pr.chunk_base;
+  r.tile = static_cast<int>(lc / r.kt);
+  r.kc0 = static_cast<int>(lc - static_cast<int64_t>(r.tile) * r.kt);
+  const int64_t left = c_end - c;
+  r.kc1 = left < r.kt - r.kc0 ? r.kc0 + static_cast<int>(left) : r.kt;
   return r;
 }
 
@@ -249,24 +278,31 @@ __device__ __forceinline__ void store_y(const Nf4Problem& pr, int M, int n0, int
 }
 
 template <int MT>
-__global__ void __launch_bounds__(kNf4Threads, 1)
+__global__ void __launch_bounds__(kNf4Threads, MT == 1 ? 2 : 1)
     nf4_gemm_kernel(const __grid_constant__ Nf4Maps maps, const Nf4GemmArgs args) {
   constexpr int MP = 8 * MT;  // rows of x per TMA box (zero past M)
-  constexpr int kSlotBytes = Nf4Cfg<MT>::kSlotBytes;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* ring = base;
-  uint32_t* lut = reinterpret_cast<uint32_t*>(base + kNf4Slots * kSlotBytes);
-  __shared__ uint64_t full[kNf4Slots], empty[kNf4Slots];
+  constexpr int kSlots = Nf4Cfg<MT>::kSlots;
+  constexpr int kXBytes = Nf4Cfg<MT>::kXBytes;
+  constexpr int kLutRow = Nf4Cfg<MT>::kLutRow;
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  // the table first: its shared address is a constant of the kernel
+  uint32_t* lut = reinterpret_cast<uint32_t*>(smem_raw);
+  uint8_t* xring = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw + Nf4Cfg<MT>::kLutBytes) + 1023) & ~uintptr_t(1023));
+  uint8_t* cring = xring + kSlots * kXBytes;
+  __shared__ uint64_t full[kNf4MaxSlots], empty[kNf4MaxSlots];
   __shared__ uint32_t lut1[256];
   __shared__ int s_fin;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int64_t C = args.chunks;
+  const int G = static_cast<int>(gridDim.x);
+  const int64_t c_begin = range_start(C, G, blockIdx.x), c_end = range_start(C, G, blockIdx.x + 1);
   // the LoRA kernel after this one may start prefetching its weights
   asm volatile("griddepcontrol.launch_dependents;");
 
   if (tid < 256) lut1[tid] = nf4_half_bits(tid >> 4) | (nf4_half_bits(tid & 15) << 16);
   if (tid == 0) {
-    for (int s = 0; s < kNf4Slots; ++s) {
+    for (int s = 0; s < kSlots; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], kNf4Warps);
     }
@@ -276,7 +312,7 @@ __global__ void __launch_bounds__(kNf4Threads, 1)
   // the compute warps spread the table to one copy per lane while the
   // producer already streams the first chunks
   if (warp < kNf4Warps) {
-    for (int i = tid; i < 256 * 32; i += kNf4Warps * 32) lut[i] = lut1[i >> 5];
+    for (int i = tid; i < 256 * 32; i += kNf4Warps * 32) lut[(i >> 5) * (kLutRow / 4) + (i & 31)] = lut1[i >> 5];
     named_sync(kNf4EpiBar, kNf4Warps * 32);
   }
 
@@ -285,70 +321,74 @@ __global__ void __launch_bounds__(kNf4Threads, 1)
     if (lane == 0) {
       for (int p = 0; p < args.num_problems; ++p) tma_prefetch_desc(&maps.x[p]);
       // Launched as a programmatic dependent of the kernel that writes x:
-      // the weight chunks of the first kNf4Slots fills do not depend on it
+      // the weight chunks of the first kSlots fills do not depend on it
       // and are requested at once; their x boxes wait for that kernel.
-      int pend_kc[kNf4Slots], pend_p[kNf4Slots], n_pend = 0;
+      int pend_kc[kSlots], pend_p[kSlots], n_pend = 0;
       bool waited = false;
       auto flush = [&]() {
         asm volatile("griddepcontrol.wait;" ::: "memory");
         for (int i = 0; i < n_pend; ++i) {
-          uint8_t* st = ring + i * kSlotBytes;
-          tc::tma_load_2d(st + kNf4RawPad, &maps.x[pend_p[i]], &full[i], pend_kc[i] * kNf4Tile, 0);
-          tc::tma_load_2d(st + kNf4RawPad + MP * 128, &maps.x[pend_p[i]], &full[i], pend_kc[i] * kNf4Tile + 64, 0);
+          uint8_t* xs = xring + i * kXBytes;
+          tc::tma_load_2d(xs, &maps.x[pend_p[i]], &full[i], pend_kc[i] * kNf4Tile, 0);
+          tc::tma_load_2d(xs + MP * 128, &maps.x[pend_p[i]], &full[i], pend_kc[i] * kNf4Tile + 64, 0);
         }
         waited = true;
       };
       uint32_t g = 0;
       bool ok = true;
-      for (int u = blockIdx.x; ok && u < args.units; u += gridDim.x) {
-        const UnitPos up = unit_pos(args, u);
-        const Nf4Problem& pr = args.prob[up.p];
-        const int kt = pr.K / kNf4Tile;
-        for (int kc = up.kc0; kc < up.kc1; ++kc, ++g) {
-          const int s = static_cast<int>(g % kNf4Slots);
-          if (g >= static_cast<uint32_t>(kNf4Slots)) {
+      for (int64_t c = c_begin; ok && c < c_end;) {
+        const Nf4Seg sg = seg_at(args, c, c_end);
+        c += sg.kc1 - sg.kc0;
+        const Nf4Problem& pr = args.prob[sg.p];
+        for (int kc = sg.kc0; kc < sg.kc1; ++kc, ++g) {
+          const int s = static_cast<int>(g % kSlots);
+          if (g >= static_cast<uint32_t>(kSlots)) {
             if (!waited) flush();
-            if (!mbar_wait(&empty[s], ((g / kNf4Slots) - 1) & 1, args.err)) {
+            if (!mbar_wait(&empty[s], ((g / kSlots) - 1) & 1, args.err)) {
               ok = false;
               break;
             }
           }
-          uint8_t* st = ring + s * kSlotBytes;
+          uint8_t* xs = xring + s * kXBytes;
           mbar_arrive_expect_tx(&full[s], kNf4ChunkBytes + 2 * MP * 128);
-          bulk_load(st, pr.w + (static_cast<int64_t>(up.tile) * kt + kc) * kNf4ChunkBytes, kNf4ChunkBytes,
+          bulk_load(cring + s * kNf4ChunkBytes,
+                    pr.w + (static_cast<int64_t>(sg.tile) * sg.kt + kc) * kNf4ChunkBytes, kNf4ChunkBytes,
                     &full[s]);
           if (waited) {
-            tc::tma_load_2d(st + kNf4RawPad, &maps.x[up.p], &full[s], kc * kNf4Tile, 0);
-            tc::tma_load_2d(st + kNf4RawPad + MP * 128, &maps.x[up.p], &full[s], kc * kNf4Tile + 64, 0);
+            tc::tma_load_2d(xs, &maps.x[sg.p], &full[s], kc * kNf4Tile, 0);
+            tc::tma_load_2d(xs + MP * 128, &maps.x[sg.p], &full[s], kc * kNf4Tile + 64, 0);
           } else {
             pend_kc[n_pend] = kc;
-            pend_p[n_pend] = up.p;
+            pend_p[n_pend] = sg.p;
             ++n_pend;
           }
         }
       }
       if (!waited) flush();
       // every copy this thread issued lands before the CTA exits
-      for (int s = 0; s < kNf4Slots; ++s)
-        if (g > static_cast<uint32_t>(s)) mbar_wait(&full[s], ((g - 1 - s) / kNf4Slots) & 1, args.err);
+      for (int s = 0; s < kSlots; ++s)
+        if (g > static_cast<uint32_t>(s)) mbar_wait(&full[s], ((g - 1 - s) / kSlots) & 1, args.err);
     }
     __syncwarp();
   } else {
     // ---------------------------------------------------------- compute ----
     const int g8 = lane >> 2, t = lane & 3;
-    const uint32_t lut_lane = smem_u32(lut) + lane * 4;
+    const uint32_t lut_base = smem_u32(lut);
+    const uint32_t lane4 = static_cast<uint32_t>(lane) * 4;  // bytes (4 lane, 0, 0, 0)
     uint32_t g = 0;
-    for (int u = blockIdx.x; u < args.units; u += gridDim.x) {
-      const UnitPos up = unit_pos(args, u);
-      const Nf4Problem& pr = args.prob[up.p];
+    for (int64_t c = c_begin; c < c_end;) {
+      const Nf4Seg sg = seg_at(args, c, c_end);
+      const bool first_piece = c == c_begin;
+      c += sg.kc1 - sg.kc0;
+      const Nf4Problem& pr = args.prob[sg.p];
       const float off = *pr.offset;
       float acc[MT][4];
 #pragma unroll
       for (int mt = 0; mt < MT; ++mt) acc[mt][0] = acc[mt][1] = acc[mt][2] = acc[mt][3] = 0.f;
-      for (int kc = up.kc0; kc < up.kc1; ++kc, ++g) {
-        const int s = static_cast<int>(g % kNf4Slots);
-        mbar_wait(&full[s], (g / kNf4Slots) & 1, args.err);
-        const uint32_t st = smem_u32(ring + s * kSlotBytes);
+      for (int kc = sg.kc0; kc < sg.kc1; ++kc, ++g) {
+        const int s = static_cast<int>(g % kSlots);
+        mbar_wait(&full[s], (g / kSlots) & 1, args.err);
+        const uint32_t st = smem_u32(cring + s * kNf4ChunkBytes);
         const uint4 c0 = lds128(st + ((warp * 2 + 0) * 32 + lane) * 16);
         const uint4 c1 = lds128(st + ((warp * 2 + 1) * 32 + lane) * 16);
         const float s127 = __uint_as_float(lds32(st + kNf4S127Off));
@@ -366,7 +406,7 @@ __global__ void __launch_bounds__(kNf4Threads, 1)
         for (int kh = 0; kh < 2; ++kh) {
           const uint4 cw = kh ? c1 : c0;
           const uint32_t words[4] = {cw.x, cw.y, cw.z, cw.w};
-          const uint32_t xb = st + kNf4RawPad + kh * MP * 128;
+          const uint32_t xb = smem_u32(xring + s * kXBytes) + kh * MP * 128;
           float part[MT][4];
 #pragma unroll
           for (int mt = 0; mt < MT; ++mt) part[mt][0] = part[mt][1] = part[mt][2] = part[mt][3] = 0.f;
@@ -377,15 +417,19 @@ __global__ void __launch_bounds__(kNf4Threads, 1)
           for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
-              const int row = 8 * mt + (lane & 7), c = 4 * h + (lane >> 3);
-              ldsm_x4(xb + row * 128 + ((c ^ (row & 7)) << 4), bf[mt][h]);
+              const int row = 8 * mt + (lane & 7), cc = 4 * h + (lane >> 3);
+              ldsm_x4(xb + row * 128 + ((cc ^ (row & 7)) << 4), bf[mt][h]);
             }
 #pragma unroll
           for (int ks = 0; ks < 4; ++ks) {
             uint32_t a[4];
 #pragma unroll
-            for (int j = 0; j < 4; ++j)  // byte j alone (one byte permute), then one shift-add
-              a[j] = lds32(lut_lane + (__byte_perm(words[ks], 0u, 0x4440u + j) << 7));
+            for (int j = 0; j < 4; ++j) {
+              if constexpr (kLutRow == 256)  // offset (byte j) * 256 + 4 lane in one byte permute
+                a[j] = lds32(lut_base + __byte_perm(words[ks], lane4, 0x5504u + (j << 4)));
+              else  // byte j alone (one byte permute), then one shift-add
+                a[j] = lds32(lut_base + lane4 + (__byte_perm(words[ks], 0u, 0x4440u + j) << 7));
+            }
 #pragma unroll
             for (int mt = 0; mt < MT; ++mt) {
               const uint32_t b[2] = {bf[mt][ks >> 1][(ks & 1) * 2], bf[mt][ks >> 1][(ks & 1) * 2 + 1]};
@@ -406,48 +450,57 @@ __global__ void __launch_bounds__(kNf4Threads, 1)
       // D fragment: rows n0 = tile*128 + 16 warp + g8 (acc 0, 1) and n0 + 8
       // (acc 2, 3); x rows 8 mt + 2t and + 1.
       const int nl = 16 * warp + g8;
-      const int n0 = up.tile * kNf4Tile + nl;
-      if (pr.splits == 1) {
+      const int n0 = sg.tile * kNf4Tile + nl;
+      if (sg.kc0 == 0 && sg.kc1 == sg.kt) {
+        // the whole tile in this CTA's range
 #pragma unroll
         for (int mt = 0; mt < MT; ++mt)
           store_y(pr, args.M, n0, 8 * mt + 2 * t, acc[mt][0], acc[mt][1], acc[mt][2], acc[mt][3]);
       } else {
-        float* part = args.partials + static_cast<int64_t>(u) * kNf4Tile * MP;
+        // A piece of a tile shared with the neighbouring CTAs: the first
+        // piece of this CTA's range goes to its slot 0, the last to slot 1.
+        float* part = args.partials + (static_cast<int64_t>(blockIdx.x) * 2 + (first_piece ? 0 : 1)) * kNf4Tile * MP;
 #pragma unroll
         for (int mt = 0; mt < MT; ++mt) {
           *reinterpret_cast<float2*>(part + nl * MP + 8 * mt + 2 * t) = make_float2(acc[mt][0], acc[mt][1]);
           *reinterpret_cast<float2*>(part + (nl + 8) * MP + 8 * mt + 2 * t) = make_float2(acc[mt][2], acc[mt][3]);
         }
+        // the tile's pieces come from CTAs g0 .. g1, in that order
+        const int64_t t0 = pr.chunk_base + static_cast<int64_t>(sg.tile) * sg.kt;
+        const int g0 = range_cta(C, G, t0), g1 = range_cta(C, G, t0 + sg.kt - 1);
         // one cumulative fence after the barrier orders every warp's
         // partial stores before the count
         named_sync(kNf4EpiBar, kNf4Warps * 32);
-        int* cnt = args.counters + pr.counter_base + up.tile;
+        int* cnt = args.counters + pr.counter_base + sg.tile;
         if (tid == 0) {
           __threadfence();
           const int old = atomicAdd(cnt, 1);
-          s_fin = old == pr.splits - 1;
+          s_fin = old == g1 - g0;
           if (s_fin) __threadfence();
         }
         named_sync(kNf4EpiBar, kNf4Warps * 32);
         if (s_fin) {
-          const float* p0 = args.partials + static_cast<int64_t>(pr.unit_base + up.tile * pr.splits) * kNf4Tile * MP;
 #pragma unroll
           for (int mt = 0; mt < MT; ++mt) {
             float v[4] = {0.f, 0.f, 0.f, 0.f};
-            // four splits' loads in flight at a time, summed in split order
-            for (int sp0 = 0; sp0 < pr.splits; sp0 += 4) {
+            // four pieces' loads in flight at a time, summed in CTA order
+            for (int q0 = g0; q0 <= g1; q0 += 4) {
               float2 a[4], b[4];
 #pragma unroll
               for (int q = 0; q < 4; ++q) {
-                if (sp0 + q < pr.splits) {
-                  const float* src = p0 + static_cast<int64_t>(sp0 + q) * kNf4Tile * MP;
+                if (q0 + q <= g1) {
+                  const int gq = q0 + q;
+                  // a range that starts inside the tile holds it as its
+                  // first piece, one that starts before it as its last
+                  const int slot = range_start(C, G, gq) >= t0 ? 0 : 1;
+                  const float* src = args.partials + (static_cast<int64_t>(gq) * 2 + slot) * kNf4Tile * MP;
                   a[q] = __ldcg(reinterpret_cast<const float2*>(src + nl * MP + 8 * mt + 2 * t));
                   b[q] = __ldcg(reinterpret_cast<const float2*>(src + (nl + 8) * MP + 8 * mt + 2 * t));
                 }
               }
 #pragma unroll
               for (int q = 0; q < 4; ++q) {
-                if (sp0 + q < pr.splits) {
+                if (q0 + q <= g1) {
                   v[0] += a[q].x;
                   v[1] += a[q].y;
                   v[2] += b[q].x;
@@ -458,7 +511,7 @@ __global__ void __launch_bounds__(kNf4Threads, 1)
             store_y(pr, args.M, n0, 8 * mt + 2 * t, v[0], v[1], v[2], v[3]);
           }
           named_sync(kNf4EpiBar, kNf4Warps * 32);
-          if (tid == 0) *cnt = 0;  // every split has counted: ready for the next launch
+          if (tid == 0) *cnt = 0;  // every piece has counted: ready for the next launch
         }
       }
     }
@@ -518,7 +571,8 @@ static cudaError_t gemm_launch(const Nf4Maps& maps, const Nf4GemmArgs& args, cud
     per_sm[dev] = occ > 0 ? occ : 1;
   }
   const int ctas = per_sm[dev] * nf4_sm_count();
-  int grid = ctas < args.units ? ctas : args.units;
+  // never more CTAs than chunks, nor than the partial buffer was sized for
+  int grid = ctas < args.max_ctas ? ctas : args.max_ctas;
   if (grid < 1) grid = 1;
   // programmatic dependent launch: the weight streaming of this kernel may
   // start while the kernel before it on the stream finishes

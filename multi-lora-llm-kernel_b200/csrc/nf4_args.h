@@ -9,9 +9,12 @@
 #include "nf4_table.h"
 
 namespace persona {
+// CTAs of the NF4 GEMM per SM, at most (the partial buffer is sized for it).
+constexpr int kNf4MaxCtasPerSm = 2;
 
 // One base linear of a launch: y[M, N] = x[M, K] W^T, W in the tiled NF4
-// format.  Its units are (tile of 128 output rows, split of the K chunks).
+// format.  Its chunks (tile of 128 output rows, 128-wide K chunk) follow
+// those of the problems before it in one linear order, tile-major.
 struct Nf4Problem {
   const uint8_t* w;
   const float* offset;  // device scalar written by the quantiser
@@ -19,20 +22,19 @@ struct Nf4Problem {
   int64_t ldy;
   const float* addend;  // non-null: y = fp16(x W^T + addend), fp32 [M, ld_addend]
   int64_t ld_addend;
+  int64_t chunk_base;  // first chunk of this problem in the launch's order
   int N, K;
-  int splits;           // K splits per tile
-  int chunks_per_split;
-  int unit_base;        // first unit of this problem
   int counter_base;     // first tile counter of this problem
 };
 
 struct Nf4GemmArgs {
   Nf4Problem prob[kNf4MaxProblems];
+  int64_t chunks;    // all problems' chunks
   int num_problems;
-  int units;
+  int max_ctas;      // grid bound that the partial buffer is sized for
   int M;
-  float* partials;   // [units][128][M_pad] fp32 (split problems only)
-  int* counters;     // per tile, zero between launches (the finishing unit resets it)
+  float* partials;   // [CTA][2][128][M_pad] fp32: a CTA's first and last tile pieces
+  int* counters;     // per tile, zero between launches (the finishing piece resets it)
   int32_t* err;
 };
 
