@@ -17,11 +17,39 @@ namespace {
 
 __device__ __forceinline__ float h2f(__half h) { return __half2float(h); }
 
+// Every kernel here is launched as a programmatic dependent of the kernel
+// before it (the LoRA kernel, the attention or the norm), so that it is
+// resident when that kernel ends.  Each one waits here, before its first read
+// or write, until the kernel before it has finished and its writes are
+// visible (no CTA returns before this point, so the grid never completes
+// ahead of that kernel), and only then lets its own dependent launch: a
+// dependent launched earlier would hold SMs while two kernels still run.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// cudaLaunchKernelEx with programmatic stream serialization allowed.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+  if (e != cudaSuccess) return e;
+  return cudaGetLastError();
+}
+
 // h[r] += delta[r] (fp16, when delta is given); out[r] = w * fp16(h / rms).
 // One CTA of 256 threads per row, D a multiple of 8.
 __global__ void __launch_bounds__(256) add_rmsnorm_kernel(__half* __restrict__ h, const __half* __restrict__ delta,
                                                           const __half* __restrict__ w, __half* __restrict__ out,
                                                           int D, float eps) {
+  pdl_wait();
   asm volatile("griddepcontrol.launch_dependents;");  // a dependent NF4 GEMM may start streaming weights
   const int r = blockIdx.x;
   __half* hr = h + static_cast<int64_t>(r) * D;
@@ -72,6 +100,8 @@ __global__ void rope_cache_kernel(__half* __restrict__ q, __half* __restrict__ k
                                   __half* __restrict__ kc, __half* __restrict__ vc, const int* __restrict__ start,
                                   int per_seq, int Hq, int Hkv, int L, float log2_theta) {
   constexpr int D = 128;
+  pdl_wait();
+  asm volatile("griddepcontrol.launch_dependents;");
   const int r = blockIdx.x;
   const int b = r / per_seq, pos = *start + (r - b * per_seq);
   if (pos >= L) return;
@@ -103,6 +133,7 @@ __global__ void rope_cache_kernel(__half* __restrict__ q, __half* __restrict__ k
 // out = fp16(fp16(silu(g)) * u), n a multiple of 8.
 __global__ void silu_mul_kernel(const __half* __restrict__ g, const __half* __restrict__ u, __half* __restrict__ out,
                                 int64_t n) {
+  pdl_wait();
   asm volatile("griddepcontrol.launch_dependents;");
   for (int64_t i = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) * 8; i < n;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x * 8) {
@@ -137,6 +168,7 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attention_kernel(
     const __half* __restrict__ q, const __half* __restrict__ kc, const __half* __restrict__ vc,
     const int* __restrict__ len_ptr, __half* __restrict__ out, int Hq, int Hkv, int L, float scale) {
   constexpr int D = 128;
+  pdl_wait();
   asm volatile("griddepcontrol.launch_dependents;");
   const int b = blockIdx.x, kh = blockIdx.y, tid = threadIdx.x;
   const int G = Hq / Hkv;
@@ -245,26 +277,24 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attention_kernel(
 
 cudaError_t launch_add_rmsnorm(void* h, const void* delta, const void* w, void* out, int rows, int D, float eps,
                                cudaStream_t st) {
-  add_rmsnorm_kernel<<<rows, 256, 0, st>>>(static_cast<__half*>(h), static_cast<const __half*>(delta),
-                                           static_cast<const __half*>(w), static_cast<__half*>(out), D, eps);
-  return cudaGetLastError();
+  return launch_pdl(add_rmsnorm_kernel, dim3(rows), dim3(256), 0, st, static_cast<__half*>(h),
+                    static_cast<const __half*>(delta), static_cast<const __half*>(w), static_cast<__half*>(out), D,
+                    eps);
 }
 
 cudaError_t launch_rope_cache(void* q, void* k, const void* v, void* kc, void* vc, const int* start, int rows,
                               int per_seq, int Hq, int Hkv, int L, float log2_theta, cudaStream_t st) {
-  rope_cache_kernel<<<rows, 256, 0, st>>>(static_cast<__half*>(q), static_cast<__half*>(k),
-                                          static_cast<const __half*>(v), static_cast<__half*>(kc),
-                                          static_cast<__half*>(vc), start, per_seq, Hq, Hkv, L, log2_theta);
-  return cudaGetLastError();
+  return launch_pdl(rope_cache_kernel, dim3(rows), dim3(256), 0, st, static_cast<__half*>(q),
+                    static_cast<__half*>(k), static_cast<const __half*>(v), static_cast<__half*>(kc),
+                    static_cast<__half*>(vc), start, per_seq, Hq, Hkv, L, log2_theta);
 }
 
 cudaError_t launch_silu_mul(const void* g, const void* u, void* out, int64_t n, cudaStream_t st) {
   int64_t blocks = (n / 8 + 255) / 256;
   if (blocks > 148 * 8) blocks = 148 * 8;
   if (blocks < 1) blocks = 1;
-  silu_mul_kernel<<<static_cast<int>(blocks), 256, 0, st>>>(static_cast<const __half*>(g),
-                                                            static_cast<const __half*>(u), static_cast<__half*>(out), n);
-  return cudaGetLastError();
+  return launch_pdl(silu_mul_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, st,
+                    static_cast<const __half*>(g), static_cast<const __half*>(u), static_cast<__half*>(out), n);
 }
 
 cudaError_t launch_decode_attention(const void* q, const void* kc, const void* vc, const int* len, void* out, int B,
@@ -277,10 +307,9 @@ cudaError_t launch_decode_attention(const void* q, const void* kc, const void* v
         cudaFuncSetAttribute(decode_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return e;
   }
-  decode_attention_kernel<<<dim3(B, Hkv), kAttnThreads, smem, st>>>(
-      static_cast<const __half*>(q), static_cast<const __half*>(kc), static_cast<const __half*>(vc), len,
-      static_cast<__half*>(out), Hq, Hkv, L, scale);
-  return cudaGetLastError();
+  return launch_pdl(decode_attention_kernel, dim3(B, Hkv), dim3(kAttnThreads), smem, st,
+                    static_cast<const __half*>(q), static_cast<const __half*>(kc), static_cast<const __half*>(vc),
+                    len, static_cast<__half*>(out), Hq, Hkv, L, scale);
 }
 
 }  // namespace persona
