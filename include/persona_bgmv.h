@@ -272,7 +272,9 @@ typedef struct persona_nf4_problem {
   int64_t K;
 } persona_nf4_problem;
 /* Workspace of persona_nf4_linear: zero-filled before its first use (calls
- * leave its counters at zero again); one launch at a time per workspace.    */
+ * leave its counters at zero again); one launch at a time per workspace.
+ * Its size depends on the current device's SM count (two fp32 tile pieces
+ * per CTA); a call that finds it too small returns PERSONA_ERR_WORKSPACE.   */
 size_t persona_nf4_linear_workspace_size(const persona_nf4_problem* problems, int num_problems);
 /* Up to PERSONA_NF4_MAX_PROBLEMS linears in one launch (e.g. q / k / v on the
  * same x); any M (launches of at most 64 rows each).                        */
