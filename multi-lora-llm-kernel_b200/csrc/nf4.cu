@@ -32,7 +32,9 @@
 // straight to y.  A tile cut between ranges leaves one fp32 piece per CTA
 // (a CTA's first and last tile may be such pieces); the last piece to finish
 // (per-tile counter) sums them in CTA order, so the result does not depend
-// on scheduling, writes y and resets the counter.
+// on scheduling, writes y and resets the counter.  A first piece followed by
+// more of the range is counted by an epilogue warp, so the compute warps do
+// not wait for the count.
 #include <cuda_fp16.h>
 
 #include "common.cuh"
@@ -42,8 +44,10 @@
 namespace persona {
 namespace {
 
-constexpr int kNf4Warps = 8;
-constexpr int kNf4Threads = (kNf4Warps + 1) * 32;
+constexpr int kNf4Warps = 8;                      // compute warps
+constexpr int kNf4ProducerWarp = kNf4Warps;       // bulk copies and TMA loads
+constexpr int kNf4EpilogueWarp = kNf4Warps + 1;   // counts a CTA's first tile piece
+constexpr int kNf4Threads = (kNf4Warps + 2) * 32;
 constexpr int kNf4MaxSlots = 6;
 
 // Dynamic shared memory: the lookup table at offset 0, then the slots' x
@@ -277,6 +281,48 @@ __device__ __forceinline__ void store_y(const Nf4Problem& pr, int M, int n0, int
   }
 }
 
+// Sums the pieces of a tile cut between the ranges of CTAs g0 .. g1 (in
+// CTA order) for the 16 rows of the tile that compute warp vw owns, and
+// writes them to y.  t0: the tile's first chunk in the launch's order.
+template <int MT>
+__device__ __forceinline__ void finish_rows(const Nf4GemmArgs& args, const Nf4Problem& pr, int64_t C, int G,
+                                            int64_t t0, int g0, int g1, int tile, int vw, int lane) {
+  constexpr int MP = 8 * MT;
+  const int g8 = lane >> 2, t = lane & 3;
+  const int nl = 16 * vw + g8;
+  const int n0 = tile * kNf4Tile + nl;
+#pragma unroll
+  for (int mt = 0; mt < MT; ++mt) {
+    float v[4] = {0.f, 0.f, 0.f, 0.f};
+    // four pieces' loads in flight at a time, summed in CTA order
+    for (int q0 = g0; q0 <= g1; q0 += 4) {
+      float2 a[4], b[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        if (q0 + q <= g1) {
+          const int gq = q0 + q;
+          // a range that starts inside the tile holds it as its first
+          // piece, one that starts before it as its last
+          const int slot = range_start(C, G, gq) >= t0 ? 0 : 1;
+          const float* src = args.partials + (static_cast<int64_t>(gq) * 2 + slot) * kNf4Tile * MP;
+          a[q] = __ldcg(reinterpret_cast<const float2*>(src + nl * MP + 8 * mt + 2 * t));
+          b[q] = __ldcg(reinterpret_cast<const float2*>(src + (nl + 8) * MP + 8 * mt + 2 * t));
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        if (q0 + q <= g1) {
+          v[0] += a[q].x;
+          v[1] += a[q].y;
+          v[2] += b[q].x;
+          v[3] += b[q].y;
+        }
+      }
+    }
+    store_y(pr, args.M, n0, 8 * mt + 2 * t, v[0], v[1], v[2], v[3]);
+  }
+}
+
 template <int MT>
 __global__ void __launch_bounds__(kNf4Threads, MT == 1 ? 2 : 1)
     nf4_gemm_kernel(const __grid_constant__ Nf4Maps maps, const Nf4GemmArgs args) {
@@ -291,6 +337,7 @@ __global__ void __launch_bounds__(kNf4Threads, MT == 1 ? 2 : 1)
       (reinterpret_cast<uintptr_t>(smem_raw + Nf4Cfg<MT>::kLutBytes) + 1023) & ~uintptr_t(1023));
   uint8_t* cring = xring + kSlots * kXBytes;
   __shared__ uint64_t full[kNf4MaxSlots], empty[kNf4MaxSlots];
+  __shared__ uint64_t first_piece_bar;  // the compute warps have stored the first piece
   __shared__ uint32_t lut1[256];
   __shared__ int s_fin;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -306,6 +353,7 @@ __global__ void __launch_bounds__(kNf4Threads, MT == 1 ? 2 : 1)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], kNf4Warps);
     }
+    mbar_init(&first_piece_bar, kNf4Warps);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
@@ -316,7 +364,36 @@ __global__ void __launch_bounds__(kNf4Threads, MT == 1 ? 2 : 1)
     named_sync(kNf4EpiBar, kNf4Warps * 32);
   }
 
-  if (warp == kNf4Warps) {
+  if (warp == kNf4EpilogueWarp) {
+    // -------------------------------------------------------- epilogue ----
+    // The first tile of this CTA's range is a piece (a tile's tail, cut at
+    // the range start) and more follows it: the compute warps store it and
+    // go on; this warp counts it, and sums the tile if it came last (the
+    // other pieces come at the ends of the ranges before, so it rarely does).
+    const Nf4Seg sg = seg_at(args, c_begin, c_end);
+    const bool piece = !(sg.kc0 == 0 && sg.kc1 == sg.kt);
+    if (piece && c_begin + (sg.kc1 - sg.kc0) < c_end) {
+      const Nf4Problem& pr = args.prob[sg.p];
+      const int64_t t0 = pr.chunk_base + static_cast<int64_t>(sg.tile) * sg.kt;
+      const int g0 = range_cta(C, G, t0), g1 = range_cta(C, G, t0 + sg.kt - 1);
+      int* cnt = args.counters + pr.counter_base + sg.tile;
+      int fin = 0;
+      if (lane == 0 && mbar_wait(&first_piece_bar, 0, args.err)) {
+        // the wait acquires the compute warps' piece stores; one cumulative
+        // fence orders them before the count
+        __threadfence();
+        const int old = atomicAdd(cnt, 1);
+        fin = old == g1 - g0;
+        if (fin) __threadfence();
+      }
+      fin = __shfl_sync(0xffffffffu, fin, 0);
+      if (fin) {
+        for (int vw = 0; vw < kNf4Warps; ++vw) finish_rows<MT>(args, pr, C, G, t0, g0, g1, sg.tile, vw, lane);
+        __syncwarp();
+        if (lane == 0) *cnt = 0;  // every piece has counted: ready for the next launch
+      }
+    }
+  } else if (warp == kNf4ProducerWarp) {
     // -------------------------------------------------------- producer ----
     if (lane == 0) {
       for (int p = 0; p < args.num_problems; ++p) tma_prefetch_desc(&maps.x[p]);
@@ -465,6 +542,12 @@ __global__ void __launch_bounds__(kNf4Threads, MT == 1 ? 2 : 1)
           *reinterpret_cast<float2*>(part + nl * MP + 8 * mt + 2 * t) = make_float2(acc[mt][0], acc[mt][1]);
           *reinterpret_cast<float2*>(part + (nl + 8) * MP + 8 * mt + 2 * t) = make_float2(acc[mt][2], acc[mt][3]);
         }
+        if (first_piece && c < c_end) {
+          // the epilogue warp counts this piece; the range goes on
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&first_piece_bar);
+          continue;
+        }
         // the tile's pieces come from CTAs g0 .. g1, in that order
         const int64_t t0 = pr.chunk_base + static_cast<int64_t>(sg.tile) * sg.kt;
         const int g0 = range_cta(C, G, t0), g1 = range_cta(C, G, t0 + sg.kt - 1);
@@ -480,36 +563,7 @@ __global__ void __launch_bounds__(kNf4Threads, MT == 1 ? 2 : 1)
         }
         named_sync(kNf4EpiBar, kNf4Warps * 32);
         if (s_fin) {
-#pragma unroll
-          for (int mt = 0; mt < MT; ++mt) {
-            float v[4] = {0.f, 0.f, 0.f, 0.f};
-            // four pieces' loads in flight at a time, summed in CTA order
-            for (int q0 = g0; q0 <= g1; q0 += 4) {
-              float2 a[4], b[4];
-#pragma unroll
-              for (int q = 0; q < 4; ++q) {
-                if (q0 + q <= g1) {
-                  const int gq = q0 + q;
-                  // a range that starts inside the tile holds it as its
-                  // first piece, one that starts before it as its last
-                  const int slot = range_start(C, G, gq) >= t0 ? 0 : 1;
-                  const float* src = args.partials + (static_cast<int64_t>(gq) * 2 + slot) * kNf4Tile * MP;
-                  a[q] = __ldcg(reinterpret_cast<const float2*>(src + nl * MP + 8 * mt + 2 * t));
-                  b[q] = __ldcg(reinterpret_cast<const float2*>(src + (nl + 8) * MP + 8 * mt + 2 * t));
-                }
-              }
-#pragma unroll
-              for (int q = 0; q < 4; ++q) {
-                if (q0 + q <= g1) {
-                  v[0] += a[q].x;
-                  v[1] += a[q].y;
-                  v[2] += b[q].x;
-                  v[3] += b[q].y;
-                }
-              }
-            }
-            store_y(pr, args.M, n0, 8 * mt + 2 * t, v[0], v[1], v[2], v[3]);
-          }
+          finish_rows<MT>(args, pr, C, G, t0, g0, g1, sg.tile, warp, lane);
           named_sync(kNf4EpiBar, kNf4Warps * 32);
           if (tid == 0) *cnt = 0;  // every piece has counted: ready for the next launch
         }
