@@ -311,6 +311,14 @@ int persona_rope_cache(void* q, void* k, const void* v, void* k_cache, void* v_c
 int persona_silu_mul(const void* g, const void* u, void* out, int64_t n, cudaStream_t stream);
 int persona_decode_attention(const void* q, const void* k_cache, const void* v_cache, const int32_t* len, void* out,
                              int64_t B, int64_t Hq, int64_t Hkv, int64_t L, float scale, cudaStream_t stream);
+/* rope_cache (per_seq 1, start = pos) and decode_attention in one launch,
+ * with the same results: each (sequence, kv head) rotates its query heads
+ * and its k head in place, writes k and v to the caches at *pos, then
+ * attends over the first *len positions.  The two steps of the reference's
+ * attention module at decode (rotary embedding, then SDPA over the cache).  */
+int persona_rope_decode_attention(void* q, void* k, const void* v, void* k_cache, void* v_cache, const int32_t* pos,
+                                  const int32_t* len, void* out, int64_t B, int64_t Hq, int64_t Hkv, int64_t L,
+                                  float theta, float scale, cudaStream_t stream);
 
 /* ---- warm-up GEMV ---------------------------------------------------------
  * y[n] = W[n, :] @ x (fp16, fp32 accumulate).  Replaces

@@ -606,6 +606,30 @@ void silu_mul_op(const at::Tensor& g, const at::Tensor& u, at::Tensor& out) {
   check_status(persona_silu_mul(g.data_ptr(), u.data_ptr(), out.data_ptr(), g.numel(), stream), op);
 }
 
+void rope_decode_attention_op(at::Tensor& q, at::Tensor& k, const at::Tensor& v, at::Tensor& k_cache,
+                              at::Tensor& v_cache, const at::Tensor& pos, const at::Tensor& len, at::Tensor& out,
+                              double theta, double scale) {
+  const char* op = "rope_decode_attention";
+  for (const at::Tensor* t : std::initializer_list<const at::Tensor*>{&q, &k, &v, &k_cache, &v_cache, &out})
+    check_half_cuda(*t, op);
+  TORCH_CHECK(q.dim() == 3 && q.size(2) == 128 && out.sizes() == q.sizes() && k.dim() == 3 && v.sizes() == k.sizes() &&
+                  k.size(2) == 128 && k.size(0) == q.size(0),
+              op, ": q, out [B, Hq, 128], k / v [B, Hkv, 128]");
+  TORCH_CHECK(k_cache.dim() == 4 && v_cache.sizes() == k_cache.sizes() && k_cache.size(0) == q.size(0) &&
+                  k_cache.size(1) == k.size(1) && k_cache.size(3) == 128,
+              op, ": caches [B, Hkv, L, 128]");
+  TORCH_CHECK(pos.is_cuda() && pos.scalar_type() == at::kInt && pos.numel() >= 1 && len.is_cuda() &&
+                  len.scalar_type() == at::kInt && len.numel() >= 1,
+              op, ": pos and len must be CUDA int32 scalars");
+  const at::cuda::OptionalCUDAGuard guard(q.device());
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  check_status(persona_rope_decode_attention(q.data_ptr(), k.data_ptr(), v.data_ptr(), k_cache.data_ptr(),
+                                             v_cache.data_ptr(), pos.data_ptr<int32_t>(), len.data_ptr<int32_t>(),
+                                             out.data_ptr(), q.size(0), q.size(1), k.size(1), k_cache.size(2),
+                                             static_cast<float>(theta), static_cast<float>(scale), stream),
+               op);
+}
+
 void decode_attention_op(const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& v_cache,
                          const at::Tensor& len, at::Tensor& out, double scale) {
   const char* op = "decode_attention";
@@ -745,6 +769,8 @@ TORCH_LIBRARY(persona, m) {
         "int per_seq, float theta) -> ()");
   m.def("silu_mul(Tensor g, Tensor u, Tensor(a!) out) -> ()");
   m.def("decode_attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor len, Tensor(a!) out, float scale) -> ()");
+  m.def("rope_decode_attention(Tensor(a!) q, Tensor(b!) k, Tensor v, Tensor(c!) k_cache, Tensor(d!) v_cache, "
+        "Tensor pos, Tensor len, Tensor(e!) out, float theta, float scale) -> ()");
 }
 
 TORCH_LIBRARY_IMPL(persona, CUDA, m) {
@@ -757,6 +783,7 @@ TORCH_LIBRARY_IMPL(persona, CUDA, m) {
   m.impl("rope_cache", &rope_cache_op);
   m.impl("silu_mul", &silu_mul_op);
   m.impl("decode_attention", &decode_attention_op);
+  m.impl("rope_decode_attention", &rope_decode_attention_op);
   m.impl("bgmv_shrink", &bgmv_shrink_cuda);
   m.impl("bgmv_expand", &bgmv_expand_cuda);
   m.impl("gemv_fp16", &persona::gemv_fp16_cuda);

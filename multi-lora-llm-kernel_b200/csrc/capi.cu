@@ -860,6 +860,27 @@ int persona_silu_mul(const void* g, const void* u, void* out, int64_t n, cudaStr
   return persona::launch_silu_mul(g, u, out, n, stream) == cudaSuccess ? PERSONA_OK : PERSONA_ERR_CUDA;
 }
 
+int persona_rope_decode_attention(void* q, void* k, const void* v, void* k_cache, void* v_cache, const int32_t* pos,
+                                  const int32_t* len, void* out, int64_t B, int64_t Hq, int64_t Hkv, int64_t L,
+                                  float theta, float scale, cudaStream_t stream) {
+  if (q == nullptr || k == nullptr || v == nullptr || k_cache == nullptr || v_cache == nullptr || pos == nullptr ||
+      len == nullptr || out == nullptr)
+    return PERSONA_ERR_INVALID_ARG;
+  if (B < 0 || B > 65535 || Hkv <= 0 || Hq <= 0 || Hq % Hkv || Hq / Hkv > 8 || Hkv > 65535 || L <= 0 ||
+      L > kI32Max || !(theta > 1.f))
+    return PERSONA_ERR_SHAPE;
+  if (!aligned16(k_cache) || !aligned16(v_cache) || (reinterpret_cast<uintptr_t>(q) & 1) ||
+      (reinterpret_cast<uintptr_t>(k) & 1) || (reinterpret_cast<uintptr_t>(v) & 1) ||
+      (reinterpret_cast<uintptr_t>(out) & 1))
+    return PERSONA_ERR_ALIGNMENT;
+  if (B == 0) return PERSONA_OK;
+  return persona::launch_rope_decode_attention(q, k, v, k_cache, v_cache, pos, len, out, static_cast<int>(B),
+                                               static_cast<int>(Hq), static_cast<int>(Hkv), static_cast<int>(L),
+                                               std::log2(theta), scale, stream) == cudaSuccess
+             ? PERSONA_OK
+             : PERSONA_ERR_CUDA;
+}
+
 int persona_decode_attention(const void* q, const void* k_cache, const void* v_cache, const int32_t* len, void* out,
                              int64_t B, int64_t Hq, int64_t Hkv, int64_t L, float scale, cudaStream_t stream) {
   if (q == nullptr || k_cache == nullptr || v_cache == nullptr || len == nullptr || out == nullptr)

@@ -104,7 +104,7 @@ __global__ void rope_cache_kernel(__half* __restrict__ q, __half* __restrict__ k
   asm volatile("griddepcontrol.launch_dependents;");
   const int r = blockIdx.x;
   const int b = r / per_seq, pos = *start + (r - b * per_seq);
-  if (pos >= L) return;
+  if (pos < 0 || pos >= L) return;
   const int j = threadIdx.x & 63;
   // inv_freq = theta^(-2j/D), angle in fp32
   const float inv_freq = exp2f(-log2_theta * static_cast<float>(2 * j) / static_cast<float>(D));
@@ -164,14 +164,66 @@ __global__ void silu_mul_kernel(const __half* __restrict__ g, const __half* __re
 // G * 128 query values, all fp32.
 constexpr int kAttnThreads = 128;
 
+// With a position (rope.pos != nullptr) the kernel first does what
+// rope_cache_kernel does for this (sequence, kv head), with the same
+// arithmetic: it rotates the G query heads and the k head of the new token
+// in place and writes k and v to the caches at *pos (nothing at all when
+// *pos is outside [0, L)); the attention below then reads them back.
+struct RopeIn {
+  __half* q;  // [B, Hq, 128], rotated in place (and read below)
+  __half* k;  // [B, Hkv, 128], rotated in place
+  const __half* v;
+  __half* kc;  // the caches, written at *pos
+  __half* vc;
+  const int* pos;
+  float log2_theta;
+};
+
+__device__ __forceinline__ void rope_pair(__half* x, int j, __half c, __half s, __half& o1, __half& o2) {
+  const __half x1 = x[j], x2 = x[j + 64];
+  o1 = __hsub(__hmul(x1, c), __hmul(x2, s));
+  o2 = __hadd(__hmul(x2, c), __hmul(x1, s));
+  x[j] = o1;
+  x[j + 64] = o2;
+}
+
+// q, kc and vc are not restrict: with a position they are written above
+// their reads, through rope.
 __global__ void __launch_bounds__(kAttnThreads) decode_attention_kernel(
-    const __half* __restrict__ q, const __half* __restrict__ kc, const __half* __restrict__ vc,
-    const int* __restrict__ len_ptr, __half* __restrict__ out, int Hq, int Hkv, int L, float scale) {
+    const __half* q, const __half* kc, const __half* vc, const int* __restrict__ len_ptr, __half* __restrict__ out,
+    int Hq, int Hkv, int L, float scale, const RopeIn rope) {
   constexpr int D = 128;
   pdl_wait();
   asm volatile("griddepcontrol.launch_dependents;");
   const int b = blockIdx.x, kh = blockIdx.y, tid = threadIdx.x;
   const int G = Hq / Hkv;
+  if (rope.pos != nullptr) {
+    const int pos = *rope.pos;
+    if (pos >= 0 && pos < L) {
+      const int j = tid & 63;
+      const float inv_freq = exp2f(-rope.log2_theta * static_cast<float>(2 * j) / static_cast<float>(D));
+      float sn, cs;
+      sincosf(static_cast<float>(pos) * inv_freq, &sn, &cs);
+      const __half c = __float2half_rn(cs), s = __float2half_rn(sn);
+      // heads 0 .. G - 1: this kv head's query heads; head G: its k
+      for (int hh = tid >> 6; hh <= G; hh += kAttnThreads / 64) {
+        __half o1, o2;
+        if (hh < G) {
+          rope_pair(rope.q + (static_cast<int64_t>(b) * Hq + kh * G + hh) * D, j, c, s, o1, o2);
+        } else {
+          rope_pair(rope.k + (static_cast<int64_t>(b) * Hkv + kh) * D, j, c, s, o1, o2);
+          const int64_t dst = ((static_cast<int64_t>(b) * Hkv + kh) * L + pos) * D;
+          const __half* vr = rope.v + (static_cast<int64_t>(b) * Hkv + kh) * D;
+          rope.kc[dst + j] = o1;
+          rope.kc[dst + j + 64] = o2;
+          rope.vc[dst + j] = vr[j];
+          rope.vc[dst + j + 64] = vr[j + 64];
+        }
+      }
+    }
+    // the rotated q and the new cache row, written above, are read below
+    __syncthreads();
+  }
   const int len = min(*len_ptr, L);
   extern __shared__ float attn_smem[];
   float* sc = attn_smem;                 // [G][L]
@@ -297,8 +349,9 @@ cudaError_t launch_silu_mul(const void* g, const void* u, void* out, int64_t n, 
                     static_cast<const __half*>(g), static_cast<const __half*>(u), static_cast<__half*>(out), n);
 }
 
-cudaError_t launch_decode_attention(const void* q, const void* kc, const void* vc, const int* len, void* out, int B,
-                                    int Hq, int Hkv, int L, float scale, cudaStream_t st) {
+namespace {
+cudaError_t attention_launch(const void* q, const void* kc, const void* vc, const int* len, void* out, int B, int Hq,
+                             int Hkv, int L, float scale, const RopeIn& rope, cudaStream_t st) {
   const int G = Hq / Hkv;
   const size_t smem = (static_cast<size_t>(G) * L + 8 * G * 128 + G * 128) * sizeof(float);
   if (smem > 227 * 1024) return cudaErrorInvalidValue;
@@ -309,7 +362,29 @@ cudaError_t launch_decode_attention(const void* q, const void* kc, const void* v
   }
   return launch_pdl(decode_attention_kernel, dim3(B, Hkv), dim3(kAttnThreads), smem, st,
                     static_cast<const __half*>(q), static_cast<const __half*>(kc), static_cast<const __half*>(vc),
-                    len, static_cast<__half*>(out), Hq, Hkv, L, scale);
+                    len, static_cast<__half*>(out), Hq, Hkv, L, scale, rope);
+}
+
+}  // namespace
+
+cudaError_t launch_decode_attention(const void* q, const void* kc, const void* vc, const int* len, void* out, int B,
+                                    int Hq, int Hkv, int L, float scale, cudaStream_t st) {
+  const RopeIn none = {};
+  return attention_launch(q, kc, vc, len, out, B, Hq, Hkv, L, scale, none, st);
+}
+
+cudaError_t launch_rope_decode_attention(void* q, void* k, const void* v, void* kc, void* vc, const int* pos,
+                                         const int* len, void* out, int B, int Hq, int Hkv, int L, float log2_theta,
+                                         float scale, cudaStream_t st) {
+  RopeIn rope;
+  rope.q = static_cast<__half*>(q);
+  rope.k = static_cast<__half*>(k);
+  rope.v = static_cast<const __half*>(v);
+  rope.kc = static_cast<__half*>(kc);
+  rope.vc = static_cast<__half*>(vc);
+  rope.pos = pos;
+  rope.log2_theta = log2_theta;
+  return attention_launch(q, kc, vc, len, out, B, Hq, Hkv, L, scale, rope, st);
 }
 
 }  // namespace persona

@@ -16,9 +16,10 @@ package's kernels:
 * LoRA: ``ops.bgmv_fused_multi`` / ``ops.bgmv_fused`` on a plan computed once
   per batch at decode, ``ops.sgmv_fused`` per request segment at prefill;
 * the rest: ``ops.add_rmsnorm`` (residual add fused into the
-  next norm), ``rope_cache`` (rotary embedding + KV-cache write),
-  ``decode_attention``, ``silu_mul``; the LM head and the prefill attention
-  are library calls (cuBLAS, scaled_dot_product_attention).
+  next norm), ``rope_cache`` (rotary embedding + KV-cache write) at prefill,
+  ``rope_decode_attention`` (the same and the attention, one launch) at
+  decode, ``silu_mul``; the LM head and the prefill attention are library
+  calls (cuBLAS, scaled_dot_product_attention).
 
 A decode step has fixed shapes and reads the position from device memory,
 so it is captured once as a CUDA graph and replayed for every token.
@@ -213,11 +214,10 @@ class MistralLoRAModel:
             ops.bgmv_fused_multi([b["xn"]] * 3, [lora[m][0] for m in ("q_proj", "k_proj", "v_proj")],
                                  [lora[m][1] for m in ("q_proj", "k_proj", "v_proj")], st.slots,
                                  [b["q"], b["k"], b["v"]], plan=st.plan)
-            q3 = b["q"].view(B, cfg.n_heads, 128)
-            ops.rope_cache(q3, b["k"].view(B, cfg.n_kv_heads, 128), b["v"].view(B, cfg.n_kv_heads, 128),
-                                         st.k_cache[li], st.v_cache[li], st.pos, 1, cfg.rope_theta)
-            ops.decode_attention(q3, st.k_cache[li], st.v_cache[li], st.length,
-                                               b["attn"].view(B, cfg.n_heads, 128), scale)
+            # rotary embedding, cache write and attention in one launch
+            ops.rope_decode_attention(b["q"].view(B, cfg.n_heads, 128), b["k"].view(B, cfg.n_kv_heads, 128),
+                                      b["v"].view(B, cfg.n_kv_heads, 128), st.k_cache[li], st.v_cache[li], st.pos,
+                                      st.length, b["attn"].view(B, cfg.n_heads, 128), cfg.rope_theta, scale)
             nf4.linear(b["attn"], [lw.o], outs=[b["o"]])
             ops.bgmv_fused(b["attn"], *lora["o_proj"], st.slots, b["o"], plan=st.plan)
             ops.add_rmsnorm(b["h"], b["o"], lw.post_norm, b["xn"], cfg.rms_eps)

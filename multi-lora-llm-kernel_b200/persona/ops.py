@@ -211,6 +211,16 @@ def decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tens
     return out
 
 
+def rope_decode_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, k_cache: torch.Tensor,
+                          v_cache: torch.Tensor, pos: torch.Tensor, length: torch.Tensor, out: torch.Tensor,
+                          theta: float, scale: float) -> torch.Tensor:
+    """``rope_cache`` (one token per sequence at ``pos``) and
+    ``decode_attention`` in one launch, with the same results."""
+    _require_cuda("rope_decode_attention", q, k, v, k_cache, v_cache, pos, length, out)
+    torch.ops.persona.rope_decode_attention(q, k, v, k_cache, v_cache, pos, length, out, float(theta), float(scale))
+    return out
+
+
 def bgmv_lora_delta_multi(xs, a_pools, b_pools, slots: torch.Tensor, deltas):
     """``deltas[i][t] = B_i[s] @ (A_i[s] @ xs[i][t])`` in fp32 (0 for rows
     without adapter), at most 64 rows: the LoRA term alone, for a base

@@ -99,6 +99,37 @@ def test_decode_attention_matches_reference(length):
     torch.testing.assert_close(out.float(), want, rtol=2e-3, atol=2e-3)
 
 
+
+@pytest.mark.parametrize("pos,G", [(0, 4), (37, 4), (255, 8), (256, 4)])
+def test_rope_decode_attention_equals_rope_cache_then_attention(pos, G):
+    """The one-launch rotary + attention gives the bits of rope_cache (one
+    token per sequence at pos) followed by decode_attention: the attention
+    output, q and k rotated in place, and both caches.  pos = L writes
+    nothing and rotates nothing, as rope_cache does."""
+    g = torch.Generator(device=_dev()).manual_seed(40 + pos)
+    B, Hkv, L = 3, 8, 256
+    Hq = Hkv * G
+    q = torch.randn(B, Hq, 128, generator=g, device=_dev()).half()
+    k = torch.randn(B, Hkv, 128, generator=g, device=_dev()).half()
+    v = torch.randn(B, Hkv, 128, generator=g, device=_dev()).half()
+    kc = torch.randn(B, Hkv, L, 128, generator=g, device=_dev()).half()
+    vc = torch.randn(B, Hkv, L, 128, generator=g, device=_dev()).half()
+    p_t = torch.tensor([pos], dtype=torch.int32, device=_dev())
+    ln = torch.tensor([min(pos + 1, L)], dtype=torch.int32, device=_dev())
+    scale = 1 / math.sqrt(128)
+    q1, k1, kc1, vc1 = q.clone(), k.clone(), kc.clone(), vc.clone()
+    out1 = torch.empty_like(q)
+    ops.rope_cache(q1, k1, v, kc1, vc1, p_t, 1, 1e6)
+    ops.decode_attention(q1, kc1, vc1, ln, out1, scale)
+    q2, k2, kc2, vc2 = q.clone(), k.clone(), kc.clone(), vc.clone()
+    out2 = torch.empty_like(q)
+    ops.rope_decode_attention(q2, k2, v, kc2, vc2, p_t, ln, out2, 1e6, scale)
+    torch.cuda.synchronize()
+    for a, b in ((out1, out2), (q1, q2), (k1, k2), (kc1, kc2), (vc1, vc2)):
+        assert torch.equal(a, b)
+    if pos >= L:
+        assert torch.equal(q2, q) and torch.equal(kc2, kc)
+
 # ------------------------------------------------------------ small model --
 CFG = MistralConfig(num_layers=2, hidden=512, n_heads=4, n_kv_heads=2, head_dim=128, intermediate=1024, vocab=1024)
 

@@ -134,3 +134,41 @@ def test_linear_with_addend_matches_the_oracle(M):
         w = Q.dequantize_f32(q.packed.cpu().numpy(), np.float32(q.offset.item()), N, K).astype(np.float64)
         want = (x.astype(np.float64) @ w.T + add).astype(np.float16)
         np.testing.assert_allclose(y.cpu().numpy().astype(np.float32), want.astype(np.float32), **TOL)
+
+
+@pytest.mark.parametrize("M", [1, 8, 20])
+def test_problems_of_different_k_in_one_launch(M):
+    """Four linears with their own x and K in one launch through the C ABI
+    (1018 chunks, three to four per CTA on a B200): the CTAs' equal chunk
+    ranges cross problem boundaries where the chunks per tile change (3, 25,
+    1, 13), tiles are cut into pieces of different lengths, and one tile is a
+    single chunk.  Each y against the oracle; a second launch gives the same
+    bits."""
+    lib = capi_lib.load()
+    shapes = [(384, 384), (4096, 3200), (128, 128), (2048, 1664)]
+    rng = np.random.default_rng(70 + M)
+    qs, xs, ys, probs = [], [], [], []
+    for i, (N, K) in enumerate(shapes):
+        q = nf4.quantize(torch.from_numpy(_weights(200 + i, N, K)).to(_dev()))
+        x = torch.from_numpy(rng.standard_normal((M, K)).astype(np.float16)).to(_dev())
+        y = torch.full((M, N), 3.0, dtype=torch.float16, device=_dev())
+        qs.append(q), xs.append(x), ys.append(y)
+        probs.append(capi_lib.Nf4Problem(q.packed.data_ptr(), q.offset.data_ptr(), x.data_ptr(), K, y.data_ptr(), N,
+                                         N, K))
+    arr = (capi_lib.Nf4Problem * len(probs))(*probs)
+    ws_bytes = lib.persona_nf4_linear_workspace_size(arr, len(probs))
+    ws = torch.zeros(ws_bytes, dtype=torch.uint8, device=_dev())
+    err = torch.zeros(1, dtype=torch.int32, device=_dev())
+    st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    capi_lib.check(lib.persona_nf4_linear(arr, len(probs), M, ws.data_ptr(), ws_bytes, err.data_ptr(), st))
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    first = [y.clone() for y in ys]
+    for q, x, y, (N, K) in zip(qs, xs, ys, shapes):
+        want = Q.linear_ref(x.cpu().numpy(), q.packed.cpu().numpy(), np.float32(q.offset.item()), N, K)
+        np.testing.assert_allclose(y.cpu().numpy().astype(np.float32), want.astype(np.float32), **TOL)
+    capi_lib.check(lib.persona_nf4_linear(arr, len(probs), M, ws.data_ptr(), ws_bytes, err.data_ptr(), st))
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    for a, b in zip(first, ys):
+        assert torch.equal(a, b)
