@@ -14,7 +14,8 @@ package's kernels:
 * base projections: ``nf4.linear`` (one launch for q / k / v, one for gate /
   up, one each for o and down);
 * LoRA: ``ops.bgmv_fused_multi`` / ``ops.bgmv_fused`` on a plan computed once
-  per batch at decode, ``ops.sgmv_fused`` per request segment at prefill;
+  per batch at decode and, with per-row slots, at prefill; ``ops.sgmv_fused``
+  per request segment for prefills of at least ``SGMV_MIN_ROWS`` rows;
 * the rest: ``ops.add_rmsnorm`` (residual add fused into the
   next norm), ``rope_cache`` (rotary embedding + KV-cache write) at prefill,
   ``rope_decode_attention`` (the same and the attention, one launch) at
@@ -28,6 +29,7 @@ so it is captured once as a CUDA graph and replayed for every token.
 from __future__ import annotations
 
 import math
+import os
 from dataclasses import dataclass, field
 from typing import List, Optional
 
@@ -36,6 +38,10 @@ import torch.nn.functional as F
 
 from persona import nf4, ops
 from persona.adapter_pool import AdapterPool
+
+# Prefill rows from which the LoRA goes through the tensor-core SGMV kernel
+# (64 items of 128 rows); fewer go through the BGMV launch with per-row slots.
+SGMV_MIN_ROWS = int(os.environ.get("PERSONA_PREFILL_SGMV_MIN_ROWS", "8192"))
 
 
 @dataclass
@@ -168,13 +174,30 @@ class MistralLoRAModel:
         xn = torch.empty_like(h)
         indptr = torch.arange(0, R + 1, T, dtype=torch.int32, device=self.device)
         start = torch.zeros(1, dtype=torch.int32, device=self.device)
+        # LoRA: the tensor-core SGMV kernel gives each 128-row item to one CTA,
+        # so it needs many items to fill the GPU; below SGMV_MIN_ROWS rows the
+        # rows go through the multi-projection BGMV launch with per-row slots
+        # (one plan for the whole prefill), as the reference's caller does.
+        use_sgmv = R >= SGMV_MIN_ROWS
+        row_slots = plan = None
+        if not use_sgmv:
+            row_slots = st.slots.repeat_interleave(T).contiguous()
+            plan = ops.bgmv_plan(row_slots, self.pool.max_slots)
+
+        def lora_apply(x, lora, names, ys):
+            if use_sgmv:
+                for name, y in zip(names, ys):
+                    ops.sgmv_fused(x, *lora[name], indptr, st.slots, y)
+            else:
+                ops.bgmv_fused_multi([x] * len(names), [lora[m][0] for m in names], [lora[m][1] for m in names],
+                                     row_slots, list(ys), plan=plan)
+
         delta = None
         for li, lw in enumerate(self.layers):
             lora = self._lora[li]
             ops.add_rmsnorm(h, delta, lw.in_norm, xn, cfg.rms_eps)
             q, k, v = nf4.linear(xn, [lw.q, lw.k, lw.v])
-            for name, y in (("q_proj", q), ("k_proj", k), ("v_proj", v)):
-                ops.sgmv_fused(xn, *lora[name], indptr, st.slots, y)
+            lora_apply(xn, lora, ("q_proj", "k_proj", "v_proj"), (q, k, v))
             q3, k3, v3 = (t.view(R, -1, 128) for t in (q, k, v))
             ops.rope_cache(q3, k3, v3, st.k_cache[li], st.v_cache[li], start, T, cfg.rope_theta)
             qa = q3.view(B, T, cfg.n_heads, 128).transpose(1, 2)
@@ -183,15 +206,14 @@ class MistralLoRAModel:
             attn = F.scaled_dot_product_attention(qa, ka, va, is_causal=True, enable_gqa=True)
             attn = attn.transpose(1, 2).reshape(R, cfg.q_dim).contiguous()
             o = nf4.linear(attn, [lw.o])[0]
-            ops.sgmv_fused(attn, *lora["o_proj"], indptr, st.slots, o)
+            lora_apply(attn, lora, ("o_proj",), (o,))
             ops.add_rmsnorm(h, o, lw.post_norm, xn, cfg.rms_eps)
             g_, u_ = nf4.linear(xn, [lw.gate, lw.up])
-            ops.sgmv_fused(xn, *lora["gate_proj"], indptr, st.slots, g_)
-            ops.sgmv_fused(xn, *lora["up_proj"], indptr, st.slots, u_)
+            lora_apply(xn, lora, ("gate_proj", "up_proj"), (g_, u_))
             act = torch.empty_like(g_)
             ops.silu_mul(g_, u_, act)
             dn = nf4.linear(act, [lw.down])[0]
-            ops.sgmv_fused(act, *lora["down_proj"], indptr, st.slots, dn)
+            lora_apply(act, lora, ("down_proj",), (dn,))
             delta = dn
         ops.add_rmsnorm(h, delta, self.final_norm, xn, cfg.rms_eps)
         last = xn.view(B, T, cfg.hidden)[:, -1, :]
