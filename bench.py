@@ -55,6 +55,8 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-decode", action="store_true",
+                    help="skip the bounded mixed-adapter decode run that the headline line carries")
     ap.add_argument("--workload", choices=["mixed_decode", "sgmv_prefill", "decode_set", "e2e_decode", "nf4_decode"],
                     default="mixed_decode",
                     help="mixed_decode is the headline; the others print their own line")
@@ -100,112 +102,143 @@ def global_slots(world):
 # ------------------------------------------------------------------ clocks --
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled while the GPU works."""
+    """SM clock and clock-event (throttle) reasons of one GPU, sampled about
+    every millisecond by a thread that makes read-only NVML queries, so that
+    even a timed region of a few milliseconds gets samples.  ``mark`` brackets
+    the timed region; ``stop`` summarises the samples inside it."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,utilization.gpu,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    # NVML clocks-event reason bits (nvmlClocksEventReason*)
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown"}
 
-    def __init__(self, index: str):
-        self.index = index
-        self.proc = None
-        self.lines = []
+    def __init__(self, pci_bus_id: str, period_s: float = 0.001):
+        self.pci = pci_bus_id
+        self.period = period_s
+        self.samples = []  # (host monotonic s, sm MHz, reasons bitmask)
+        self.max_mhz = None
+        self.error = None
+        self._stop = threading.Event()
+        self.thread = None
 
     def start(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "50"],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.thread = threading.Thread(target=self._read, daemon=True)
-            self.thread.start()
-        except OSError:
-            self.proc = None
+            import pynvml
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append((time.monotonic(), line.strip()))
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByPciBusId(self.pci)
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+            reasons = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                pynvml.nvmlDeviceGetCurrentClocksThrottleReasons
+        except Exception as e:  # no NVML: report why, keep benchmarking
+            self.error = f"NVML unavailable: {e}"
+            return
 
-    def stop(self, window=None):
-        """Summarise the samples that arrived inside ``window`` (host
-        monotonic seconds bracketing the timed region)."""
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
-        self.thread.join(timeout=2)
-        sm, inside, mx, reasons = [], [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for t, ln in self.lines:
-            f = [c.strip() for c in ln.split(",")]
-            if len(f) < 10:
-                continue
-            try:
-                mhz, mxv = float(f[1]), float(f[2])
-            except ValueError:
-                continue
-            mx = mxv
-            sm.append(mhz)
-            if window is None or window[0] <= t <= window[1]:
-                inside.append(mhz)
-                for nm, val in zip(names, f[6:10]):
-                    if val.lower() == "active":
-                        reasons.add(nm)
-        return {"sm_mhz": statistics.median(inside) if inside else None, "sm_max_mhz": mx,
-                "reasons": sorted(reasons), "samples": len(sm), "samples_in_timed_region": len(inside)}
+        def run():
+            while not self._stop.is_set():
+                try:
+                    mhz = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
+                    rs = reasons(h)
+                    self.samples.append((time.monotonic(), float(mhz), int(rs)))
+                except Exception as e:  # pragma: no cover - driver hiccup
+                    self.error = str(e)
+                    return
+                time.sleep(self.period)
+
+        self.thread = threading.Thread(target=run, daemon=True)
+        self.thread.start()
+
+    def stop(self, window=None, busy_s=None):
+        """Summary of the samples inside ``window`` (host monotonic seconds);
+        ``busy_s``: device time of the timed region, for time x clock."""
+        self._stop.set()
+        if self.thread is not None:
+            self.thread.join(timeout=2)
+        if self.error and not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [self.error], "samples": 0,
+                    "samples_in_timed_region": 0}
+        inside = [x for x in self.samples if window is None or window[0] <= x[0] <= window[1]]
+        reasons = sorted({name for _, _, rs in inside for bit, name in self.REASONS.items() if rs & bit})
+        med = statistics.median([m for _, m, _ in inside]) if inside else None
+        out = {"sm_mhz": med, "sm_max_mhz": self.max_mhz, "reasons": reasons, "samples": len(self.samples),
+               "samples_in_timed_region": len(inside), "source": "NVML (read-only), ~1 ms period"}
+        if med is not None and busy_s is not None:
+            out["timed_s_x_median_mhz"] = busy_s * med
+        return out
 
 
 # -------------------------------------------------------------- CPU legs --
 
-class CpuSample:
-    """A bounded sample of the workload for the oracle port (the reference's
-    fp32 CPU algorithm, persona/ops.py:12-56): the q_proj call (4096->4096,
-    rank 64) on `rows` rows of the Zipf batch with a pool of `slots` slots."""
+def cpu_model() -> str:
+    try:
+        for ln in Path("/proc/cpuinfo").read_text().splitlines():
+            if ln.startswith("model name"):
+                return ln.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+
+    return platform.processor() or "unknown"
+
+
+class CpuLayer:
+    """The reference's CPU algorithm (its fp32 torch BGMV, persona/ops.py:12-68,
+    restated in oracle/bgmv_torch_ref.py) on the headline workload: the seven
+    projections of one decoder layer, 512 rows of the Zipf batch, rank 64, a
+    256-slot pool, fp16 storage.  ``call(i)`` runs projection i (or all seven
+    with i=None) and returns (seconds, algorithmic bytes)."""
 
     def __init__(self, rows: int = ROWS_PER_GPU, slots: int = POOL_SLOTS):
+        import torch
+
         from oracle import bgmv_oracle as O
-        from persona.workloads import make_projection, zipf_slots
+        from persona.workloads import zipf_slots
 
-        self.O = O
+        self.torch = torch
         rng = np.random.Generator(np.random.PCG64(SEED))
-        self.slots = zipf_slots(rng, rows, slots)
-        self.p = make_projection(rng, "q_proj", rows, 4096, 4096, RANK, slots, "f16")
-        self.bytes = O.algorithmic_bytes(rows, 4096, 4096, RANK, self.slots)
-        self.desc = (f"numpy port of the reference fp32 BGMV: q_proj 4096->4096, {rows} rows, rank 64, "
-                     f"{slots}-slot pool widened per call")
+        self.slots_np = zipf_slots(rng, rows, slots)
+        self.slots = torch.from_numpy(self.slots_np)
+        g = torch.Generator().manual_seed(SEED * 1000 + 17)
+        self.projs = []
+        for name, K, N in projections():
+            lim = 1.0 / np.sqrt(K)
+            a = (torch.rand(slots, RANK, K, generator=g) * (2 * lim) - lim).half()
+            b = (torch.randn(slots, N, RANK, generator=g) * 0.04).half()
+            x = torch.randn(rows, K, generator=g).half()
+            self.projs.append(dict(name=name, a=a, b=b, x=x, y=torch.zeros(rows, N, dtype=torch.float16),
+                                   bytes=O.algorithmic_bytes(rows, K, N, RANK, self.slots_np)))
+        self.rows, self.pool = rows, slots
 
-    def call(self) -> float:
-        y = self.p.y.copy()
+    def call(self, i=None):
+        from oracle import bgmv_torch_ref as TR
+
+        ps = self.projs if i is None else [self.projs[i % len(self.projs)]]
         t0 = time.perf_counter()
-        self.O.bgmv_forward_ref(self.p.x, self.p.a_pool, self.p.b_pool, self.slots, y=y)
-        return time.perf_counter() - t0
+        for p in ps:
+            TR.bgmv_forward_ref(p["x"], p["a"], p["b"], self.slots, p["y"])
+        return time.perf_counter() - t0, sum(p["bytes"] for p in ps)
+
+    def describe(self, per_step: str) -> str:
+        return (f"the reference's fp32 torch BGMV (persona/ops.py:12-68, restated in oracle/bgmv_torch_ref.py) "
+                f"on {per_step} of the headline layer ({self.rows} rows, rank 64, {self.pool}-slot pool, fp16, "
+                f"whole pool widened per call as the reference does); torch threads={self.torch.get_num_threads()}, "
+                f"host cpus={os.cpu_count()}, cpu={cpu_model()}")
 
 
-def blas_threads() -> int:
-    try:
-        from threadpoolctl import threadpool_info
+def cpu_baseline(seconds: float = 20.0):
+    """The CPU leg of our arm: the seven projections of the headline layer,
+    one after another, for about ``seconds`` (at least one full layer)."""
+    import torch
 
-        return max([i.get("num_threads", 1) for i in threadpool_info()] or [1])
-    except Exception:
-        return 1
-
-
-def cpu_baseline(seconds: float = 12.0, min_reps: int = 2):
-    """The oracle port timed on the full q_proj call for ~`seconds`."""
-    smp = CpuSample()
-    smp.call()  # warm-up
-    times = []
-    t_end = time.perf_counter() + seconds
-    while len(times) < min_reps or time.perf_counter() < t_end:
-        times.append(smp.call())
-    med = statistics.median(times)
-    th = blas_threads()
-    return {"value": smp.bytes / med / 1e9, "unit": UNIT, "cores": th, "kind": "port",
-            "sample": f"{smp.desc}; {len(times)} reps, median {med * 1e3:.1f} ms; BLAS threads={th} "
-                      f"(pool widening single-threaded); host cpus={os.cpu_count()}"}
+    lay = CpuLayer()
+    lay.call(0)  # warm-up
+    t_tot, b_tot, n = 0.0, 0, 0
+    while n < len(lay.projs) or t_tot < seconds:
+        t, b = lay.call(n)
+        t_tot, b_tot, n = t_tot + t, b_tot + b, n + 1
+    return {"value": b_tot / t_tot / 1e9, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
+            "cpu_model": cpu_model(), "torch_threads": torch.get_num_threads(), "host_cpus": os.cpu_count(),
+            "sample": lay.describe(f"{n} projection calls ({n / len(lay.projs):.1f} layers), "
+                                   f"{t_tot:.1f} s in total")}
 
 
 def workload_config(world: int) -> dict:
@@ -222,37 +255,43 @@ def workload_config(world: int) -> dict:
 
 def run_reference(args):
     """The reference arm: the reference's CPU implementation of the path (its
-    fp32 torch BGMV, restated by the oracle port) on the host cores.  Under
-    torchrun only rank 0 works."""
+    fp32 torch BGMV, restated in oracle/bgmv_torch_ref.py) on the host cores,
+    on our arm's workload.  One step is the whole 7-projection layer at full
+    size when --steps + --warmup of them fit in about two minutes; otherwise
+    one full-size projection per step, cycling through the seven (so that
+    every seven steps cover the layer).  Under torchrun only rank 0 works."""
+    import torch
+
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
     t0 = time.perf_counter()
-    # Per-step sample: the largest of these whose warm-up + steps fit in ~2 minutes.
     budget = 120.0
     steps = max(1, args.steps)
     warm = max(0, args.warmup)
-    smp = None
-    for rows, slots in ((64, 32), (16, 8), (4, 2), (1, 1)):
-        smp = CpuSample(rows=rows, slots=slots)
-        smp.call()
-        t1 = min(smp.call() for _ in range(2))
-        if (steps + warm) * t1 <= budget:
-            break
-    for _ in range(warm):
-        smp.call()
-    times = [smp.call() for _ in range(steps)]
-    med = statistics.median(times)
-    value = smp.bytes / med / 1e9
-    th = blas_threads()
+    lay = CpuLayer()
+    t_layer, _ = lay.call(None)
+    whole = (steps + warm) * t_layer <= budget
+    for k in range(warm):
+        lay.call(None if whole else k)
+    times, byts = [], []
+    for k in range(steps):
+        t, b = lay.call(None if whole else k)
+        times.append(t)
+        byts.append(b)
+    value = sum(byts) / sum(times) / 1e9
+    per_step = "all seven projections per step" if whole else "one projection per step, cycling through the seven"
+    cfg = workload_config(args.gpus)
+    cfg["workload"] += f" (CPU arm: {per_step})"
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
-        "steps": steps, "warmup": warm, "ms_per_step": med * 1e3,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "steps": steps, "warmup": warm, "ms_per_step": statistics.mean(times) * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32 (fp16 storage)",
         "data": "synthetic (seeded Zipf slots, random-init rank-64 adapters)",
-        "config": workload_config(args.gpus),
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": th, "kind": "port",
-                         "sample": f"{smp.desc}; median of {steps} steps; BLAS threads={th}"},
+        "config": cfg,
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
+                         "cpu_model": cpu_model(), "torch_threads": torch.get_num_threads(),
+                         "host_cpus": os.cpu_count(), "sample": lay.describe(per_step)},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "wall_s": time.perf_counter() - t0,
     }
@@ -421,7 +460,7 @@ def run_ours(args):
     torch.cuda.synchronize()
     barrier()
     e2e_ms_local = e_start.elapsed_time(e_end) / e_steps
-    clk = clocks.stop(window=(host_t0, host_t1))
+    clk = clocks.stop(window=(host_t0, host_t1), busy_s=ms_local * K_steps * 1e-3)
     ops.check_errors(dev)
 
     ms = max_over_ranks(ms_local)
@@ -477,6 +516,18 @@ def run_ours(args):
         }
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline()
+    if world == 1 and not args.no_decode:
+        # the metric's second half: mixed-adapter decode tokens/s (config 5 at
+        # batch 8 with 8 adapters), a bounded run after the BGMV measurement
+        del projs, xs, a_s, b_s, ys, host, bufs
+        torch.cuda.empty_cache()
+        dm = decode_measure(dev, 1, 0, 8, 3, 3)
+        dl = decode_line(dm, 1, 3, 3)
+        line["decode"] = {k: dl[k] for k in ("value", "unit", "ms_per_step", "prefill_ms", "decode_ms",
+                                             "decode_ms_per_token_step", "decode_tokens_per_s", "roofline",
+                                             "config", "gpu_launches_per_decode_step")}
+        line["decode"]["metric"] = "mixed-adapter decode tokens/s (whole generation: prefill + 127 steps)"
+        line["decode"]["steps"], line["decode"]["warmup"] = 3, 3
     if world > 1:
         barrier()
         dist.destroy_process_group()
@@ -786,35 +837,21 @@ def run_sgmv_tp(args):
     return 0
 
 
-def run_e2e(args):
-    """Config 5: mixed-adapter greedy decode on a random-init Mistral-7B
-    architecture (32 layers, NF4 base linears, rank-16 adapters on all seven
-    projections), one adapter per row, prompts of 128 random token ids, 128
-    new tokens per row.  One GPU: batch 8 with 8 adapters; several GPUs:
-    data-parallel replicas (one process per GPU, no collective on the data
-    path) with batch 64 and 64 adapters each.  A step is one whole generation
-    (prefill + 127 graph-replayed decode steps), timed with CUDA events on
-    each rank, max over ranks; value = all ranks' new tokens / that time."""
-    import datetime
-
+def decode_measure(dev, world: int, rank: int, B: int, warm: int, steps: int) -> dict:
+    """Config 5 on this rank: mixed-adapter greedy decode on a random-init
+    Mistral-7B architecture (32 layers, NF4 base linears, rank-16 adapters on
+    all seven projections), one adapter per row (B rows, B adapters),
+    prompts of 128 random token ids, 128 new tokens per row.  A step is one
+    whole generation (prefill + 127 graph-replayed decode steps), timed with
+    CUDA events; returns this rank's times and the bytes a decode step must
+    move."""
     import torch
-    import torch.distributed as dist
 
     from persona import ops
     from persona.adapter_pool import AdapterPool
     from persona.engine import Request, StaticBatchEngine
     from persona.mistral import MistralConfig, MistralLoRAModel
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    if world != args.gpus:
-        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
-    B = args.batch or (8 if world == 1 else 64)
     D, prompt, new = B, 128, 128
     cfg = MistralConfig()
     pool = AdapterPool(max_slots=D, r=16, device=dev)
@@ -827,22 +864,11 @@ def run_e2e(args):
     gen = torch.Generator().manual_seed(SEED * 10 + rank)
     reqs = [Request(f"r{i}", f"persona{i % D}", torch.randint(0, cfg.vocab, (prompt,), generator=gen).tolist(),
                     slot=pool.name_to_slot[f"persona{i % D}"]) for i in range(B)]
-    # a step is a whole generation (~0.3 s): at most 10 timed, 3 to 20 warm-up
-    warm, steps = min(max(3, args.warmup), 20), min(max(1, args.steps), 10)
     for _ in range(warm):
         eng.run_static_generate(reqs, max_new_tokens=new)
-    if world > 1:
-        dist.barrier(device_ids=[local])
     torch.cuda.synchronize()
     runs = [eng.run_static_generate(reqs, max_new_tokens=new) for _ in range(steps)]
     ops.check_errors(dev)
-    ms = sum(r["prefill_ms"] + r["decode_ms"] for r in runs) / steps
-    pre = sum(r["prefill_ms"] for r in runs) / steps
-    dec = sum(r["decode_ms"] for r in runs) / steps
-    t = torch.tensor([ms, pre, dec], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms, pre, dec = (float(v) for v in t.tolist())
     # bytes one decode step must stream: the NF4 base weights and the LM head,
     # the adapters the batch uses (all 7 projections, 32 layers) and the KV
     # cache at the mean length
@@ -853,24 +879,70 @@ def run_e2e(args):
         (cfg.hidden, cfg.intermediate), (cfg.hidden, cfg.intermediate), (cfg.intermediate, cfg.hidden)))
     per_step += lora_per_adapter * cfg.num_layers * len({q.slot for q in reqs})
     per_step += B * cfg.num_layers * 2 * cfg.kv_dim * 2 * (prompt + new / 2)
-    step_ms = dec / (new - 1)
+    out = {
+        "ms": sum(r_["prefill_ms"] + r_["decode_ms"] for r_ in runs) / steps,
+        "prefill_ms": sum(r_["prefill_ms"] for r_ in runs) / steps,
+        "decode_ms": sum(r_["decode_ms"] for r_ in runs) / steps,
+        "bytes_per_decode_step": per_step, "B": B, "D": D, "prompt": prompt, "new": new,
+        "launches_per_decode_step": 13 * cfg.num_layers + 5,
+    }
+    del eng, model, pool
+    torch.cuda.empty_cache()
+    return out
+
+
+def decode_line(m: dict, world: int, steps: int, warm: int) -> dict:
     peak, _ = load_peaks()
+    step_ms = m["decode_ms"] / (m["new"] - 1)
+    return {
+        "workload": "e2e_decode", "metric": "mixed-adapter decode tokens/s",
+        "value": world * m["B"] * m["new"] / (m["ms"] * 1e-3), "unit": "tokens/s", "n_gpus": world,
+        "steps": steps, "warmup": warm, "ms_per_step": m["ms"], "higher_is_better": True, "scaling": "weak",
+        "dtype": "f16 (NF4 base weights)", "data": "synthetic: random-init weights and adapters, random ids",
+        "config": {"workload": "Mistral-7B architecture, 32 layers, NF4 base, rank-16 adapters on q/k/v/o/"
+                               "gate/up/down, greedy", "batch_per_gpu": m["B"], "adapters": m["D"],
+                   "prompt_tokens": m["prompt"], "new_tokens": m["new"],
+                   "parallelism": f"dp{world} replicas" if world > 1 else "1 GPU"},
+        "prefill_ms": m["prefill_ms"], "decode_ms": m["decode_ms"], "decode_ms_per_token_step": step_ms,
+        "decode_tokens_per_s": world * m["B"] / (step_ms * 1e-3),
+        "roofline": {"bound": "hbm", "bytes_per_decode_step": m["bytes_per_decode_step"],
+                     "achieved": m["bytes_per_decode_step"] / (step_ms * 1e-3) / 1e9, "peak": peak, "unit": "GB/s",
+                     "frac": m["bytes_per_decode_step"] / (step_ms * 1e-3) / 1e9 / peak},
+        "gpu_launches_per_decode_step": m["launches_per_decode_step"],
+    }
+
+
+def run_e2e(args):
+    """Config 5 alone (see decode_measure).  One GPU: batch 8 with 8
+    adapters; several GPUs: data-parallel replicas (one process per GPU, no
+    collective on the data path) with batch 64 and 64 adapters each; value =
+    all ranks' new tokens / the max over ranks of the generation time."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
+    B = args.batch or (8 if world == 1 else 64)
+    # a step is a whole generation (~0.3 s): at most 10 timed, 3 to 20 warm-up
+    warm, steps = min(max(3, args.warmup), 20), min(max(1, args.steps), 10)
+    if world > 1:
+        dist.barrier(device_ids=[local])
+    m = decode_measure(dev, world, rank, B, warm, steps)
+    t = torch.tensor([m["ms"], m["prefill_ms"], m["decode_ms"]], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    m["ms"], m["prefill_ms"], m["decode_ms"] = (float(v) for v in t.tolist())
     if rank == 0:
-        print(json.dumps({
-            "workload": "e2e_decode", "metric": "mixed-adapter decode tokens/s",
-            "value": world * B * new / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world, "steps": steps,
-            "warmup": warm, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-            "dtype": "f16 (NF4 base weights)", "data": "synthetic: random-init weights and adapters, random ids",
-            "config": {"workload": "Mistral-7B architecture, 32 layers, NF4 base, rank-16 adapters on q/k/v/o/"
-                                   "gate/up/down, greedy", "batch_per_gpu": B, "adapters": D,
-                       "prompt_tokens": prompt, "new_tokens": new,
-                       "parallelism": f"dp{world} replicas" if world > 1 else "1 GPU"},
-            "prefill_ms": pre, "decode_ms": dec, "decode_ms_per_token_step": step_ms,
-            "roofline": {"bound": "hbm", "bytes_per_decode_step": per_step,
-                         "achieved": per_step / (step_ms * 1e-3) / 1e9, "peak": peak, "unit": "GB/s",
-                         "frac": per_step / (step_ms * 1e-3) / 1e9 / peak},
-            "gpu_launches_per_decode_step": 13 * cfg.num_layers + 5,
-        }), flush=True)
+        print(json.dumps(decode_line(m, world, steps, warm)), flush=True)
     if world > 1:
         dist.barrier(device_ids=[local])
         dist.destroy_process_group()

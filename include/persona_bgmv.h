@@ -18,7 +18,7 @@
  * The LoRA scale alpha/r is folded into b_pool by the pool loader; no op
  * takes a scale.  All base pointers must be 16-byte aligned and K, N, ldx,
  * ldy and the strides multiples of 8 (the reference's own preconditions,
- * csrc/bgmv_shrink.cu:100-104, csrc/bgmv_expand.cu:229-233).
+ * csrc/bgmv_shrink.cu:100-104, csrc/bgmv_expand.cu:107-111).
  */
 #ifndef PERSONA_BGMV_H
 #define PERSONA_BGMV_H
@@ -53,6 +53,9 @@ extern "C" {
 #define PERSONA_DEV_ERR_SLOT 1    /* a slot < -1 or >= S: that row was left alone */
 #define PERSONA_DEV_ERR_TIMEOUT 2 /* a bounded wait gave up                       */
 #define PERSONA_DEV_ERR_SEGMENT 4 /* SGMV segment table out of order or range     */
+#define PERSONA_DEV_ERR_PLAN 8    /* PERSONA_REUSE_PLAN: the workspace holds no plan
+                                     for this T and S (nothing was computed), or a
+                                     plan entry was out of range (that item skipped) */
 
 /* Flags of the BGMV ops. */
 #define PERSONA_REUSE_PLAN 1 /* workspace already holds the plan of these slots */
@@ -184,12 +187,14 @@ int persona_sgmv_fused(const void* x, int64_t ldx, const void* a_pool, int64_t a
 
 /* ---- fused BGMV without any allocation -----------------------------------
  * No reference counterpart.  Same operation, arguments and results as
- * persona_bgmv_fused, minus the workspace: the row-grouping plan lives in a
- * fixed device array inside this library (one per device), so the call
- * needs no buffer from the caller and allocates nothing itself.  It serves
- * callers that cannot hand out device memory per call: an engine that has
- * already carved all of HBM into its own pools (KV cache, adapter pool), or
- * a host binding with no device allocator of its own.
+ * persona_bgmv_fused, minus the workspace: the workspace (row-grouping plan,
+ * the split kernel's partial sums and counters) lives in a fixed device
+ * array inside this library, one per device, about 6.7 MB, held by every
+ * GPU that loads the library until the process exits.  The call needs no
+ * buffer from the caller and allocates nothing itself.  It serves callers
+ * that cannot hand out device memory per call: an engine that has already
+ * carved all of HBM into its own pools (KV cache, adapter pool), or a host
+ * binding with no device allocator of its own.
  * Limits and rules:
  *  - T <= PERSONA_NOALLOC_MAX_ROWS; a larger T returns
  *    PERSONA_ERR_NOALLOC_ROWS and enqueues nothing.
@@ -197,7 +202,9 @@ int persona_sgmv_fused(const void* x, int64_t ldx, const void* a_pool, int64_t a
  *    (cudaGetSymbolAddress, with that device current); make that first call
  *    before any stream capture begins.
  *  - Nothing in the array has to start at zero: each call rewrites the plan
- *    before the kernel reads it.
+ *    and resets the counters before the kernel reads them.  Calls of at most
+ *    PERSONA_SMALL_MAX_ROWS rows run the decode-sized kernel and do not
+ *    touch the array.
  *  - All calls on one device share the array: calls whose device work can
  *    overlap (different streams, unsynchronised threads) race and must be
  *    serialised, e.g. on one stream.                                        */

@@ -99,4 +99,11 @@ cudaError_t launch_sgmv_tc(int mode, int dtype, int R, const CUtensorMap& tx, co
                            cudaStream_t st);
 cudaError_t launch_gemv_fp16(const void* x, const void* W, void* y, int K, int N, cudaStream_t st);
 
+// persona_bgmv_fused (capi.cu); plan_small = false: no plan on the
+// decode-sized path, whose kernel reads none.
+int fused_impl(const void* x, int64_t ldx, const void* a_pool, int64_t a_slot_stride, int64_t a_row_stride,
+               const void* b_pool, int64_t b_slot_stride, const int32_t* slots, void* y, int64_t ldy, int64_t T,
+               int64_t K, int64_t N, int64_t R, int64_t S, int dtype, void* workspace, size_t workspace_bytes,
+               int flags, int32_t* dev_err, cudaStream_t stream, bool plan_small);
+
 }  // namespace persona

@@ -51,6 +51,10 @@ __global__ void __launch_bounds__(THREADS)
   __shared__ int s_counts[4];  // valid, null, bad, items (running over chunks)
 
   const int tid = threadIdx.x;
+  // The BGMV kernel after this one is launched as a programmatic dependent:
+  // let it become resident and set up now; it reads the plan only after
+  // this kernel has completed (griddepcontrol.wait).
+  asm volatile("griddepcontrol.launch_dependents;");
   PlanView pv = plan_view(plan, T);
   if (tid < 4) s_counts[tid] = 0;
   init_work_state(plan, T, tid, THREADS);

@@ -41,6 +41,8 @@
 // into 16-bit hi and lo halves, both small swizzled shared-memory operands),
 // and a consumer thread per output column reads its 16 accumulators, adds y
 // and stores.  Rank 8 keeps the warp-MMA expand.
+#include <atomic>
+
 #include "bgmv_stages.cuh"
 #include "tcgen05.cuh"
 
@@ -89,6 +91,7 @@ struct SplitShared {
   ProbGeom geom[kMaxProblems];
   int units_s, units;
   uint32_t tmem;
+  int abort;  // set by the first wait of the CTA that gives up
 };
 
 constexpr int kSRingBytes = kSlots * kSlotBytes;
@@ -206,12 +209,21 @@ __device__ __forceinline__ void st_release(int* p, int v) {
   asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
-// Spin (bounded) until *p == want; false (and the timeout bit) if it never does.
-__device__ __forceinline__ bool wait_word(const int* p, int want, int32_t* err) {
+// Spin (bounded) until *p == want.  False if it never does (timeout bit,
+// CTA abort flag and the launch's abort word set) or if the CTA or the
+// launch has already given up.
+__device__ __forceinline__ bool wait_word(const int* p, int want, int32_t* err, int* abort, int* launch_abort) {
   if (ld_acquire(p) == want) return true;
+  volatile int* ab = abort;
   const long long t0 = clock64();
   while (ld_acquire(p) != want) {
+    if (*ab || ld_acquire(launch_abort) != 0) {
+      *ab = 1;
+      return false;
+    }
     if (clock64() - t0 > kWaitBudgetCycles) {
+      *ab = 1;
+      atomicExch(launch_abort, 1);
       raise_error(err, PERSONA_DEV_ERR_TIMEOUT);
       return false;
     }
@@ -222,6 +234,14 @@ __device__ __forceinline__ bool wait_word(const int* p, int want, int32_t* err) 
 
 }  // namespace
 
+// Failure handling.  Every wait is bounded and, through sh.abort, gives up
+// at once after any wait of the CTA gave up.  Roles leave their loops at a
+// unit boundary (the consumers decide together, so that their named
+// barriers stay matched); a stage whose wait failed is still walked through
+// but its slot is not released, so the producer never re-arms a slot whose
+// loads may still be landing.  The producer waits (bounded) for its own
+// loads before the CTA exits, and the MMA warp for its own MMAs before the
+// tensor memory is freed.
 template <typename DT, int R, int MODE>
 __global__ void __launch_bounds__(kSplitThreads, 1)
     bgmv_split_kernel(const __grid_constant__ SplitMaps maps, const SplitArgs args) {
@@ -244,10 +264,10 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
   PlanView pv = plan_view(args.ws, args.T);
   const int P = args.num_problems;
   WorkView wv = work_view(args.ws, args.T, P);
-  const int n_items = pv.hdr[kHdrItems];
-  const int epoch = wv.sync[kSyncEpoch];
   const int64_t tpad = plan_tpad(args.T);
 
+  // Prologue that touches no input: it may overlap the kernel before this
+  // one (launched as its programmatic dependent; normally the plan kernel).
   if (tid == 0) {
     for (int s = 0; s < kSlots; ++s) {
       mbar_init(&sm.full[s], 1);
@@ -262,17 +282,39 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
     mbar_init(sm.mma_fin, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (threadIdx.x == 0)
-    plan_units(sh, args, n_items, C::kKC, C::kNB, static_cast<int>(gridDim.x) * kGroups, kDoShrink, kDoExpand);
+  if (warp == kConsumerWarps && lane < P) {
+    if (kDoShrink) tma_prefetch_desc(&maps.a[lane]);
+    if (kDoExpand) tma_prefetch_desc(&maps.b[lane]);
+  }
   if (kTcE && grp == 0 && warp == kMmaWarp) {  // one allocation for both groups
     tc::tmem_alloc(&sh.tmem, kTmemCols);
     tc::tmem_relinquish();
+  }
+  // The plan, x, y and the shared counters may be written by the kernel
+  // before this one: nothing below reads them before it has completed.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  // With PERSONA_REUSE_PLAN the workspace is trusted only if its header is
+  // the plan of this T and S; every CTA reads the same header, so they all
+  // take the same branch.
+  const int n_items = pv.hdr[kHdrItems];
+  const bool plan_ok = pv.hdr[kHdrMagic] == kPlanMagic && pv.hdr[kHdrT] == args.T && pv.hdr[kHdrS] == args.S &&
+                       pv.hdr[kHdrRowsPerItem] == kRowsPerItem && n_items >= 0 && n_items <= tpad;
+  const int epoch = wv.sync[kSyncEpoch];
+  if (threadIdx.x == 0) {
+    sh.abort = 0;
+    if (plan_ok) {
+      plan_units(sh, args, n_items, C::kKC, C::kNB, static_cast<int>(gridDim.x) * kGroups, kDoShrink, kDoExpand);
+    } else {
+      sh.units_s = sh.units = 0;
+      if (blockIdx.x == 0) raise_error(args.err, PERSONA_DEV_ERR_PLAN);
+    }
   }
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tmem = sh.tmem + static_cast<uint32_t>(grp) * kGroupTmemCols;
   const int units_s = sh.units_s, units = sh.units;
+  int* const abort = &sh.abort;
 
   // Unit u -> (kind, problem, item, slice); [lo, hi) is the k range of a
   // shrink slice or the n range of an expand slice.
@@ -310,12 +352,10 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
     return d;
   };
 
-  if (warp == kConsumerWarps) {
+  if (!plan_ok) {
+    // nothing to do; fall through to the teardown (no counter is touched)
+  } else if (warp == kConsumerWarps) {
     // ------------------------------------------------------- producer --
-    if (lane < P) {
-      if (kDoShrink) tma_prefetch_desc(&maps.a[lane]);
-      if (kDoExpand) tma_prefetch_desc(&maps.b[lane]);
-    }
     // Claims run two units ahead: the atomic for unit j+2 is issued while
     // unit j streams and its result is first read one unit later, so the
     // round trip to L2 never stalls the loads.  The kernel issues no L2
@@ -326,27 +366,47 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
     auto claim_issue = [&]() -> int { return lane == 0 ? atomicAdd(&wv.sync[kSyncQueue], 1) : 0; };
     auto claim_read = [&](int pending) -> int { return __shfl_sync(0xffffffffu, pending, 0); };
     uint32_t g = 0;
+    // Arms the next ring slot for `bytes`; -1 if its wait gave up (the slot
+    // is then left alone).
     auto claim_slot = [&](uint32_t bytes) -> int {
       const int s = static_cast<int>(g % kSlots);
+      int ok = 1;
       if (lane == 0) {
-        if (g >= kSlots) mbar_wait(&sm.empty[s], ((g / kSlots) - 1) & 1, args.err);
-        mbar_arrive_expect_tx(&sm.full[s], bytes);
+        if (g >= kSlots) ok = mbar_wait_abortable(&sm.empty[s], ((g / kSlots) - 1) & 1, args.err, abort) ? 1 : 0;
+        if (ok && *reinterpret_cast<volatile int*>(abort)) ok = 0;
+        if (ok) mbar_arrive_expect_tx(&sm.full[s], bytes);
       }
-      __syncwarp();
-      return s;
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      return ok ? s : -1;
     };
     int u = claim_read(claim_issue());
     int pending = u < units ? claim_issue() : 0;
-    for (int j = 0;; ++j) {
+    bool dead = false;
+    for (int j = 0; !dead; ++j) {
       const Dec d = decode(u);
       const int iq = j % kUnitRing;
-      if (lane == 0 && j >= kUnitRing) mbar_wait(&sm.uempty[iq], ((j / kUnitRing) - 1) & 1, args.err);
-      __syncwarp();
+      int ok = 1;
+      if (lane == 0 && j >= kUnitRing)
+        ok = mbar_wait_abortable(&sm.uempty[iq], ((j / kUnitRing) - 1) & 1, args.err, abort) ? 1 : 0;
+      if (!__shfl_sync(0xffffffffu, ok, 0)) break;  // the other roles find no unit and give up too
       int4 it = make_int4(0, 0, 0, 0);
       int row = 0;
       if (d.kind != kUnitEnd) {
         it = pv.items[d.item];
-        row = lane < it.z ? pv.perm[it.y + lane] : 0;
+        // A plan from the plan kernels always passes; a damaged one turns
+        // the item into a no-op (no rows) instead of an access out of range.
+        bool good = it.x >= 0 && it.x < args.S && it.z >= 1 && it.z <= kRowsPerItem && it.y >= 0 &&
+                    it.y <= args.T - it.z;
+        if (good && lane < it.z) {
+          row = pv.perm[it.y + lane];
+          if (row < 0 || row >= args.T) good = false;
+        }
+        good = __all_sync(0xffffffffu, good);
+        if (!good) {
+          if (lane == 0 && d.slice == 0) raise_error(args.err, PERSONA_DEV_ERR_PLAN);
+          it = make_int4(0, it.y >= 0 && it.y < args.T ? it.y : 0, 0, 0);
+          row = 0;
+        }
       }
       UnitDesc* ud = &sm.units[iq];
       if (lane < kRowsPerItem) ud->rows[lane] = row;
@@ -376,6 +436,10 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
           const int nbox = (valid + 63) / 64;
           const uint32_t xb = static_cast<uint32_t>(valid) * 2u;
           const int s = claim_slot(static_cast<uint32_t>(nbox * C::kABoxBytes) + static_cast<uint32_t>(c) * xb);
+          if (s < 0) {
+            dead = true;
+            break;
+          }
           uint8_t* st = sm.ring + s * kSlotBytes;
           if (lane == 0)
             for (int b = 0; b < nbox; ++b)
@@ -389,16 +453,24 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
         const int stage_rows = sh.geom[d.prob].stage_rows;
         if (MODE == kModeExpand) {
           const int s = claim_slot(static_cast<uint32_t>(c * R * 4));
-          if (lane < c)
-            bulk_load(sm.ring + s * kSlotBytes + lane * R * 4, args.v_in + static_cast<int64_t>(row) * R, R * 4,
-                      &sm.full[s]);
-          ++g;
+          if (s < 0) {
+            dead = true;
+          } else {
+            if (lane < c)
+              bulk_load(sm.ring + s * kSlotBytes + lane * R * 4, args.v_in + static_cast<int64_t>(row) * R, R * 4,
+                        &sm.full[s]);
+            ++g;
+          }
         }
-        for (int n0 = d.lo; n0 < d.hi; n0 += stage_rows) {
+        for (int n0 = d.lo; !dead && n0 < d.hi; n0 += stage_rows) {
           const int rows_here = min(stage_rows, d.hi - n0);
           const int nbox = (rows_here + pr.n_box - 1) / pr.n_box;
           const uint32_t yb = static_cast<uint32_t>(rows_here) * 2u;
           const int s = claim_slot(static_cast<uint32_t>(nbox * pr.n_box * 2 * R) + static_cast<uint32_t>(c) * yb);
+          if (s < 0) {
+            dead = true;
+            break;
+          }
           uint8_t* st = sm.ring + s * kSlotBytes;
           if (lane == 0)
             for (int b = 0; b < nbox; ++b)
@@ -411,6 +483,11 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
       }
       u = u_next;
     }
+    // Every copy this warp issued lands before the CTA exits (normally the
+    // consumers have waited for all of them already).
+    if (lane == 0)
+      for (int s = 0; s < kSlots; ++s)
+        if (g > static_cast<uint32_t>(s)) mbar_wait(&sm.full[s], ((g - 1 - s) / kSlots) & 1, args.err);
     __syncwarp();
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA --
@@ -421,9 +498,10 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
     if (lane == 0) {
       uint32_t g = 0, ue = 0;
       const uint32_t vop = smem_u32(sm.vop);
-      for (int j = 0;; ++j) {
+      bool dead = false;
+      for (int j = 0; !dead; ++j) {
         const int iq = j % kUnitRing;
-        mbar_wait(&sm.ufull[iq], (j / kUnitRing) & 1, args.err);
+        if (!mbar_wait_abortable(&sm.ufull[iq], (j / kUnitRing) & 1, args.err, abort)) break;
         const int kind = sm.units[iq].kind, prob = sm.units[iq].prob, slice = sm.units[iq].slice;
         if (kind == kUnitEnd) break;
         const ProbGeom& gg = sh.geom[prob];
@@ -437,20 +515,23 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
           nst = (hi - lo + gg.stage_rows - 1) / gg.stage_rows;
           if (MODE == kModeExpand) {  // the v stage
             const int s = static_cast<int>(g % kSlots);
-            mbar_wait(&sm.full[s], (g / kSlots) & 1, args.err);
+            if (!mbar_wait_abortable(&sm.full[s], (g / kSlots) & 1, args.err, abort)) break;
             mbar_arrive(&sm.mma_done[s]);
             ++g;
           }
         }
         const bool tc_unit = kTcE && kind == kUnitExpand;
         if (tc_unit) {
-          mbar_wait(sm.vready, ue & 1, args.err);
+          if (!mbar_wait_abortable(sm.vready, ue & 1, args.err, abort)) break;
           tc::fence_after_sync();
           ++ue;
         }
         for (int i = 0; i < nst; ++i, ++g) {
           const int s = static_cast<int>(g % kSlots);
-          mbar_wait(&sm.full[s], (g / kSlots) & 1, args.err);
+          if (!mbar_wait_abortable(&sm.full[s], (g / kSlots) & 1, args.err, abort)) {
+            dead = true;
+            break;
+          }
           if (tc_unit) {
             tc::fence_after_sync();
             const int rows_here = min(gg.stage_rows, hi - (lo + i * gg.stage_rows));
@@ -471,7 +552,7 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
             mbar_arrive(&sm.mma_done[s]);
           }
         }
-        mbar_arrive(&sm.uempty[iq]);
+        if (!dead) mbar_arrive(&sm.uempty[iq]);
       }
       // Every MMA this thread issued completes before TMEM is released.
       tc::commit(sm.mma_fin);
@@ -492,7 +573,9 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
     uint32_t g = 0;
     for (int j = 0;; ++j) {
       const int iq = j % kUnitRing;
-      mbar_wait(&sm.ufull[iq], (j / kUnitRing) & 1, args.err);
+      const bool got = mbar_wait_abortable(&sm.ufull[iq], (j / kUnitRing) & 1, args.err, abort);
+      // all four consumer warps go on, or none does
+      if (!named_all(bar_cons, kConsumers, got && *reinterpret_cast<volatile int*>(abort) == 0)) break;
       const UnitDesc* ud = &sm.units[iq];
       const int kind = ud->kind;
       if (kind == kUnitEnd) break;
@@ -512,7 +595,7 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
           for (int i = 0; i < 4; ++i) d[t][0][i] = d[t][1][i] = 0.f;
         for (int k0 = klo; k0 < khi; k0 += C::kKC, ++g) {
           const int s = static_cast<int>(g % kSlots);
-          mbar_wait(&sm.full[s], (g / kSlots) & 1, args.err);
+          const bool ok = mbar_wait_abortable(&sm.full[s], (g / kSlots) & 1, args.err, abort);
           uint8_t* st = sm.ring + s * kSlotBytes;
           const int valid = min(C::kKC, khi - k0);
           if (valid & 63) {
@@ -527,7 +610,7 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
           }
           shrink_stage<DT, R>(st, ((valid + 63) / 64) * 4, warp, lane, d);
           __syncwarp();
-          if (lane == 0) mbar_arrive_relaxed(&sm.empty[s]);
+          if (lane == 0 && ok) mbar_arrive_relaxed(&sm.empty[s]);
         }
         // This slice's partial v: sum the two accumulators and the warps that
         // split k for each rank tile.
@@ -610,14 +693,14 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
         float* vfb = sm.vf;
         if (MODE == kModeExpand) {
           const int s = static_cast<int>(g % kSlots);
-          mbar_wait(&sm.full[s], (g / kSlots) & 1, args.err);
+          const bool ok = mbar_wait_abortable(&sm.full[s], (g / kSlots) & 1, args.err, abort);
           const float* vs = reinterpret_cast<const float*>(sm.ring + s * kSlotBytes);
           for (int e = tid; e < E; e += kConsumers) vfb[e] = vs[e];
           __syncwarp();
-          if (lane == 0) mbar_arrive_relaxed(&sm.empty[s]);
+          if (lane == 0 && ok) mbar_arrive_relaxed(&sm.empty[s]);
           ++g;
         } else {
-          if (tid == 0) wait_word(wv.ready + prob * tpad + item, epoch, args.err);
+          if (tid == 0) wait_word(wv.ready + prob * tpad + item, epoch, args.err, abort, &wv.sync[kSyncAbort]);
           named_sync(bar_cons, kConsumers);
           const float* vfin = wv.vfinal + (static_cast<int64_t>(prob) * tpad + pos) * R;
           for (int e = tid; e < E; e += kConsumers) vfb[e] = __ldcg(vfin + e);
@@ -670,8 +753,8 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
           const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
           for (int n0 = nlo; n0 < nhi; n0 += stage_rows, ++g) {
             const int s = static_cast<int>(g % kSlots);
-            mbar_wait(&sm.full[s], (g / kSlots) & 1, args.err);
-            mbar_wait(&sm.mma_done[s], (g / kSlots) & 1, args.err);
+            bool ok = mbar_wait_abortable(&sm.full[s], (g / kSlots) & 1, args.err, abort);
+            ok = mbar_wait_abortable(&sm.mma_done[s], (g / kSlots) & 1, args.err, abort) && ok;
             __syncwarp();
             tc::fence_after_sync();
             const int rows_here = min(stage_rows, nhi - n0);
@@ -696,7 +779,7 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
             }
             tc::fence_before_sync();
             __syncwarp();
-            if (lane == 0) mbar_arrive_relaxed(&sm.empty[s]);
+            if (lane == 0 && ok) mbar_arrive_relaxed(&sm.empty[s]);
 #pragma unroll
             for (int b = 0; b < 2; ++b) {
               const int n = n0 + b * 128 + quarter * 32 + lane;
@@ -712,10 +795,10 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
           v_fragments<DT, R>(vfb, scale_down, lane, vhi, vlo);
           for (int n0 = nlo; n0 < nhi; n0 += stage_rows, ++g) {
             const int s = static_cast<int>(g % kSlots);
-            mbar_wait(&sm.full[s], (g / kSlots) & 1, args.err);
+            const bool ok = mbar_wait_abortable(&sm.full[s], (g / kSlots) & 1, args.err, abort);
             const int rows_here = min(stage_rows, nhi - n0);
             expand_stage<DT, R>(sm.ring + s * kSlotBytes, vhi, vlo, rows_here, pr.n_box, n0, c, rows, y, pr.ldy,
-                                scale_up, warp, lane, &sm.empty[s]);
+                                scale_up, warp, lane, ok ? &sm.empty[s] : nullptr);
           }
         }
         named_sync(bar_cons, kConsumers);
@@ -725,17 +808,24 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
     }
   }
   // The last CTA to finish resets the claim counter and bumps the epoch for
-  // the next launch on this workspace.
+  // the next launch on this workspace; after a launch in which a CTA gave up
+  // it also clears the per-item counters and ready words, so the next launch
+  // starts clean.
   tc::fence_before_sync();
   __syncthreads();
   if (kTcE && grp == 0 && warp == kMmaWarp) {
     tc::fence_after_sync();
     tc::tmem_dealloc(sh.tmem, kTmemCols);
   }
-  if (threadIdx.x == 0) {
+  if (threadIdx.x == 0 && plan_ok) {
+    if (sh.abort) atomicExch(&wv.sync[kSyncAbort], 1);
     __threadfence();
     if (atomicAdd(&wv.sync[kSyncDone], 1) == static_cast<int>(gridDim.x) - 1) {
       __threadfence();
+      if (ld_acquire(&wv.sync[kSyncAbort]) != 0) {
+        for (int64_t i = 0; i < 2 * kMaxProblems * tpad; ++i) wv.s_cnt[i] = 0;  // s_cnt, then ready
+        wv.sync[kSyncAbort] = 0;
+      }
       wv.sync[kSyncQueue] = 0;
       wv.sync[kSyncDone] = 0;
       wv.sync[kSyncEpoch] = epoch + 1 > 0 ? epoch + 1 : 1;
@@ -759,12 +849,14 @@ template <typename DT, int R, int MODE>
 static cudaError_t split_launch(const SplitMaps& maps, const SplitArgs& a, cudaStream_t stream) {
   auto kern = bgmv_split_kernel<DT, R, MODE>;
   constexpr int kMaxDev = 64;
-  static int ctas[kMaxDev] = {};
+  // CTAs per device (one per SM); racing first calls compute the same value
+  static std::atomic<int> ctas[kMaxDev];
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= kMaxDev) return cudaErrorInvalidDevice;
-  if (ctas[dev] == 0) {
+  int grid = ctas[dev].load(std::memory_order_acquire);
+  if (grid == 0) {
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSplitSmemBytes);
     if (e != cudaSuccess) return e;
     int per_sm = 0, sms = 0;
@@ -772,9 +864,24 @@ static cudaError_t split_launch(const SplitMaps& maps, const SplitArgs& a, cudaS
     if (e != cudaSuccess) return e;
     e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     if (e != cudaSuccess) return e;
-    ctas[dev] = (per_sm > 0 ? per_sm : 1) * sms;
+    grid = (per_sm > 0 ? per_sm : 1) * sms;
+    ctas[dev].store(grid, std::memory_order_release);
   }
-  kern<<<ctas[dev], kSplitThreads, kSplitSmemBytes, stream>>>(maps, a);
+  // Programmatic dependent of the kernel before it (normally the plan
+  // kernel, which lets its dependents start at once): the CTAs set up their
+  // barriers and tensor memory while it runs, then wait for it to complete.
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kSplitThreads);
+  cfg.dynamicSmemBytes = kSplitSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, kern, maps, a);
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 

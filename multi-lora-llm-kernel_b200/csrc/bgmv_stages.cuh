@@ -91,7 +91,8 @@ __device__ __forceinline__ void shrink_stage(const uint8_t* stage, int ksteps, i
 // One B stage: for each 8-column tile this warp owns,
 // y[row][n] = round(y_tile[row][n] + scale * (v_hi + v_lo)[row] . B[n]).
 // The slot is released (relaxed arrive on `empty`) as soon as its data is in
-// registers, before the y stores, so that no arrive waits on global stores.
+// registers, before the y stores, so that no arrive waits on global stores;
+// `empty` is null when the stage's wait gave up (the slot stays held).
 template <typename DT, int R>
 __device__ __forceinline__ void expand_stage(const uint8_t* stage, const uint32_t (&vhi)[RankCfg<R>::kKSteps][4],
                                              const uint32_t (&vlo)[RankCfg<R>::kKSteps][4], int rows_here,
@@ -165,7 +166,7 @@ __device__ __forceinline__ void expand_stage(const uint8_t* stage, const uint32_
   const int row0 = g < c ? static_cast<int>(lds32(smem_u32(rows + g))) : 0;
   const int row1 = g + 8 < c ? static_cast<int>(lds32(smem_u32(rows + g + 8))) : 0;
   __syncwarp();
-  if (lane == 0) mbar_arrive_relaxed(empty);
+  if (lane == 0 && empty != nullptr) mbar_arrive_relaxed(empty);
 #pragma unroll
   for (int ti = 0; ti < kMT; ++ti) {
     const int tile = warp + ti * kConsumerWarps;

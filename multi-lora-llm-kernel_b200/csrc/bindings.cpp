@@ -70,6 +70,7 @@ std::string describe_error(int bits) {
   if (bits & PERSONA_DEV_ERR_SLOT) os << " slot out of range;";
   if (bits & PERSONA_DEV_ERR_TIMEOUT) os << " device wait timed out;";
   if (bits & PERSONA_DEV_ERR_SEGMENT) os << " invalid segment table;";
+  if (bits & PERSONA_DEV_ERR_PLAN) os << " reused plan does not match the call;";
   return os.str();
 }
 

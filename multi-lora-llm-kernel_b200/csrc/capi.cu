@@ -123,10 +123,10 @@ int check_b(const void* b_pool, int64_t b_slot_stride, const void* y, int64_t ld
             int64_t R) {
   if (b_pool == nullptr || y == nullptr) return PERSONA_ERR_INVALID_ARG;
   if (N <= 0 || N > kI32Max) return PERSONA_ERR_SHAPE;
-  if (!rank_supported(R)) return PERSONA_ERR_RANK;       // csrc/bgmv_expand.cu:190-205
-  if (N % 8 != 0) return PERSONA_ERR_SHAPE;              // csrc/bgmv_expand.cu:229
+  if (!rank_supported(R)) return PERSONA_ERR_RANK;       // csrc/bgmv_expand.cu:68-83
+  if (N % 8 != 0) return PERSONA_ERR_SHAPE;              // csrc/bgmv_expand.cu:107
   if (ldy < N || b_slot_stride < N * R) return PERSONA_ERR_SHAPE;
-  if (!aligned16(b_pool) || !aligned16(y)) return PERSONA_ERR_ALIGNMENT;  // :230-233
+  if (!aligned16(b_pool) || !aligned16(y)) return PERSONA_ERR_ALIGNMENT;  // :108-111
   if (ldy % 8 || b_slot_stride % 8) return PERSONA_ERR_ALIGNMENT;
   return PERSONA_OK;
 }
@@ -314,12 +314,15 @@ int persona_bgmv_expand(const float* v, const void* b_pool, int64_t b_slot_strid
   return run_split(kModeExpand, dtype, R, maps, a, stream);
 }
 
-int persona_bgmv_fused(const void* x, int64_t ldx, const void* a_pool, int64_t a_slot_stride,
-                       int64_t a_row_stride, const void* b_pool, int64_t b_slot_stride,
-                       const int32_t* slots, void* y, int64_t ldy, int64_t T, int64_t K,
-                       int64_t N, int64_t R, int64_t S, int dtype, void* workspace,
-                       size_t workspace_bytes, int flags, int32_t* dev_err,
-                       cudaStream_t stream) {
+}  // extern "C"
+
+namespace persona {
+// persona_bgmv_fused; plan_small = false skips the plan on the decode-sized
+// path (whose kernel reads no plan), for callers that keep no plan around.
+int fused_impl(const void* x, int64_t ldx, const void* a_pool, int64_t a_slot_stride, int64_t a_row_stride,
+               const void* b_pool, int64_t b_slot_stride, const int32_t* slots, void* y, int64_t ldy, int64_t T,
+               int64_t K, int64_t N, int64_t R, int64_t S, int dtype, void* workspace, size_t workspace_bytes,
+               int flags, int32_t* dev_err, cudaStream_t stream, bool plan_small) {
   if (flags & ~(PERSONA_REUSE_PLAN | PERSONA_SPLIT_ONLY)) return PERSONA_ERR_INVALID_ARG;
   int st = check_common(T, S, dtype, workspace, workspace_bytes, slots);
   if (st != PERSONA_OK) return st;
@@ -329,7 +332,7 @@ int persona_bgmv_fused(const void* x, int64_t ldx, const void* a_pool, int64_t a
   if ((st = check_b(b_pool, b_slot_stride, y, ldy, N, R)) != PERSONA_OK) return st;
   if (K < 64) return PERSONA_ERR_SHAPE;
   if (small_path(T, flags, &K, 1)) {
-    if ((st = plan_if_needed(slots, T, S, workspace, flags, dev_err, stream)) != PERSONA_OK) return st;
+    if (plan_small && (st = plan_if_needed(slots, T, S, workspace, flags, dev_err, stream)) != PERSONA_OK) return st;
     const persona_bgmv_problem one = {x, ldx, a_pool, a_slot_stride, a_row_stride, b_pool, b_slot_stride,
                                       y, ldy, K, N};
     return run_small(&one, 1, slots, T, R, S, dtype, dev_err, stream);
@@ -355,6 +358,20 @@ int persona_bgmv_fused(const void* x, int64_t ldx, const void* a_pool, int64_t a
   a.T = static_cast<int>(T);
   a.S = static_cast<int>(S);
   return run_split(kModeFused, dtype, R, maps, a, stream);
+}
+
+}  // namespace persona
+
+extern "C" {
+
+int persona_bgmv_fused(const void* x, int64_t ldx, const void* a_pool, int64_t a_slot_stride,
+                       int64_t a_row_stride, const void* b_pool, int64_t b_slot_stride,
+                       const int32_t* slots, void* y, int64_t ldy, int64_t T, int64_t K,
+                       int64_t N, int64_t R, int64_t S, int dtype, void* workspace,
+                       size_t workspace_bytes, int flags, int32_t* dev_err,
+                       cudaStream_t stream) {
+  return persona::fused_impl(x, ldx, a_pool, a_slot_stride, a_row_stride, b_pool, b_slot_stride, slots, y, ldy, T, K,
+                             N, R, S, dtype, workspace, workspace_bytes, flags, dev_err, stream, true);
 }
 
 size_t persona_bgmv_multi_workspace_size(int64_t T, int num_problems) {

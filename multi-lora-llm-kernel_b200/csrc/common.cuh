@@ -129,6 +129,39 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int32_
   }
 }
 
+// Bounded wait that also gives up at once when *abort is set, i.e. when
+// another thread of the CTA has already given up; running out of budget sets
+// *abort.  A CTA whose pipeline broke therefore ends after one wait budget
+// instead of spending a full budget on every later wait.  A phase that has
+// completed is still reported as complete after an abort.
+__device__ __forceinline__ bool mbar_wait_abortable(uint64_t* bar, uint32_t parity, int32_t* err, int* abort) {
+  if (mbar_try_wait(bar, parity)) return true;
+  volatile int* ab = abort;
+  const long long t0 = clock64();
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*ab) return false;
+    if (clock64() - t0 > kWaitBudgetCycles) {
+      *ab = 1;
+      raise_error(err, PERSONA_DEV_ERR_TIMEOUT);
+      return false;
+    }
+  }
+}
+
+// True in every thread of named barrier `id` (nthreads threads) iff `v` is
+// true in all of them; also a barrier.
+__device__ __forceinline__ bool named_all(uint32_t id, uint32_t nthreads, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.and.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(v ? 1u : 0u), "r"(id), "r"(nthreads)
+      : "memory");
+  return r != 0;
+}
+
 // ------------------------------------------------------------------ TMA --
 
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {

@@ -340,6 +340,7 @@ __global__ void __launch_bounds__(kNf4Threads, MT == 1 ? 2 : 1)
   __shared__ uint64_t first_piece_bar;  // the compute warps have stored the first piece
   __shared__ uint32_t lut1[256];
   __shared__ int s_fin;
+  __shared__ int s_abort;  // set by the first wait of the CTA that gives up; later waits return at once
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t C = args.chunks;
   const int G = static_cast<int>(gridDim.x);
@@ -354,6 +355,7 @@ __global__ void __launch_bounds__(kNf4Threads, MT == 1 ? 2 : 1)
       mbar_init(&empty[s], kNf4Warps);
     }
     mbar_init(&first_piece_bar, kNf4Warps);
+    s_abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
@@ -378,7 +380,7 @@ __global__ void __launch_bounds__(kNf4Threads, MT == 1 ? 2 : 1)
       const int g0 = range_cta(C, G, t0), g1 = range_cta(C, G, t0 + sg.kt - 1);
       int* cnt = args.counters + pr.counter_base + sg.tile;
       int fin = 0;
-      if (lane == 0 && mbar_wait(&first_piece_bar, 0, args.err)) {
+      if (lane == 0 && mbar_wait_abortable(&first_piece_bar, 0, args.err, &s_abort)) {
         // the wait acquires the compute warps' piece stores; one cumulative
         // fence orders them before the count
         __threadfence();
@@ -421,7 +423,7 @@ __global__ void __launch_bounds__(kNf4Threads, MT == 1 ? 2 : 1)
           const int s = static_cast<int>(g % kSlots);
           if (g >= static_cast<uint32_t>(kSlots)) {
             if (!waited) flush();
-            if (!mbar_wait(&empty[s], ((g / kSlots) - 1) & 1, args.err)) {
+            if (!mbar_wait_abortable(&empty[s], ((g / kSlots) - 1) & 1, args.err, &s_abort)) {
               ok = false;
               break;
             }
@@ -464,7 +466,10 @@ __global__ void __launch_bounds__(kNf4Threads, MT == 1 ? 2 : 1)
       for (int mt = 0; mt < MT; ++mt) acc[mt][0] = acc[mt][1] = acc[mt][2] = acc[mt][3] = 0.f;
       for (int kc = sg.kc0; kc < sg.kc1; ++kc, ++g) {
         const int s = static_cast<int>(g % kSlots);
-        mbar_wait(&full[s], (g / kSlots) & 1, args.err);
+        // A failed wait (CTA gave up) still walks the chunk, so that the
+        // warps' barriers stay matched, but keeps the slot: the producer
+        // never re-arms a slot whose copies may still be landing.
+        const bool ok = mbar_wait_abortable(&full[s], (g / kSlots) & 1, args.err, &s_abort);
         const uint32_t st = smem_u32(cring + s * kNf4ChunkBytes);
         const uint4 c0 = lds128(st + ((warp * 2 + 0) * 32 + lane) * 16);
         const uint4 c1 = lds128(st + ((warp * 2 + 1) * 32 + lane) * 16);
@@ -522,7 +527,7 @@ __global__ void __launch_bounds__(kNf4Threads, MT == 1 ? 2 : 1)
           }
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[s]);
+        if (lane == 0 && ok) mbar_arrive(&empty[s]);
       }
       // D fragment: rows n0 = tile*128 + 16 warp + g8 (acc 0, 1) and n0 + 8
       // (acc 2, 3); x rows 8 mt + 2t and + 1.

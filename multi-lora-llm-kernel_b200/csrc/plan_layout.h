@@ -5,7 +5,7 @@
 //   word 8..    perm[T_pad]         int32 row indices
 //   then        items[T_pad]        int4 {slot, begin, count, 0}, 16-byte aligned
 //   then (each region starting on a 256-byte boundary)
-//   sync        kSyncWords words (claim counter, CTAs done, epoch), then
+//   sync        kSyncWords words (claim counter, CTAs done, epoch, abort), then
 //               s_cnt[kMaxProblems][T_pad] (shrink slices done per item) and
 //               ready[kMaxProblems][T_pad] (epoch at which v is complete)
 //   vfinal      fp32 [problems][T_pad][64]  v per plan position
@@ -42,6 +42,7 @@ constexpr int kSyncWords = 16;
 constexpr int kSyncQueue = 0;
 constexpr int kSyncDone = 1;
 constexpr int kSyncEpoch = 2;
+constexpr int kSyncAbort = 3;  // a CTA of the launch gave up a wait: the last CTA clears the counters
 constexpr int kPartSlots = 1024;
 constexpr int kPartFloats = 16 * 64;
 constexpr int kMaxProblems = 8;  // projections one split launch can carry

@@ -178,6 +178,8 @@ def check_errors(device: Optional[torch.device] = None, synchronize: bool = True
             what.append("device wait timed out")
         if bits & 4:
             what.append("invalid segment table")
+        if bits & 8:
+            what.append("reused plan does not match the call")
         raise RuntimeError(f"persona: device error 0x{bits:x}: {', '.join(what)}")
 
 

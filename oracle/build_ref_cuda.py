@@ -83,7 +83,9 @@ def build(reference: Path, force: bool = False) -> Path:
 
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("PERSONA_REFERENCE_DIR"),
+                    required="PERSONA_REFERENCE_DIR" not in os.environ,
+                    help="checkout of the reference repository (default: $PERSONA_REFERENCE_DIR)")
     ap.add_argument("--force", action="store_true")
     a = ap.parse_args()
     print(build(Path(a.reference), a.force))

@@ -56,7 +56,9 @@ def store16(a32: np.ndarray, dtype: str) -> np.ndarray:
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default=os.environ.get("PERSONA_REFERENCE", "/root/reference"))
+    ap.add_argument("--ref", default=os.environ.get("PERSONA_REFERENCE_DIR"),
+                    required="PERSONA_REFERENCE_DIR" not in os.environ,
+                    help="checkout of the reference repository (default: $PERSONA_REFERENCE_DIR)")
     args = ap.parse_args()
     ops = load_ref_ops(Path(args.ref))
     out = {}

@@ -42,7 +42,9 @@ def load_ref_pool(ref_root: Path):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default=os.environ.get("PERSONA_REFERENCE", "/root/reference"))
+    ap.add_argument("--ref", default=os.environ.get("PERSONA_REFERENCE_DIR"),
+                    required="PERSONA_REFERENCE_DIR" not in os.environ,
+                    help="checkout of the reference repository (default: $PERSONA_REFERENCE_DIR)")
     args = ap.parse_args()
     ref = load_ref_pool(Path(args.ref))
     out = {"adapter": {k: list(v) if isinstance(v, tuple) else v for k, v in ADAPTER.items()},

@@ -394,6 +394,45 @@ def test_c_abi_fused_and_planned():
     assert int(err.item()) == 0
 
 
+def test_c_abi_reused_plan_must_match_the_call():
+    """PERSONA_REUSE_PLAN on a workspace whose plan belongs to another batch
+    (a smaller T) or that was never planned: the split kernel checks the
+    plan header, flags PERSONA_DEV_ERR_PLAN and leaves y alone; the same
+    workspace then serves a normal call."""
+    lib = capi_lib.load()
+    T, T_other = 300, 100
+    wl = workloads.mixed_batch(seed=8, T=T, S=32, names=["q_proj"])
+    p = wl.projections[0]
+    x, a, b, sl = t16(p.x, "f16"), t16(p.a_pool, "f16"), t16(p.b_pool, "f16"), ti(wl.slots)
+    K, N, R, S = p.K, p.N, p.R, p.S
+    ws_bytes = lib.persona_bgmv_workspace_size(T)
+    stream = torch.cuda.current_stream().cuda_stream
+    PLAN_BIT = 8  # PERSONA_DEV_ERR_PLAN
+    for planned_rows in (T_other, None):
+        ws = torch.zeros(ws_bytes, dtype=torch.uint8, device=dev())
+        err = torch.zeros(1, dtype=torch.int32, device=dev())
+        if planned_rows is not None:
+            capi_lib.check(lib.persona_bgmv_plan(sl.data_ptr(), planned_rows, S, ws.data_ptr(), ws_bytes,
+                                                 err.data_ptr(), stream))
+        y = t16(p.y, "f16")
+        capi_lib.check(lib.persona_bgmv_fused(x.data_ptr(), K, a.data_ptr(), R * K, K, b.data_ptr(), N * R,
+                                              sl.data_ptr(), y.data_ptr(), N, T, K, N, R, S, capi_lib.F16,
+                                              ws.data_ptr(), ws_bytes, capi_lib.REUSE_PLAN, err.data_ptr(), stream))
+        torch.cuda.synchronize()
+        assert int(err.item()) & PLAN_BIT
+        assert np.array_equal(n16(y, "f16").view(np.uint16), p.y.view(np.uint16))
+        # the same workspace, planned by the call itself
+        err.zero_()
+        capi_lib.check(lib.persona_bgmv_fused(x.data_ptr(), K, a.data_ptr(), R * K, K, b.data_ptr(), N * R,
+                                              sl.data_ptr(), y.data_ptr(), N, T, K, N, R, S, capi_lib.F16,
+                                              ws.data_ptr(), ws_bytes, 0, err.data_ptr(), stream))
+        torch.cuda.synchronize()
+        assert int(err.item()) == 0
+        y_ref = p.y.copy()
+        O.bgmv_forward_ref(p.x, p.a_pool, p.b_pool, wl.slots, y=y_ref)
+        np.testing.assert_allclose(y.float().cpu().numpy(), y_ref.astype(np.float32), **TOL)
+
+
 def test_gemv_fp16():
     rng = np.random.default_rng(0)
     W = rng.standard_normal((300, 520)).astype(np.float16)

@@ -145,32 +145,51 @@ def test_multi_odd_shapes_and_strided_outputs_through_c_abi():
                                         0, err.data_ptr(), stream) == 1
 
 
+def _oracle_on_rows(rows, slots, x, a_pool, b_pool, y0, dtype="f16"):
+    """The oracle on a subset of rows: only the adapters those rows use are
+    copied from the device and widened (same math per row, far less CPU)."""
+    sl = slots[rows]
+    used = np.unique(sl[sl >= 0])
+    remap = np.full(int(slots.max()) + 2, -1, np.int32)
+    remap[used] = np.arange(len(used), dtype=np.int32)
+    sl_c = np.where(sl >= 0, remap[np.maximum(sl, 0)], -1).astype(np.int32)
+    idx = torch.from_numpy(used.astype(np.int64)).to(a_pool.device)
+    a_np = a_pool.index_select(0, idx).cpu().numpy()
+    b_np = b_pool.index_select(0, idx).cpu().numpy()
+    ri = torch.from_numpy(np.asarray(rows, np.int64)).to(x.device)
+    y_ref = y0.index_select(0, ri).cpu().numpy()
+    O.bgmv_forward_ref(x.index_select(0, ri).cpu().numpy(), a_np, b_np, sl_c, dtype, y=y_ref)
+    return y_ref
+
+
 def test_multi_full_size_mixed_decode_layer():
     """The seven projections at 512 rows, rank 64, 256 adapters (Zipf slots +
-    5% rows without adapter), fp16, generated on the device; each projection
-    of the one launch against bgmv_fused on it (which the full-size oracle
-    tests pin), and rows without adapter untouched."""
+    5% rows without adapter), fp16, generated on the device: every projection
+    of the one launch against the oracle (all rows of q/k/v/o, every third
+    row of gate/up/down), and rows without adapter untouched bit for bit."""
     rng = np.random.Generator(np.random.PCG64(4))
     T, R, S = 512, 64, 256
     slots = workloads.zipf_slots(rng, T, S)
     sd = torch.from_numpy(slots).to(dev())
     g = torch.Generator(device=dev()).manual_seed(4)
-    xs, a_s, b_s, ys = [], [], [], []
-    for K, N in workloads.PROJECTIONS.values():
+    names, xs, a_s, b_s, ys = [], [], [], [], []
+    for name, (K, N) in workloads.PROJECTIONS.items():
         lim = 1.0 / np.sqrt(K)
+        names.append(name)
         a_s.append(((torch.rand(S, R, K, generator=g, device=dev()) * 2 - 1) * lim).half())
         b_s.append((torch.randn(S, N, R, generator=g, device=dev()) * 0.04).half())
         xs.append(torch.randn(T, K, generator=g, device=dev()).half())
         ys.append(torch.randn(T, N, generator=g, device=dev()).half())
     y0 = [y.clone() for y in ys]
     ops.bgmv_fused_multi(xs, a_s, b_s, sd, ys)
-    null = torch.from_numpy(slots < 0).to(dev())
-    for i in range(len(xs)):
-        y1 = y0[i].clone()
-        ops.bgmv_fused(xs[i], a_s[i], b_s[i], sd, y1)
-        torch.testing.assert_close(ys[i].float(), y1.float(), **TOL)
-        assert torch.equal(ys[i][null], y0[i][null])
     ops.check_errors(dev())
+    null = torch.from_numpy(slots < 0).to(dev())
+    for i, name in enumerate(names):
+        rows = np.arange(T) if xs[i].shape[1] == 4096 and ys[i].shape[1] <= 4096 else np.arange(0, T, 3)
+        y_ref = _oracle_on_rows(rows, slots, xs[i], a_s[i], b_s[i], y0[i])
+        got = ys[i].index_select(0, torch.from_numpy(rows).to(dev())).float().cpu().numpy()
+        np.testing.assert_allclose(got, y_ref.astype(np.float32), err_msg=name, **TOL)
+        assert torch.equal(ys[i][null], y0[i][null]), name
 
 
 @pytest.mark.parametrize("dtype", ["f16", "bf16"])

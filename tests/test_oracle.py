@@ -126,3 +126,45 @@ def test_sgmv_slots_expand_segments_and_skip_bad_ones():
     # past the end
     assert O.sgmv_slots(np.array([0, 4, 12], np.int32), np.array([0, 1], np.int32), 10).tolist() == \
         [0] * 4 + [-1] * 6
+
+
+# ---- the torch restatement that bench.py's CPU legs time --------------------
+
+def _torch16(a, dtype):
+    import torch
+
+    a = np.ascontiguousarray(a)
+    if dtype == "f16":
+        return torch.from_numpy(a)
+    return torch.from_numpy(a.view(np.int16)).view(torch.bfloat16)
+
+
+@pytest.mark.parametrize("dtype", ["f16", "bf16"])
+@pytest.mark.parametrize("R", [8, 64])
+def test_torch_restatement_matches_reference(golden, dtype, R):
+    import torch
+
+    from oracle import bgmv_torch_ref as TR
+
+    c = _case(golden, f"shrink_{dtype}_r{R}")
+    v = TR.bgmv_shrink_ref(_torch16(c["x"], dtype), _torch16(c["a"], dtype), torch.from_numpy(c["slots"]))
+    np.testing.assert_allclose(v.numpy(), c["v"], rtol=1e-5, atol=1e-5)
+    c = _case(golden, f"expand_{dtype}_r{R}")
+    y = _torch16(c["y_in"].copy(), dtype)
+    TR.bgmv_expand_ref(torch.from_numpy(c["v"]), _torch16(c["b"], dtype), torch.from_numpy(c["slots"]), y)
+    got = y.numpy() if dtype == "f16" else y.view(torch.int16).numpy().view(np.uint16)
+    np.testing.assert_allclose(O.to_f32(got, dtype), O.to_f32(c["y_out"], dtype), rtol=1e-2, atol=1e-2)
+    null = c["slots"] < 0
+    assert np.array_equal(got[null].view(np.uint16), c["y_in"][null].view(np.uint16))
+
+
+def test_torch_restatement_forward_matches_reference(golden):
+    import torch
+
+    from oracle import bgmv_torch_ref as TR
+
+    c = _case(golden, "forward_f16")
+    y = torch.zeros(c["y"].shape, dtype=torch.float16)
+    TR.bgmv_forward_ref(torch.from_numpy(c["x"]), torch.from_numpy(c["a"]), torch.from_numpy(c["b"]),
+                        torch.from_numpy(c["slots"]), y)
+    np.testing.assert_allclose(y.float().numpy(), c["y"].astype(np.float32), rtol=1e-3, atol=1e-3)
