@@ -367,13 +367,14 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
     auto claim_read = [&](int pending) -> int { return __shfl_sync(0xffffffffu, pending, 0); };
     uint32_t g = 0;
     // Arms the next ring slot for `bytes`; -1 if its wait gave up (the slot
-    // is then left alone).
+    // is then left alone).  A slot is only ever released by consumers whose
+    // own wait for its loads succeeded, so a completed empty wait means the
+    // slot's previous loads have landed and re-arming it is safe.
     auto claim_slot = [&](uint32_t bytes) -> int {
       const int s = static_cast<int>(g % kSlots);
       int ok = 1;
       if (lane == 0) {
         if (g >= kSlots) ok = mbar_wait_abortable(&sm.empty[s], ((g / kSlots) - 1) & 1, args.err, abort) ? 1 : 0;
-        if (ok && *reinterpret_cast<volatile int*>(abort)) ok = 0;
         if (ok) mbar_arrive_expect_tx(&sm.full[s], bytes);
       }
       ok = __shfl_sync(0xffffffffu, ok, 0);

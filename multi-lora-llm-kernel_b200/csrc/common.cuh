@@ -129,22 +129,28 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int32_
   }
 }
 
-// Bounded wait that also gives up at once when *abort is set, i.e. when
-// another thread of the CTA has already given up; running out of budget sets
-// *abort.  A CTA whose pipeline broke therefore ends after one wait budget
-// instead of spending a full budget on every later wait.  A phase that has
-// completed is still reported as complete after an abort.
+// Bounded wait that also gives up when *abort is set, i.e. when another
+// thread of the CTA has already given up; running out of budget sets *abort.
+// A CTA whose pipeline broke therefore ends after about one wait budget
+// instead of spending a full budget on every later wait.  The flag is read
+// only once a wait has lasted kAbortPollCycles, so a wait that completes
+// normally costs what the plain bounded wait costs.  A phase that has
+// completed is reported as complete after an abort too.
+constexpr long long kAbortPollCycles = 1LL << 16;
 __device__ __forceinline__ bool mbar_wait_abortable(uint64_t* bar, uint32_t parity, int32_t* err, int* abort) {
   if (mbar_try_wait(bar, parity)) return true;
-  volatile int* ab = abort;
   const long long t0 = clock64();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (*ab) return false;
-    if (clock64() - t0 > kWaitBudgetCycles) {
-      *ab = 1;
-      raise_error(err, PERSONA_DEV_ERR_TIMEOUT);
-      return false;
+    const long long dt = clock64() - t0;
+    if (dt > kAbortPollCycles) {
+      volatile int* ab = abort;
+      if (*ab) return false;
+      if (dt > kWaitBudgetCycles) {
+        *ab = 1;
+        raise_error(err, PERSONA_DEV_ERR_TIMEOUT);
+        return false;
+      }
     }
   }
 }
