@@ -465,6 +465,14 @@ def run_ours(args):
 
     ms = max_over_ranks(ms_local)
     e2e_ms = max_over_ranks(e2e_ms_local)
+    # every rank's launch: rows, algorithmic bytes, mean launch time, fraction of HBM peak
+    mine = {"rank": rank, "rows": T, "adapters": int(np.unique(slots[slots >= 0]).size),
+            "bytes_per_launch": int(step_bytes), "launch_us": fused_ms_per_step * 1e3,
+            "frac": step_bytes / (fused_ms_per_step * 1e-3) / 1e9 / load_peaks()[0]}
+    per_rank = [mine]
+    if world > 1:
+        per_rank = [None] * world
+        dist.all_gather_object(per_rank, mine)
     total_bytes = sum_over_ranks(step_bytes)
     total_rows = sum_over_ranks(float((slots >= 0).sum()))
     fused_ms_max = max_over_ranks(fused_ms_per_step)
@@ -513,6 +521,7 @@ def run_ours(args):
             "gpu_launches": K_steps * 2,
             "clocks": clk,
             "fused_ms_per_step_max_rank": fused_ms_max,
+            "per_rank": per_rank,
         }
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline()

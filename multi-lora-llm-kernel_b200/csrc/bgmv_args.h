@@ -22,7 +22,10 @@ cudaError_t launch_shrink_rowwise(int dtype, const void* x, int64_t ldx, const v
                                   int32_t* err, cudaStream_t st);
 cudaError_t launch_sgmv_plan(const int32_t* indptr, const int32_t* seg_slots, int nseg, int T, int S,
                              int rows_per_item, int32_t* plan, int32_t* row_slots, int32_t* dev_err,
-                             cudaStream_t stream);
+                             cudaStream_t stream, int32_t* item_state = nullptr, int item_state_stride = 0);
+constexpr int kSgmvMaxCtas = 160;  // CTAs of a tensor-core SGMV launch (pieces are sized for it)
+// Bytes of the pieces region of the SGMV workspace (two pieces of 128 x 32 fp32 per CTA).
+constexpr size_t kSgmvPieceBytes = static_cast<size_t>(2) * kSgmvMaxCtas * 128 * 32 * 4;
 int bgmv_stage_rows(int R);  // B rows one ring slot holds at rank R
 // Split kernels (bgmv_split.cu): every item of every problem cut into K / N
 // slices claimed by all CTAs; workspace = bgmv_ws_bytes(T, problems)
@@ -91,6 +94,10 @@ struct SgmvTcArgs {
   int32_t* err;
   int T, K, N;  // N: output columns this launch computes, from column n0 of y and B
   int n0;
+  float* vfin;        // fused: [T, R] the items' v (workspace)
+  float* pieces;      // [2 * CTAs][128][R] partial v of items cut between CTAs (workspace)
+  int32_t* item_cnt;  // [items] pieces counted (zeroed by the plan kernel)
+  int32_t* item_ready;  // [items] 1 once the item's v is complete (zeroed by the plan kernel)
   int num_peers;                   // tensor parallel: other ranks' y (same layout as y)
   uint16_t* peers[kMaxTpPeers];    // that receive every finished tile
 };

@@ -198,7 +198,10 @@ template <int THREADS>
 __global__ void __launch_bounds__(THREADS)
     sgmv_plan_kernel(const int32_t* __restrict__ indptr, const int32_t* __restrict__ seg_slots, int nseg,
                      int T, int S, int rows_per_item, int32_t* __restrict__ plan, int32_t* __restrict__ row_slots,
-                     int32_t* dev_err) {
+                     int32_t* dev_err, int32_t* __restrict__ item_state, int item_state_stride) {
+  // The tensor-core kernel after this one is launched as a programmatic
+  // dependent: it may set up while this kernel runs.
+  asm volatile("griddepcontrol.launch_dependents;");
   // row_slots == nullptr: items and header only (the tensor-core kernels
   // read nothing else); otherwise also the per-row slots, the identity
   // permutation and the split kernels' shared state.
@@ -289,6 +292,13 @@ __global__ void __launch_bounds__(THREADS)
     }
     __syncthreads();
   }
+  // Per-item counter and ready word of the tensor-core kernel (two arrays
+  // item_state_stride words apart), zero for every item of this plan.
+  if (item_state != nullptr)
+    for (int i = tid; i < s_total_full + s_base[1]; i += THREADS) {
+      item_state[i] = 0;
+      item_state[item_state_stride + i] = 0;
+    }
   if (tid == 0) {
     pv.hdr[kHdrItems] = s_total_full + s_base[1];
     pv.hdr[kHdrValid] = 0;
@@ -304,9 +314,9 @@ __global__ void __launch_bounds__(THREADS)
 
 cudaError_t launch_sgmv_plan(const int32_t* indptr, const int32_t* seg_slots, int nseg, int T, int S,
                              int rows_per_item, int32_t* plan, int32_t* row_slots, int32_t* dev_err,
-                             cudaStream_t stream) {
+                             cudaStream_t stream, int32_t* item_state, int item_state_stride) {
   sgmv_plan_kernel<512><<<1, 512, 0, stream>>>(indptr, seg_slots, nseg, T, S, rows_per_item, plan, row_slots,
-                                               dev_err);
+                                               dev_err, item_state, item_state_stride);
   return cudaGetLastError();
 }
 

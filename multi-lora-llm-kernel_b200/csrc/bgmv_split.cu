@@ -89,6 +89,7 @@ struct ProbGeom {
 
 struct SplitShared {
   ProbGeom geom[kMaxProblems];
+  int sorder[kMaxProblems], eorder[kMaxProblems];  // problems in claim order (longest units first)
   int units_s, units;
   uint32_t tmem;
   int abort;  // set by the first wait of the CTA that gives up
@@ -99,8 +100,9 @@ constexpr int kSVopBytes = 2 * kRowsPerItem * kMaxR * 2;  // v hi / lo MMA opera
 constexpr int kSVBytes = kRowsPerItem * kMaxR * 4;
 constexpr int kSRedBytes = kRowsPerItem * kMaxR * 4;
 constexpr int kSUnitBytes = kUnitRing * static_cast<int>(sizeof(UnitDesc));
-constexpr int kSBarCount = 3 * kSlots + 2 * kUnitRing + 2;
-constexpr int kGroupSmemRaw = kSRingBytes + kSVopBytes + 2 * kSVBytes + kSRedBytes + kSUnitBytes + kSBarCount * 8 + 16;
+constexpr int kSBarCount = 3 * kSlots + 2 * kUnitRing + 2 + 4;
+constexpr int kGroupSmemRaw =
+    kSRingBytes + kSVopBytes + 4 * kSVBytes + kSRedBytes + kSUnitBytes + kSBarCount * 8 + 16;
 constexpr int kGroupSmem = (kGroupSmemRaw + 1023) / 1024 * 1024;
 constexpr int kSplitSmemBytes = kGroups * kGroupSmem + 1024;
 static_assert(kSplitSmemBytes <= 227 * 1024, "one CTA per SM");
@@ -109,7 +111,8 @@ struct SplitSmem {
   uint8_t* ring;
   uint8_t* vop;  // [hi | lo] expand operands (1024-aligned)
   float* pv;     // [16][R] this unit's partial / the item's v
-  float* vf;     // [16][R] the item's v for the expand
+  float* vf;     // [16][R] the item's v for the expand (separate expand op)
+  float* vbuf;   // [2][16][R] the items' v of the next fused expand units, copied in by the producer
   float* red;    // per-warp MMA tiles / maxima
   UnitDesc* units;
   uint64_t* full;
@@ -119,6 +122,8 @@ struct SplitSmem {
   uint64_t* mma_done;  // [kSlots] expand MMAs of the slot's stage complete
   uint64_t* vready;    // the expand unit's v operands are in shared memory
   uint64_t* mma_fin;   // every MMA of the pipeline complete (before TMEM is freed)
+  uint64_t* vfull;     // [2] vbuf[b] has landed
+  uint64_t* vempty;    // [2] the consumers are done with vbuf[b]
   int* flag;
 };
 
@@ -131,16 +136,19 @@ __device__ __forceinline__ SplitSmem carve(uint8_t* raw, int grp) {
   uint8_t* q = base + kSRingBytes + kSVopBytes;
   p.pv = reinterpret_cast<float*>(q);
   p.vf = reinterpret_cast<float*>(q + kSVBytes);
-  p.red = reinterpret_cast<float*>(q + 2 * kSVBytes);
-  p.units = reinterpret_cast<UnitDesc*>(q + 2 * kSVBytes + kSRedBytes);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(q + 2 * kSVBytes + kSRedBytes + kSUnitBytes);
+  p.vbuf = reinterpret_cast<float*>(q + 2 * kSVBytes);
+  p.red = reinterpret_cast<float*>(q + 4 * kSVBytes);
+  p.units = reinterpret_cast<UnitDesc*>(q + 4 * kSVBytes + kSRedBytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(q + 4 * kSVBytes + kSRedBytes + kSUnitBytes);
   p.full = bars;
   p.empty = bars + kSlots;
   p.ufull = bars + 2 * kSlots;
   p.uempty = bars + 2 * kSlots + kUnitRing;
   p.mma_done = bars + 2 * kSlots + 2 * kUnitRing;
-  p.vready = bars + 3 * kSlots + 2 * kUnitRing;
-  p.mma_fin = bars + 3 * kSlots + 2 * kUnitRing + 1;
+  p.vready = p.mma_done + kSlots;
+  p.mma_fin = p.vready + 1;
+  p.vfull = p.mma_fin + 1;
+  p.vempty = p.vfull + 2;
   p.flag = reinterpret_cast<int*>(bars + kSBarCount);
   return p;
 }
@@ -184,13 +192,22 @@ __device__ void plan_units(SplitShared& sh, const SplitArgs& a, int n_items, int
     g.nks = shrink ? (g.kst + g.ks_st - 1) / g.ks_st : 0;
     g.es_st = expand ? (g.nst + nes - 1) / nes : 0;
     g.nes = expand ? (g.nst + g.es_st - 1) / g.es_st : 0;
+  }
+  // Claim order inside each phase: problem by problem, the same order in
+  // both phases, so an expand unit's item was shrunk long before (ordering
+  // the phases by unit length instead made the first expand units wait for
+  // the last shrink units: 356 against 306 us per launch).
+  for (int q = 0; q < P; ++q) sh.sorder[q] = sh.eorder[q] = q;
+  for (int q = 0; q < P; ++q) {
+    ProbGeom& g = sh.geom[sh.sorder[q]];
     g.s_base = s_units;
     g.p_base = s_units;  // partial slots follow the shrink units one to one
     s_units += n_items * g.nks;
   }
-  for (int p = 0; p < P; ++p) {
-    sh.geom[p].e_base = s_units + e_units;
-    e_units += n_items * sh.geom[p].nes;
+  for (int q = 0; q < P; ++q) {
+    ProbGeom& g = sh.geom[sh.eorder[q]];
+    g.e_base = s_units + e_units;
+    e_units += n_items * g.nes;
   }
   sh.units_s = s_units;
   sh.units = s_units + e_units;
@@ -205,6 +222,14 @@ __device__ __forceinline__ int ld_acquire(const int* p) {
   asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
+__device__ __forceinline__ int ld_relaxed(const int* p) {
+  int v;
+  asm volatile("ld.relaxed.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+// Orders this thread's generic-proxy global accesses with async-proxy (bulk
+// copy) accesses of the same memory.
+__device__ __forceinline__ void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
 __device__ __forceinline__ void st_release(int* p, int v) {
   asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
@@ -280,6 +305,10 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
     }
     mbar_init(sm.vready, 1);
     mbar_init(sm.mma_fin, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&sm.vfull[b], 1);
+      mbar_init(&sm.vempty[b], 1);
+    }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == kConsumerWarps && lane < P) {
@@ -327,8 +356,8 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
     d.prob = d.item = d.slice = d.lo = d.hi = 0;
     if (u >= units) return d;
     if (u < units_s) {
-      int p = 0;
-      while (p + 1 < P && sh.geom[p + 1].s_base <= u) ++p;
+      int p = sh.sorder[0];
+      for (int q = 1; q < P && sh.geom[sh.sorder[q]].s_base <= u; ++q) p = sh.sorder[q];
       const ProbGeom& gg = sh.geom[p];
       const int v = u - gg.s_base;
       d.kind = kUnitShrink;
@@ -338,8 +367,8 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
       d.lo = d.slice * gg.ks_st * C::kKC;
       d.hi = min(args.prob[p].K, d.lo + gg.ks_st * C::kKC);
     } else {
-      int p = 0;
-      while (p + 1 < P && sh.geom[p + 1].e_base <= u) ++p;
+      int p = sh.eorder[0];
+      for (int q = 1; q < P && sh.geom[sh.eorder[q]].e_base <= u; ++q) p = sh.eorder[q];
       const ProbGeom& gg = sh.geom[p];
       const int v = u - gg.e_base;
       d.kind = kUnitExpand;
@@ -380,29 +409,34 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
       ok = __shfl_sync(0xffffffffu, ok, 0);
       return ok ? s : -1;
     };
+    // A plan item is used only if it lies inside the plan: one from the plan
+    // kernels always does; a damaged one becomes a no-op unit (no rows)
+    // instead of an access out of range.
+    auto item_ok = [&](const int4& q) {
+      return q.x >= 0 && q.x < args.S && q.z >= 1 && q.z <= kRowsPerItem && q.y >= 0 && q.y <= args.T - q.z;
+    };
     int u = claim_read(claim_issue());
     int pending = u < units ? claim_issue() : 0;
+    // The item record and rows of the next unit are loaded while the current
+    // unit's stages are issued, so no unit waits on them.
+    // Fused expand units: the item's v (written by the finisher of its last
+    // shrink slice) is copied into vbuf by this warp, so the consumers find
+    // it in shared memory; its ready word is read one unit ahead too.
+    auto ready_word = [&](const Dec& q) -> const int* { return wv.ready + q.prob * tpad + q.item; };
+    Dec d = decode(u);
+    int4 it = d.kind != kUnitEnd ? pv.items[d.item] : make_int4(0, 0, 0, 0);
+    int row = d.kind != kUnitEnd && item_ok(it) && lane < it.z ? pv.perm[it.y + lane] : 0;
+    int rd = MODE == kModeFused && d.kind == kUnitExpand && lane == 0 ? ld_relaxed(ready_word(d)) : 0;
+    uint32_t ev = 0;  // fused expand units whose v this warp has copied
     bool dead = false;
     for (int j = 0; !dead; ++j) {
-      const Dec d = decode(u);
       const int iq = j % kUnitRing;
       int ok = 1;
       if (lane == 0 && j >= kUnitRing)
         ok = mbar_wait_abortable(&sm.uempty[iq], ((j / kUnitRing) - 1) & 1, args.err, abort) ? 1 : 0;
       if (!__shfl_sync(0xffffffffu, ok, 0)) break;  // the other roles find no unit and give up too
-      int4 it = make_int4(0, 0, 0, 0);
-      int row = 0;
       if (d.kind != kUnitEnd) {
-        it = pv.items[d.item];
-        // A plan from the plan kernels always passes; a damaged one turns
-        // the item into a no-op (no rows) instead of an access out of range.
-        bool good = it.x >= 0 && it.x < args.S && it.z >= 1 && it.z <= kRowsPerItem && it.y >= 0 &&
-                    it.y <= args.T - it.z;
-        if (good && lane < it.z) {
-          row = pv.perm[it.y + lane];
-          if (row < 0 || row >= args.T) good = false;
-        }
-        good = __all_sync(0xffffffffu, good);
+        const bool good = __all_sync(0xffffffffu, item_ok(it) && (lane >= it.z || (row >= 0 && row < args.T)));
         if (!good) {
           if (lane == 0 && d.slice == 0) raise_error(args.err, PERSONA_DEV_ERR_PLAN);
           it = make_int4(0, it.y >= 0 && it.y < args.T ? it.y : 0, 0, 0);
@@ -424,15 +458,52 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
       if (lane == 0) mbar_arrive(&sm.ufull[iq]);
       if (d.kind == kUnitEnd) break;
 
-      // The next unit's claim has returned by now; issue the one after it.
+      // The next unit's claim has returned by now; issue the one after it,
+      // and start loading the next unit's item record.
       const int u_next = claim_read(pending);
       pending = u_next < units ? claim_issue() : 0;
+      const Dec dn = decode(u_next);
+      const int4 itn = dn.kind != kUnitEnd ? pv.items[dn.item] : make_int4(0, 0, 0, 0);
+      const int rdn = MODE == kModeFused && dn.kind == kUnitExpand && lane == 0 ? ld_relaxed(ready_word(dn)) : 0;
+      int rown = 0;
+      bool rows_loaded = false;
+      auto load_next_rows = [&]() {  // once itn has arrived: after the first stage is issued
+        if (!rows_loaded) {
+          rows_loaded = true;
+          if (dn.kind != kUnitEnd && item_ok(itn) && lane < itn.z) rown = pv.perm[itn.y + lane];
+        }
+      };
 
       const int slot = it.x, c = it.z;
       const SplitProblem& pr = args.prob[d.prob];
+      if (MODE == kModeFused && d.kind == kUnitExpand) {
+        int vok = 1;
+        if (lane == 0) {
+          const int eb = static_cast<int>(ev & 1);
+          if (ev >= 2) vok = mbar_wait_abortable(&sm.vempty[eb], ((ev >> 1) - 1) & 1, args.err, abort) ? 1 : 0;
+          if (vok) {
+            if (rd == epoch)
+              asm volatile("fence.acq_rel.gpu;" ::: "memory");  // acquire side of the value read a unit ago
+            else
+              vok = wait_word(ready_word(d), epoch, args.err, abort, &wv.sync[kSyncAbort]) ? 1 : 0;
+          }
+          if (vok) {
+            fence_proxy_async_global();  // the finisher's stores, read by the bulk copy
+            const uint32_t vb = static_cast<uint32_t>(c * R * 4);
+            mbar_arrive_expect_tx(&sm.vfull[eb], vb);
+            if (vb > 0)
+              bulk_load(sm.vbuf + eb * (kRowsPerItem * kMaxR),
+                        wv.vfinal + (static_cast<int64_t>(d.prob) * tpad + it.y) * R, vb, &sm.vfull[eb]);
+          }
+        }
+        if (__shfl_sync(0xffffffffu, vok, 0))
+          ++ev;
+        else
+          dead = true;
+      }
       if (d.kind == kUnitShrink) {
         const uint16_t* x = static_cast<const uint16_t*>(pr.x);
-        for (int k0 = d.lo; k0 < d.hi; k0 += C::kKC) {
+        for (int k0 = d.lo; !dead && k0 < d.hi; k0 += C::kKC) {
           const int valid = min(C::kKC, d.hi - k0);
           const int nbox = (valid + 63) / 64;
           const uint32_t xb = static_cast<uint32_t>(valid) * 2u;
@@ -448,6 +519,7 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
           if (lane < c)
             bulk_load(st + C::kXOff + lane * C::kXPitch, x + static_cast<int64_t>(row) * pr.ldx + k0, xb, &sm.full[s]);
           ++g;
+          load_next_rows();
         }
       } else {
         const uint16_t* yg = static_cast<const uint16_t*>(pr.y);
@@ -480,15 +552,24 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
             bulk_load(st + C::kYOff + lane * C::kYStride, yg + static_cast<int64_t>(row) * pr.ldy + n0, yb,
                       &sm.full[s]);
           ++g;
+          load_next_rows();
         }
       }
+      load_next_rows();
       u = u_next;
+      d = dn;
+      it = itn;
+      row = rown;
+      rd = rdn;
     }
     // Every copy this warp issued lands before the CTA exits (normally the
     // consumers have waited for all of them already).
-    if (lane == 0)
+    if (lane == 0) {
       for (int s = 0; s < kSlots; ++s)
         if (g > static_cast<uint32_t>(s)) mbar_wait(&sm.full[s], ((g - 1 - s) / kSlots) & 1, args.err);
+      for (uint32_t b = 0; b < 2; ++b)
+        if (ev > b) mbar_wait(&sm.vfull[b], ((ev - 1 - b) >> 1) & 1, args.err);
+    }
     __syncwarp();
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA --
@@ -496,6 +577,8 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
     // tensor-core kernel it issues D[box] = B_box * (v_hi + v_lo)^T into the
     // slot's accumulators and commits to mma_done[slot]; every other stage
     // gets a plain arrive so that mma_done keeps one phase per slot use.
+    // (Releasing a slot from the MMA commit instead, with a separate ring of
+    // accumulators, measured slower: 340 against 305 us per launch.)
     if (lane == 0) {
       uint32_t g = 0, ue = 0;
       const uint32_t vop = smem_u32(sm.vop);
@@ -571,7 +654,8 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
         if (s < 0 || s >= args.S) args.v_out[i] = 0.f;
       }
     }
-    uint32_t g = 0;
+    uint32_t g = 0;   // stage counter, as in the producer and the MMA warp
+    uint32_t ev = 0;  // fused expand units, as in the producer
     for (int j = 0;; ++j) {
       const int iq = j % kUnitRing;
       const bool got = mbar_wait_abortable(&sm.ufull[iq], (j / kUnitRing) & 1, args.err, abort);
@@ -678,6 +762,7 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
           } else {
             float* vfin = wv.vfinal + (static_cast<int64_t>(prob) * tpad + pos) * R;
             for (int e = tid; e < E; e += kConsumers) vfin[e] = sm.pv[e];
+            fence_proxy_async_global();  // another SM's producer bulk-copies v
           }
           named_sync(bar_cons, kConsumers);
           if (tid == 0) {
@@ -692,6 +777,7 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
       if (kDoExpand && kind == kUnitExpand) {
         uint16_t* y = static_cast<uint16_t*>(pr.y);
         float* vfb = sm.vf;
+        bool okv = true;
         if (MODE == kModeExpand) {
           const int s = static_cast<int>(g % kSlots);
           const bool ok = mbar_wait_abortable(&sm.full[s], (g / kSlots) & 1, args.err, abort);
@@ -701,10 +787,9 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
           if (lane == 0 && ok) mbar_arrive_relaxed(&sm.empty[s]);
           ++g;
         } else {
-          if (tid == 0) wait_word(wv.ready + prob * tpad + item, epoch, args.err, abort, &wv.sync[kSyncAbort]);
-          named_sync(bar_cons, kConsumers);
-          const float* vfin = wv.vfinal + (static_cast<int64_t>(prob) * tpad + pos) * R;
-          for (int e = tid; e < E; e += kConsumers) vfb[e] = __ldcg(vfin + e);
+          // the producer has copied this item's v into vbuf[ev & 1]
+          okv = mbar_wait_abortable(&sm.vfull[ev & 1], (ev >> 1) & 1, args.err, abort);
+          vfb = sm.vbuf + (ev & 1) * (kRowsPerItem * kMaxR);
         }
         named_sync(bar_cons, kConsumers);
         // Power-of-two scale that keeps the 16-bit v halves finite (f16 only).
@@ -803,6 +888,11 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
           }
         }
         named_sync(bar_cons, kConsumers);
+        if (MODE == kModeFused) {
+          // vbuf[ev & 1] may take the v of a later unit
+          if (tid == 0 && okv) mbar_arrive(&sm.vempty[ev & 1]);
+          ++ev;
+        }
       }
       __syncwarp();
       if (lane == 0) mbar_arrive_relaxed(&sm.uempty[iq]);

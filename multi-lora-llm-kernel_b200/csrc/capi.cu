@@ -443,7 +443,14 @@ int persona_gemv_fp16(const void* x, const void* W, void* y, int64_t K, int64_t 
 
 // ----------------------------------------------------------------- SGMV ---
 namespace {
-size_t sgmv_ws_bytes(int64_t T) { return persona::bgmv_ws_bytes(T) + 4 * static_cast<size_t>(persona::plan_tpad(T)); }
+// Workspace of the segmented ops: the BGMV workspace (plan, counters, v),
+// the per-row slots of the split-kernel path, and the tensor-core kernel's
+// partial-v pieces.
+size_t sgmv_rows_offset(int64_t T) { return persona::bgmv_ws_bytes(T); }
+size_t sgmv_pieces_offset(int64_t T) {
+  return persona::align256(sgmv_rows_offset(T) + 4 * static_cast<size_t>(persona::plan_tpad(T)));
+}
+size_t sgmv_ws_bytes(int64_t T) { return sgmv_pieces_offset(T) + persona::kSgmvPieceBytes; }
 
 int sgmv_prepare(const int32_t* seg_indptr, const int32_t* seg_slots, int64_t nseg, int64_t T, int64_t S,
                  void* workspace, size_t workspace_bytes, int32_t* dev_err, cudaStream_t stream,
@@ -453,7 +460,7 @@ int sgmv_prepare(const int32_t* seg_indptr, const int32_t* seg_slots, int64_t ns
   if (seg_indptr == nullptr || (nseg > 0 && seg_slots == nullptr)) return PERSONA_ERR_INVALID_ARG;
   if (workspace == nullptr || workspace_bytes < sgmv_ws_bytes(T)) return PERSONA_ERR_WORKSPACE;
   if ((reinterpret_cast<uintptr_t>(workspace) & 15) != 0) return PERSONA_ERR_ALIGNMENT;
-  *row_slots = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(workspace) + persona::bgmv_ws_bytes(T));
+  *row_slots = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(workspace) + sgmv_rows_offset(T));
   return persona::launch_sgmv_plan(seg_indptr, seg_slots, static_cast<int>(nseg), static_cast<int>(T),
                                    static_cast<int>(S), persona::kRowsPerItem, static_cast<int32_t*>(workspace),
                                    *row_slots, dev_err, stream) == cudaSuccess
@@ -511,9 +518,12 @@ int sgmv_tc_run(int mode, const void* x, int64_t ldx, const void* a_pool, int64_
   }
   if (mode == kModeShrink && (v_out == nullptr || !aligned16(v_out))) return PERSONA_ERR_ALIGNMENT;
   if (mode == kModeExpand && (v_in == nullptr || !aligned16(v_in))) return PERSONA_ERR_ALIGNMENT;
-  // items of 128 rows and the header are all the tensor-core kernel reads
+  // The tensor-core kernel reads the header and the items of 128 rows; the
+  // plan kernel also zeroes the per-item counters and ready words it uses.
+  const WorkView wv = work_view(static_cast<int32_t*>(workspace), T);
   if (launch_sgmv_plan(seg_indptr, seg_slots, static_cast<int>(nseg), static_cast<int>(T), static_cast<int>(S),
-                       128, static_cast<int32_t*>(workspace), nullptr, dev_err, stream) != cudaSuccess)
+                       128, static_cast<int32_t*>(workspace), nullptr, dev_err, stream, wv.s_cnt,
+                       static_cast<int>(wv.ready - wv.s_cnt)) != cudaSuccess)
     return PERSONA_ERR_CUDA;
   if (mode == kModeShrink) {
     // rows outside every segment (or with slot -1) get v = 0 first
@@ -531,6 +541,10 @@ int sgmv_tc_run(int mode, const void* x, int64_t ldx, const void* a_pool, int64_
   a.K = static_cast<int>(K);
   a.N = static_cast<int>(n1 - n0);
   a.n0 = static_cast<int>(n0);
+  a.vfin = wv.vfinal;
+  a.pieces = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + sgmv_pieces_offset(T));
+  a.item_cnt = wv.s_cnt;
+  a.item_ready = wv.ready;
   a.num_peers = num_peers;
   for (int q = 0; q < num_peers; ++q) a.peers[q] = static_cast<uint16_t*>(peers[q]);
   if (n1 == n0 && (mode & kModeExpand)) return PERSONA_OK;

@@ -13,9 +13,8 @@ package's kernels:
 
 * base projections: ``nf4.linear`` (one launch for q / k / v, one for gate /
   up, one each for o and down);
-* LoRA: ``ops.bgmv_fused_multi`` / ``ops.bgmv_fused`` on a plan computed once
-  per batch at decode and, with per-row slots, at prefill; ``ops.sgmv_fused``
-  per request segment for prefills of at least ``SGMV_MIN_ROWS`` rows;
+* LoRA: ``ops.bgmv_fused_multi`` on a plan computed once per batch at decode;
+  ``ops.sgmv_fused`` over the request segments at prefill;
 * the rest: ``ops.add_rmsnorm`` (residual add fused into the
   next norm), ``rope_cache`` (rotary embedding + KV-cache write) at prefill,
   ``rope_decode_attention`` (the same and the attention, one launch) at
@@ -29,7 +28,6 @@ so it is captured once as a CUDA graph and replayed for every token.
 from __future__ import annotations
 
 import math
-import os
 from dataclasses import dataclass, field
 from typing import List, Optional
 
@@ -38,11 +36,6 @@ import torch.nn.functional as F
 
 from persona import nf4, ops
 from persona.adapter_pool import AdapterPool
-
-# Prefill rows from which the LoRA goes through the tensor-core SGMV kernel
-# (64 items of 128 rows); fewer go through the BGMV launch with per-row slots.
-SGMV_MIN_ROWS = int(os.environ.get("PERSONA_PREFILL_SGMV_MIN_ROWS", "8192"))
-
 
 @dataclass
 class MistralConfig:
@@ -174,23 +167,13 @@ class MistralLoRAModel:
         xn = torch.empty_like(h)
         indptr = torch.arange(0, R + 1, T, dtype=torch.int32, device=self.device)
         start = torch.zeros(1, dtype=torch.int32, device=self.device)
-        # LoRA: the tensor-core SGMV kernel gives each 128-row item to one CTA,
-        # so it needs many items to fill the GPU; below SGMV_MIN_ROWS rows the
-        # rows go through the multi-projection BGMV launch with per-row slots
-        # (one plan for the whole prefill), as the reference's caller does.
-        use_sgmv = R >= SGMV_MIN_ROWS
-        row_slots = plan = None
-        if not use_sgmv:
-            row_slots = st.slots.repeat_interleave(T).contiguous()
-            plan = ops.bgmv_plan(row_slots, self.pool.max_slots)
-
+        # LoRA over the request segments (one adapter per prompt): the
+        # segmented kernel splits its work evenly over the SMs whatever the
+        # number of prompts (the reference's caller expands the same segments
+        # into per-token slots, persona/lora_layer.py:21-28).
         def lora_apply(x, lora, names, ys):
-            if use_sgmv:
-                for name, y in zip(names, ys):
-                    ops.sgmv_fused(x, *lora[name], indptr, st.slots, y)
-            else:
-                ops.bgmv_fused_multi([x] * len(names), [lora[m][0] for m in names], [lora[m][1] for m in names],
-                                     row_slots, list(ys), plan=plan)
+            for name, y in zip(names, ys):
+                ops.sgmv_fused(x, *lora[name], indptr, st.slots, y)
 
         delta = None
         for li, lw in enumerate(self.layers):

@@ -9,6 +9,7 @@ import numpy as np
 import pytest
 
 from oracle import nf4_oracle as Q
+from oracle import nf4_oracle as O
 
 ROOT = Path(__file__).resolve().parents[1]
 TABLE_H = ROOT / "multi-lora-llm-kernel_b200" / "csrc" / "nf4_table.h"
@@ -80,3 +81,65 @@ def test_linear_reference_is_the_dense_product():
     want = (x.astype(np.float64) @ Q.dequantize_f32(packed, offset, N, K).astype(np.float64).T).astype(np.float16)
     assert np.array_equal(y, want)
     assert Q.dequantize_f16(packed, offset, N, K).dtype == np.float16
+
+
+# ---- bitsandbytes storage -> this format (persona.nf4.from_bitsandbytes) ----
+
+def _bnb_tensors(st):
+    import torch
+
+    kw = dict(packed=torch.from_numpy(st["packed"]), absmax=torch.from_numpy(st["absmax"]),
+              shape=st["shape"], quant_map=torch.from_numpy(st["quant_map"]), blocksize=st["blocksize"])
+    if "nested_absmax" in st:
+        kw.update(nested_absmax=torch.from_numpy(st["nested_absmax"]),
+                  nested_quant_map=torch.from_numpy(st["nested_quant_map"]),
+                  nested_offset=st["nested_offset"], nested_blocksize=st["nested_blocksize"])
+    return kw
+
+
+@pytest.mark.parametrize("double_quant", [True, False])
+def test_bitsandbytes_storage_converts(double_quant):
+    """Codes carry over bit for bit; every scale moves by at most half a step
+    of this format's per-tile int8 code (parity with bitsandbytes itself is
+    unpinned: it is not installed, its storage is restated in oracle/)."""
+    from oracle import bnb_nf4
+    from persona import nf4
+
+    rng = np.random.default_rng(7)
+    N, K = 256, 384
+    w = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+    st = bnb_nf4.quantize_nf4(w, double_quant=double_quant)
+    q = nf4.from_bitsandbytes(**_bnb_tensors(st), device="cpu")
+    codes, am = O.unpack(q.packed.numpy(), np.float32(q.offset.item()), N, K)
+    assert np.array_equal(codes, bnb_nf4.codes(st))
+    want = bnb_nf4.scales(st).reshape(N, K // 64)
+    s127 = q.packed.numpy()[:, :, O.S127_OFF:O.S127_OFF + 4].copy().view(np.float32).reshape(N // 128, K // 128)
+    step = np.repeat(np.repeat(s127, 128, axis=0), 2, axis=1)
+    assert np.all(np.abs(am - want) <= 0.5 * step * 1.001 + 1e-9)
+    w_ours = O.dequantize_f32(q.packed.numpy(), np.float32(q.offset.item()), N, K)
+    w_bnb = bnb_nf4.dequantize(st)
+    assert np.abs(w_ours - w_bnb).max() <= 0.5 * step.max() * 1.001 + 1e-3 * np.abs(w_bnb).max()
+
+
+def test_bitsandbytes_storage_rejects_other_layouts():
+    import torch
+
+    from oracle import bnb_nf4
+    from persona import nf4
+
+    st = bnb_nf4.quantize_nf4(np.zeros((128, 128), np.float32) + 0.01)
+    kw = _bnb_tensors(st)
+    with pytest.raises(ValueError, match="blocksize"):
+        nf4.from_bitsandbytes(**{**kw, "blocksize": 128})
+    with pytest.raises(ValueError, match="NF4 table"):
+        nf4.from_bitsandbytes(**{**kw, "quant_map": torch.linspace(-1, 1, 16)})
+    with pytest.raises(ValueError, match="multiples of 128"):
+        nf4.from_bitsandbytes(**{**kw, "shape": (128, 64)})
+
+
+def test_dynamic_map_shape():
+    from oracle import bnb_nf4
+
+    m = bnb_nf4.dynamic_map_signed()
+    assert m.shape == (256,) and np.all(np.diff(m) >= 0) and m[0] >= -1 and m[-1] == 1.0
+    assert np.sum(m == 0) >= 1 and np.abs(m).max() == 1.0

@@ -172,3 +172,30 @@ def test_problems_of_different_k_in_one_launch(M):
     assert int(err.item()) == 0
     for a, b in zip(first, ys):
         assert torch.equal(a, b)
+
+
+def test_bitsandbytes_checkpoint_through_the_kernels():
+    """A weight in bitsandbytes' NF4 storage (double-quantised scales,
+    restated in oracle/bnb_nf4.py), converted by nf4.from_bitsandbytes and
+    applied by the decode GEMM and by the dequantiser: against the fp32
+    product with the weight that storage describes (tolerance: this format's
+    scale step, plus fp16 rounding)."""
+    from oracle import bnb_nf4
+
+    rng = np.random.default_rng(11)
+    N, K, M = 512, 1024, 8
+    w = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+    st = bnb_nf4.quantize_nf4(w)
+    q = nf4.from_bitsandbytes(torch.from_numpy(st["packed"]).cuda(), torch.from_numpy(st["absmax"]).cuda(),
+                              st["shape"], torch.from_numpy(st["quant_map"]), blocksize=64,
+                              nested_absmax=torch.from_numpy(st["nested_absmax"]).cuda(),
+                              nested_quant_map=torch.from_numpy(st["nested_quant_map"]).cuda(),
+                              nested_offset=st["nested_offset"], nested_blocksize=256)
+    w_bnb = bnb_nf4.dequantize(st)
+    x = rng.standard_normal((M, K)).astype(np.float16)
+    y = nf4.linear(torch.from_numpy(x).cuda(), [q])[0].float().cpu().numpy()
+    want = x.astype(np.float64) @ w_bnb.astype(np.float64).T
+    np.testing.assert_allclose(y, want, rtol=2e-2, atol=2e-2)
+    wd = nf4.dequantize(q).float().cpu().numpy()
+    np.testing.assert_allclose(wd, w_bnb, rtol=1e-2, atol=2e-4)
+    ops.check_errors(torch.device("cuda", 0))
