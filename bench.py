@@ -57,7 +57,8 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true",
                     help="skip the bounded mixed-adapter decode run that the headline line carries")
-    ap.add_argument("--workload", choices=["mixed_decode", "sgmv_prefill", "decode_set", "e2e_decode", "nf4_decode"],
+    ap.add_argument("--workload", choices=["mixed_decode", "sgmv_prefill", "decode_set", "e2e_decode", "nf4_decode",
+                                           "decode_kernels"],
                     default="mixed_decode",
                     help="mixed_decode is the headline; the others print their own line")
     ap.add_argument("--batch", type=int, default=None,
@@ -1026,6 +1027,62 @@ def run_nf4(args):
     return 0
 
 
+def run_decode_kernels(args):
+    """Two small kernels of the paths, each timed alone with CUDA events:
+    the row-grouping plan of the headline batch (512 Zipf rows, 256-slot
+    pool) and the decode step's rotary + cache write + attention launch
+    (batch 8, 32 query / 8 KV heads, head dim 128, 255 cached positions,
+    the caches of 32 layers cycled so the KV reads come from HBM).  One line
+    each."""
+    import torch
+
+    from persona import ops
+
+    if args.gpus != 1:
+        raise SystemExit("--workload decode_kernels runs on one GPU")
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    steps, warm = max(1, args.steps), max(3, args.warmup)
+    stream = torch.cuda.current_stream()
+    slots = torch.from_numpy(global_slots(1).astype(np.int32)).to(dev)
+    ms = _timed(lambda: ops.bgmv_plan(slots, POOL_SLOTS), warm, stream)
+    ms = _timed(lambda: ops.bgmv_plan(slots, POOL_SLOTS), steps, stream)
+    print(json.dumps({"workload": "decode_kernels", "kernel": "bgmv_plan_kernel",
+                      "metric": "row-grouping plan of the 512-row Zipf batch, us per launch", "value": ms * 1e3,
+                      "unit": "us", "higher_is_better": False, "n_gpus": 1, "steps": steps, "warmup": warm,
+                      "config": {"rows": ROWS_PER_GPU, "pool_slots": POOL_SLOTS}}), flush=True)
+    B, Hq, Hkv, L, D, layers = 8, 32, 8, 256, 128, 32
+    g = torch.Generator(device=dev).manual_seed(SEED * 1000 + 53)
+    kc = [torch.randn(B, Hkv, L, D, generator=g, device=dev).half() for _ in range(layers)]
+    vc = [torch.randn(B, Hkv, L, D, generator=g, device=dev).half() for _ in range(layers)]
+    q = torch.randn(B, Hq, D, generator=g, device=dev).half()
+    k = torch.randn(B, Hkv, D, generator=g, device=dev).half()
+    v = torch.randn(B, Hkv, D, generator=g, device=dev).half()
+    out = torch.empty_like(q)
+    pos = torch.full((1,), L - 1, dtype=torch.int32, device=dev)
+    length = torch.full((1,), L, dtype=torch.int32, device=dev)
+
+    def all_layers():
+        for li in range(layers):
+            ops.rope_decode_attention(q, k, v, kc[li], vc[li], pos, length, out, 1e6, D ** -0.5)
+
+    _timed(all_layers, warm, stream)
+    ms = _timed(all_layers, steps, stream) / layers
+    ops.check_errors(dev)
+    byts = B * Hkv * L * D * 2 * 2 + B * (Hq + 2 * Hkv) * D * 2 + B * Hq * D * 2  # KV read, q/k/v in, out
+    peak, _ = load_peaks()
+    print(json.dumps({"workload": "decode_kernels", "kernel": "decode_attention_kernel (rotary + cache write fused)",
+                      "metric": "decode attention (rotary + cache write + attention), us per launch",
+                      "value": ms * 1e3, "unit": "us", "higher_is_better": False, "n_gpus": 1, "steps": steps,
+                      "warmup": warm, "config": {"batch": B, "q_heads": Hq, "kv_heads": Hkv, "positions": L,
+                                                 "l2": f"{layers} layers' caches cycled ({layers * 2 * kc[0].numel() * 2 / 1e6:.0f} MB > L2)"},
+                      "roofline": {"bound": "hbm", "algorithmic_bytes": byts,
+                                   "achieved": byts / (ms * 1e-3) / 1e9, "peak": peak, "unit": "GB/s",
+                                   "frac": byts / (ms * 1e-3) / 1e9 / peak},
+                      "gpu_launches": steps * layers}), flush=True)
+    return 0
+
+
 def main():
     global ONLY
     args = parse_args()
@@ -1036,6 +1093,8 @@ def main():
         return run_e2e(args)
     if args.workload == "nf4_decode":
         return run_nf4(args)
+    if args.workload == "decode_kernels":
+        return run_decode_kernels(args)
     if args.workload == "sgmv_prefill" and args.gpus > 1:
         return run_sgmv_tp(args)
     if args.workload != "mixed_decode":

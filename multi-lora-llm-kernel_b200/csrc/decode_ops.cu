@@ -10,9 +10,12 @@
 
 #include <cstdint>
 
+#include <cooperative_groups.h>
+
 #include "decode_args.h"
 
 namespace persona {
+namespace cg = cooperative_groups;
 namespace {
 
 __device__ __forceinline__ float h2f(__half h) { return __half2float(h); }
@@ -154,21 +157,27 @@ __global__ void silu_mul_kernel(const __half* __restrict__ g, const __half* __re
 }
 
 // One new token per sequence: out[b, h] = softmax(q[b, h] K[b, h / G]^T *
-// scale) V[b, h / G] over positions [0, *len).  One CTA of 128 threads per
-// (sequence, kv head) computes the G = Hq / Hkv <= 8 query heads that share
-// the cache rows, so K and V are read once.  Scores: a thread per position,
-// 16-byte loads of its K row, G dot products (q in shared memory).  P V:
-// threads as 8 position groups x 16 column chunks of 8 dims, 16-byte V
-// loads eight positions at a time, then a sum over the groups in shared
-// memory.  Dynamic shared memory: G * L scores + 8 * G * 128 partial sums +
-// G * 128 query values, all fp32.
+// scale) V[b, h / G] over positions [0, *len).  One thread-block cluster of
+// P CTAs (128 threads each) per (sequence, kv head) computes the G = Hq / Hkv
+// <= 8 query heads that share the cache rows, so K and V are read once; the
+// positions are cut into P equal ranges, one per CTA, so that B * Hkv * P
+// CTAs (not B * Hkv) stream the cache.  Per CTA: scores, a thread per
+// position (16-byte loads of its K row, G dot products, q in shared memory);
+// the softmax statistics of its range (max m, sum l of exp(s - m)); P V as 8
+// position groups x 16 column chunks of 8 dims (16-byte V loads), summed
+// over the groups in shared memory.  The CTAs then combine their ranges
+// through distributed shared memory: out = sum_r e^(m_r - M) acc_r /
+// sum_r e^(m_r - M) l_r with M = max_r m_r, each CTA writing a slice of the
+// output.
 constexpr int kAttnThreads = 128;
+constexpr int kAttnMaxSplit = 8;  // CTAs per cluster (portable maximum)
+constexpr int kAttnChunk = 64;    // positions per CTA the split aims at
 
-// With a position (rope.pos != nullptr) the kernel first does what
-// rope_cache_kernel does for this (sequence, kv head), with the same
+// With a position (rope.pos != nullptr), rank 0 of the cluster first does
+// what rope_cache_kernel does for this (sequence, kv head), with the same
 // arithmetic: it rotates the G query heads and the k head of the new token
 // in place and writes k and v to the caches at *pos (nothing at all when
-// *pos is outside [0, L)); the attention below then reads them back.
+// *pos is outside [0, L)); after a cluster barrier every CTA reads them back.
 struct RopeIn {
   __half* q;  // [B, Hq, 128], rotated in place (and read below)
   __half* k;  // [B, Hkv, 128], rotated in place
@@ -188,16 +197,20 @@ __device__ __forceinline__ void rope_pair(__half* x, int j, __half c, __half s, 
 }
 
 // q, kc and vc are not restrict: with a position they are written above
-// their reads, through rope.
+// their reads, through rope.  cmax: the largest range a CTA can get,
+// ceil(L / P), which sizes the score buffer.
 __global__ void __launch_bounds__(kAttnThreads) decode_attention_kernel(
     const __half* q, const __half* kc, const __half* vc, const int* __restrict__ len_ptr, __half* __restrict__ out,
-    int Hq, int Hkv, int L, float scale, const RopeIn rope) {
+    int Hq, int Hkv, int L, int cmax, float scale, const RopeIn rope) {
   constexpr int D = 128;
+  cg::cluster_group cluster = cg::this_cluster();
+  const int P = static_cast<int>(cluster.num_blocks());
+  const int rank = static_cast<int>(cluster.block_rank());
   pdl_wait();
   asm volatile("griddepcontrol.launch_dependents;");
   const int b = blockIdx.x, kh = blockIdx.y, tid = threadIdx.x;
   const int G = Hq / Hkv;
-  if (rope.pos != nullptr) {
+  if (rope.pos != nullptr && rank == 0) {
     const int pos = *rope.pos;
     if (pos >= 0 && pos < L) {
       const int j = tid & 63;
@@ -221,22 +234,27 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attention_kernel(
         }
       }
     }
-    // the rotated q and the new cache row, written above, are read below
-    __syncthreads();
+    __threadfence();
   }
+  // the rotated q and the new cache row, written by rank 0, are read below
+  // by every CTA of the cluster (release / acquire at cluster scope)
+  if (rope.pos != nullptr) cluster.sync();
   const int len = min(*len_ptr, L);
+  const int chunk = (len + P - 1) / P;
+  const int p0 = min(len, rank * chunk), p1 = min(len, p0 + chunk);
   extern __shared__ float attn_smem[];
-  float* sc = attn_smem;                 // [G][L]
-  float* part = sc + G * L;              // [8][G][D]
-  float* qs = part + 8 * G * D;          // [G][D]
-  __shared__ float s_inv[8];
+  float* sc = attn_smem;          // [G][cmax] scores, then exp(s - m)
+  float* part = sc + G * cmax;    // [8][G][D] P V per position group
+  float* qs = part + 8 * G * D;   // [G][D]
+  float* accs = qs + G * D;       // [G][D] this range's unnormalised P V
+  __shared__ float s_m[8], s_l[8];
   for (int i = tid; i < G * D; i += kAttnThreads)
     qs[i] = __half2float(q[(static_cast<int64_t>(b) * Hq + kh * G) * D + i]);
   __syncthreads();
   const __half* kb = kc + (static_cast<int64_t>(b) * Hkv + kh) * L * D;
   const __half* vb = vc + (static_cast<int64_t>(b) * Hkv + kh) * L * D;
   // scores
-  for (int p = tid; p < len; p += kAttnThreads) {
+  for (int p = p0 + tid; p < p1; p += kAttnThreads) {
     const uint4* kr = reinterpret_cast<const uint4*>(kb + static_cast<int64_t>(p) * D);
     uint4 kv[D / 8];
 #pragma unroll
@@ -254,51 +272,55 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attention_kernel(
           dot = fmaf(qh[8 * i + 2 * j + 1], kf.y, dot);
         }
       }
-      sc[h * L + p] = dot * scale;
+      sc[h * cmax + (p - p0)] = dot * scale;
     }
   }
   __syncthreads();
-  // softmax statistics per head: warp w reduces heads w, w + 4
+  // softmax statistics of this range per head: warp w reduces heads w, w + 4
   const int warp = tid >> 5, lane = tid & 31;
+  const int n = p1 - p0;
   for (int h = warp; h < G; h += kAttnThreads / 32) {
     float m = -INFINITY;
-    for (int p = lane; p < len; p += 32) m = fmaxf(m, sc[h * L + p]);
+    for (int p = lane; p < n; p += 32) m = fmaxf(m, sc[h * cmax + p]);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
     float l = 0.f;
-    for (int p = lane; p < len; p += 32) {
-      const float e = __expf(sc[h * L + p] - m);
-      sc[h * L + p] = e;
+    for (int p = lane; p < n; p += 32) {
+      const float e = __expf(sc[h * cmax + p] - m);
+      sc[h * cmax + p] = e;
       l += e;
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
-    if (lane == 0) s_inv[h] = l > 0.f ? 1.f / l : 0.f;
+    if (lane == 0) {
+      s_m[h] = m;
+      s_l[h] = l;
+    }
   }
   __syncthreads();
-  // P V: position group pg, 8-dim column chunk dc
+  // P V over this range: position group pg, 8-dim column chunk dc
   const int pg = tid >> 4, dc = tid & 15;
   float acc[8][8];
 #pragma unroll
   for (int h = 0; h < 8; ++h)
 #pragma unroll
     for (int j = 0; j < 8; ++j) acc[h][j] = 0.f;
-  for (int p0 = pg; p0 < len; p0 += 8 * 8) {
+  for (int q0 = pg; q0 < n; q0 += 8 * 8) {
     uint4 vv[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      const int p = p0 + 8 * i;
-      vv[i] = p < len ? reinterpret_cast<const uint4*>(vb + static_cast<int64_t>(p) * D)[dc] : make_uint4(0, 0, 0, 0);
+      const int p = q0 + 8 * i;
+      vv[i] = p < n ? reinterpret_cast<const uint4*>(vb + static_cast<int64_t>(p0 + p) * D)[dc] : make_uint4(0, 0, 0, 0);
     }
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      const int p = p0 + 8 * i;
-      if (p < len) {
+      const int p = q0 + 8 * i;
+      if (p < n) {
         const __half2* v2 = reinterpret_cast<const __half2*>(&vv[i]);
 #pragma unroll
         for (int h = 0; h < 8; ++h) {
           if (h < G) {
-            const float w = sc[h * L + p];
+            const float w = sc[h * cmax + p];
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
               const float2 vf = __half22float2(v2[j]);
@@ -317,12 +339,32 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attention_kernel(
       for (int j = 0; j < 8; ++j) part[(pg * G + h) * D + 8 * dc + j] = acc[h][j];
   __syncthreads();
   for (int i = tid; i < G * D; i += kAttnThreads) {
-    const int h = i / D;
     float sum = 0.f;
 #pragma unroll
     for (int g = 0; g < 8; ++g) sum += part[g * G * D + i];
-    out[(static_cast<int64_t>(b) * Hq + kh * G) * D + i] = __float2half_rn(sum * s_inv[h]);
+    accs[i] = sum;
   }
+  // every range's statistics and P V are in its CTA's shared memory
+  cluster.sync();
+  // combine the ranges, in rank order: this CTA writes outputs
+  // [rank * G * D / P, (rank + 1) * G * D / P)
+  const int o0 = rank * G * D / P, o1 = (rank + 1) * G * D / P;
+  for (int i = o0 + tid; i < o1; i += kAttnThreads) {
+    const int h = i / D;
+    float M = -INFINITY;
+    for (int r = 0; r < P; ++r) M = fmaxf(M, *cluster.map_shared_rank(&s_m[h], r));
+    float num = 0.f, den = 0.f;
+    if (M != -INFINITY) {
+      for (int r = 0; r < P; ++r) {
+        const float w = __expf(*cluster.map_shared_rank(&s_m[h], r) - M);
+        num = fmaf(w, *cluster.map_shared_rank(accs + i, r), num);
+        den = fmaf(w, *cluster.map_shared_rank(&s_l[h], r), den);
+      }
+    }
+    out[(static_cast<int64_t>(b) * Hq + kh * G) * D + i] = __float2half_rn(den > 0.f ? num / den : 0.f);
+  }
+  // no CTA leaves while another may still read its shared memory
+  cluster.sync();
 }
 
 }  // namespace
@@ -353,16 +395,37 @@ namespace {
 cudaError_t attention_launch(const void* q, const void* kc, const void* vc, const int* len, void* out, int B, int Hq,
                              int Hkv, int L, float scale, const RopeIn& rope, cudaStream_t st) {
   const int G = Hq / Hkv;
-  const size_t smem = (static_cast<size_t>(G) * L + 8 * G * 128 + G * 128) * sizeof(float);
+  int P = (L + kAttnChunk - 1) / kAttnChunk;
+  P = P < 1 ? 1 : P > kAttnMaxSplit ? kAttnMaxSplit : P;
+  const int cmax = (L + P - 1) / P;
+  const size_t smem = (static_cast<size_t>(G) * cmax + 8 * G * 128 + 2 * G * 128) * sizeof(float);
   if (smem > 227 * 1024) return cudaErrorInvalidValue;
   if (smem > 48 * 1024) {
     const cudaError_t e =
         cudaFuncSetAttribute(decode_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return e;
   }
-  return launch_pdl(decode_attention_kernel, dim3(B, Hkv), dim3(kAttnThreads), smem, st,
-                    static_cast<const __half*>(q), static_cast<const __half*>(kc), static_cast<const __half*>(vc),
-                    len, static_cast<__half*>(out), Hq, Hkv, L, scale, rope);
+  // one cluster of P CTAs per (sequence, kv head), launched as a
+  // programmatic dependent of the kernel before it
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(B, Hkv, P);
+  cfg.blockDim = dim3(kAttnThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = P;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, decode_attention_kernel, static_cast<const __half*>(q),
+                                           static_cast<const __half*>(kc), static_cast<const __half*>(vc), len,
+                                           static_cast<__half*>(out), Hq, Hkv, L, cmax, scale, rope);
+  if (e != cudaSuccess) return e;
+  return cudaGetLastError();
 }
 
 }  // namespace
