@@ -165,8 +165,164 @@ __global__ void __launch_bounds__(THREADS)
   }
 }
 
+// The same plan by a stable counting sort, for pools of at most
+// kCountMaxKeys - 2 slots (keys: the slot, S for -1, S + 1 for a slot out of
+// range).  One CTA of 512 threads; per chunk of CH rows (the chunking of
+// bgmv_plan_kernel, so the two give the same plan):
+//  * per-key row counts (one shared-memory atomic per distinct key of a
+//    warp) and their exclusive scan:
+//    the first perm position of every key;
+//  * rounds of 512 rows, 32 consecutive rows per warp: a row's rank among
+//    the earlier rows of its key is its rank among the equal keys of its warp
+//    (__match_any_sync), plus the same key's rows in the earlier warps of the
+//    round (a per-warp count table, scanned per key), plus those of the
+//    earlier rounds;
+//  * items: per key, its full items then its partial one, placed by two
+//    scans over the keys (full items of all keys first, in key order).
+// About ten block barriers per chunk, instead of the radix sort's passes.
+constexpr int kCountThreads = 512;
+constexpr int kCountWarps = kCountThreads / 32;
+constexpr int kCountMaxKeys = 512;
+
+template <int CH>
+__global__ void __launch_bounds__(kCountThreads)
+    bgmv_plan_count_kernel(const int32_t* __restrict__ slots, int T, int S, int rows_per_item,
+                           int32_t* __restrict__ plan, int32_t* dev_err) {
+  static_assert(CH % kCountThreads == 0, "rounds of whole warps");
+  using Scan = cub::BlockScan<int, kCountThreads>;
+  __shared__ typename Scan::TempStorage scan;
+  __shared__ int cnt[kCountMaxKeys];    // rows per key in this chunk
+  __shared__ int start[kCountMaxKeys];  // first perm position of the key in this chunk
+  __shared__ int run[kCountMaxKeys];    // rows of the key placed by earlier rounds
+  __shared__ int whist[kCountWarps][kCountMaxKeys];
+  __shared__ int s_counts[4];  // valid, null, bad, items (running over chunks)
+  __shared__ int s_full;       // full items of this chunk
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // The BGMV kernel after this one is launched as a programmatic dependent.
+  asm volatile("griddepcontrol.launch_dependents;");
+  PlanView pv = plan_view(plan, T);
+  if (tid < 4) s_counts[tid] = 0;
+  init_work_state(plan, T, tid, kCountThreads);
+  const int nkeys = S + 2;
+  const uint32_t lt_mask = (1u << lane) - 1u;
+
+  for (int base = 0; base < T; base += CH) {
+    const int len = min(CH, T - base);
+    for (int k = tid; k < nkeys; k += kCountThreads) {
+      cnt[k] = 0;
+      run[k] = 0;
+    }
+    __syncthreads();
+    int keys[CH / kCountThreads];
+#pragma unroll
+    for (int r = 0; r < CH / kCountThreads; ++r) {
+      const int i = r * kCountThreads + tid;
+      int key = -1;
+      if (i < len) {
+        const int sl = slots[base + i];
+        key = sl >= 0 && sl < S ? sl : sl == -1 ? S : S + 1;
+      }
+      // one atomic per distinct key of the warp: a hot slot (a Zipf batch
+      // puts a fifth of its rows on one adapter) would otherwise serialise
+      // its rows on one shared-memory word
+      const uint32_t act = __ballot_sync(0xffffffffu, key >= 0);
+      if (key >= 0) {
+        const uint32_t peers = __match_any_sync(act, key);
+        if ((peers & lt_mask) == 0) atomicAdd(&cnt[key], __popc(peers));
+      }
+      keys[r] = key;
+    }
+    __syncthreads();
+    {
+      const int c = tid < nkeys ? cnt[tid] : 0;
+      int off;
+      Scan(scan).ExclusiveSum(c, off);
+      if (tid < nkeys) start[tid] = off;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int r = 0; r < CH / kCountThreads; ++r) {
+      if (r * kCountThreads >= len) break;
+      for (int k = lane; k < nkeys; k += 32) whist[warp][k] = 0;
+      __syncwarp();
+      const int key = keys[r];
+      const uint32_t act = __ballot_sync(0xffffffffu, key >= 0);
+      int rank = 0;
+      if (key >= 0) {
+        const uint32_t peers = __match_any_sync(act, key);
+        rank = __popc(peers & lt_mask);
+        if (rank == 0) whist[warp][key] = __popc(peers);
+      }
+      __syncthreads();
+      // per key: rows of the earlier warps of this round (exclusive), and the
+      // running count over the rounds
+      for (int k = tid; k < nkeys; k += kCountThreads) {
+        int off = run[k];
+#pragma unroll
+        for (int w = 0; w < kCountWarps; ++w) {
+          const int h = whist[w][k];
+          whist[w][k] = off;
+          off += h;
+        }
+        run[k] = off;
+      }
+      __syncthreads();
+      if (key >= 0) pv.perm[base + start[key] + whist[warp][key] + rank] = base + r * kCountThreads + tid;
+      __syncthreads();
+    }
+    // items of the valid keys: full ones first (key order), then partial ones
+    int nf = 0, np = 0, c = 0;
+    if (tid < S) {
+      c = cnt[tid];
+      nf = c / rows_per_item;
+      np = (c % rows_per_item) != 0 ? 1 : 0;
+    }
+    int off_f, off_p, tot_f, tot_p;
+    Scan(scan).ExclusiveSum(nf, off_f, tot_f);
+    __syncthreads();
+    Scan(scan).ExclusiveSum(np, off_p, tot_p);
+    const int item_base = s_counts[3];
+    if (tid < S && c > 0) {
+      const int p0 = base + start[tid];
+      for (int f = 0; f < nf; ++f)
+        pv.items[item_base + off_f + f] = make_int4(tid, p0 + f * rows_per_item, rows_per_item, 0);
+      if (np) pv.items[item_base + tot_f + off_p] = make_int4(tid, p0 + nf * rows_per_item, c - nf * rows_per_item, 0);
+    }
+    if (tid == 0) {
+      s_full = tot_f;
+      s_counts[0] += start[S];                 // valid rows: every key below S
+      s_counts[1] += cnt[S];
+      s_counts[2] += cnt[S + 1];
+      s_counts[3] = item_base + tot_f + tot_p;
+    }
+    __syncthreads();
+  }
+  (void)s_full;
+  if (tid == 0) {
+    pv.hdr[kHdrItems] = s_counts[3];
+    pv.hdr[kHdrValid] = s_counts[0];
+    pv.hdr[kHdrNull] = s_counts[1];
+    pv.hdr[kHdrBad] = s_counts[2];
+    pv.hdr[kHdrT] = T;
+    pv.hdr[kHdrS] = S;
+    pv.hdr[kHdrRowsPerItem] = rows_per_item;
+    pv.hdr[kHdrMagic] = kPlanMagic;
+    if (s_counts[2] > 0) raise_error(dev_err, PERSONA_DEV_ERR_SLOT);
+  }
+}
+
 cudaError_t launch_bgmv_plan(const int32_t* slots, int T, int S, int rows_per_item,
                              int32_t* plan, int32_t* dev_err, cudaStream_t stream) {
+  if (S + 2 <= kCountMaxKeys) {
+    // chunks as in bgmv_plan_kernel below
+    if (T <= 512)
+      bgmv_plan_count_kernel<512><<<1, kCountThreads, 0, stream>>>(slots, T, S, rows_per_item, plan, dev_err);
+    else if (T <= 1024)
+      bgmv_plan_count_kernel<1024><<<1, kCountThreads, 0, stream>>>(slots, T, S, rows_per_item, plan, dev_err);
+    else
+      bgmv_plan_count_kernel<2048><<<1, kCountThreads, 0, stream>>>(slots, T, S, rows_per_item, plan, dev_err);
+    return cudaGetLastError();
+  }
   if (T <= 256) {
     bgmv_plan_kernel<128, 2><<<1, 128, 0, stream>>>(slots, T, S, rows_per_item, plan, dev_err);
   } else if (T <= 512) {

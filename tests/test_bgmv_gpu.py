@@ -329,7 +329,7 @@ def test_fused_is_deterministic():
 
 # ------------------------------------------------------------------- plan --
 
-@pytest.mark.parametrize("T,S", [(1, 1), (8, 8), (255, 7), (256, 300), (257, 3), (512, 256), (600, 2),
+@pytest.mark.parametrize("T,S", [(1, 1), (8, 8), (255, 7), (256, 300), (257, 3), (512, 256), (600, 2), (300, 600), (1500, 2000),
                                  (2048, 256), (2049, 5), (5000, 3)])
 def test_plan_matches_oracle(T, S):
     rng = np.random.default_rng(T + S)
