@@ -213,6 +213,9 @@ __device__ void plan_units(SplitShared& sh, const SplitArgs& a, int n_items, int
   sh.units = s_units + e_units;
 }
 
+__device__ __forceinline__ void sts16(uint32_t addr, uint16_t v) {
+  asm volatile("st.shared.u16 [%0], %1;" ::"r"(addr), "h"(v) : "memory");
+}
 __device__ __forceinline__ void sts32(uint32_t addr, uint32_t v) {
   asm volatile("st.shared.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
 }
@@ -864,17 +867,34 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
               }
             }
             tc::fence_before_sync();
-            __syncwarp();
-            if (lane == 0 && ok) mbar_arrive_relaxed(&sm.empty[s]);
+            // The new values go back into the staged y tile (this thread's
+            // column), then each lane stores 16-byte runs of 8 columns of one
+            // row: a warp's 32 columns of c rows take 4c vector stores instead
+            // of 32c two-byte ones.
 #pragma unroll
             for (int b = 0; b < 2; ++b) {
-              const int n = n0 + b * 128 + quarter * 32 + lane;
-              if (b < nbt && n < nhi) {
+              if (b < nbt) {
+                const int n = b * 128 + quarter * 32 + lane;
 #pragma unroll
                 for (int t = 0; t < kRowsPerItem; ++t)
-                  if (t < c) y[static_cast<int64_t>(rows[t]) * pr.ldy + n] = out[b][t];
+                  if (t < c) sts16(ytile + t * C::kYStride + n * 2, out[b][t]);
               }
             }
+            __syncwarp();
+#pragma unroll
+            for (int b = 0; b < 2; ++b) {
+              if (b < nbt) {
+                for (int q = lane; q < 4 * c; q += 32) {
+                  const int t = q >> 2, col = b * 128 + quarter * 32 + (q & 3) * 8;
+                  if (n0 + col < nhi) {  // nhi and the column are multiples of 8
+                    const uint4 val = lds128(ytile + t * C::kYStride + col * 2);
+                    *reinterpret_cast<uint4*>(y + static_cast<int64_t>(rows[t]) * pr.ldy + n0 + col) = val;
+                  }
+                }
+              }
+            }
+            __syncwarp();
+            if (lane == 0 && ok) mbar_arrive_relaxed(&sm.empty[s]);
           }
         } else {
           uint32_t vhi[C::kKSteps][4], vlo[C::kKSteps][4];
