@@ -122,6 +122,35 @@ def test_partition_rows_single_rank_and_validation():
     assert partition_rows(slots, 1, 100, 10)[0].tolist() == [0, 2, 3, 4]
     with pytest.raises(ValueError):
         partition_rows(slots, 0, 100, 10)
+    with pytest.raises(ValueError):
+        partition_rows(slots, 2, 100, 10, rows_per_item=0)
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_partition_rows_balances_item_loads(world):
+    """Zipf batch of 512 rows per rank: every active row lands on exactly one
+    rank, a split adapter is cut at whole 16-row items (only its last piece
+    may be partial), and the per-item load -- one adapter read per 16-row
+    item plus the rows' bytes -- is balanced within 10% across ranks."""
+    rng = np.random.Generator(np.random.PCG64(2))
+    slots = workloads.zipf_slots(rng, 512 * world, 256)
+    ab, rb = 64 * 81920 * 2, 124928 * 2  # rank 64, the 7 projections of one layer
+    parts = partition_rows(slots, world, ab, rb)
+    seen = np.zeros(slots.size, np.int64)
+    for p in parts:
+        seen[p] += 1
+    assert np.array_equal(seen, (slots >= 0).astype(np.int64))
+    loads = []
+    for p in parts:
+        s = slots[p]
+        _, c = np.unique(s, return_counts=True)
+        loads.append(int(np.sum(-(-c // 16))) * ab + s.size * rb)
+    assert max(loads) <= 1.1 * (sum(loads) / world)
+    for slot in np.unique(slots[slots >= 0]):
+        per_rank = [int(np.sum(slots[p] == slot)) for p in parts]
+        split = [n for n in per_rank if n > 0]
+        if len(split) > 1:
+            assert sum(n % 16 != 0 for n in split) <= 1
 
 
 @pytest.mark.parametrize("worker", [_row_shard_worker, _tp_worker])

@@ -82,7 +82,7 @@ def _worker(rank, world, port, dtype_name, R):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [2, 4])
+@pytest.mark.parametrize("world", [2, 4, 8])
 @pytest.mark.parametrize("dtype_name,R", [("bf16", 16), ("f16", 32)])
 def test_tensor_parallel_sgmv(world, dtype_name, R):
     if torch.cuda.device_count() < world:
