@@ -483,7 +483,7 @@ def run_ours(args):
         achieved = step_bytes / (fused_ms_per_step * 1e-3) / 1e9
         traffic = None
         tf = ROOT / "profiles" / "bgmv_fused_mixed_batch_traffic.json"
-        if tf.exists() and world == 1:  # captured on the one-GPU launch (512 rows)
+        if tf.exists() and world == 1 and len(projs) == 7:  # captured on the one-GPU 7-projection launch
             traffic = json.loads(tf.read_text()).get("traffic_bytes_per_launch")
         line = {
             "metric": METRIC,
@@ -1047,8 +1047,8 @@ def run_decode_kernels(args):
     slots = torch.from_numpy(global_slots(1).astype(np.int32)).to(dev)
     ms = _timed(lambda: ops.bgmv_plan(slots, POOL_SLOTS), warm, stream)
     ms = _timed(lambda: ops.bgmv_plan(slots, POOL_SLOTS), steps, stream)
-    print(json.dumps({"workload": "decode_kernels", "kernel": "bgmv_plan_kernel",
-                      "metric": "row-grouping plan of the 512-row Zipf batch, us per launch", "value": ms * 1e3,
+    print(json.dumps({"workload": "decode_kernels", "kernel": "bgmv_plan_count_kernel<512> (one CTA; pools up to 510 slots)",
+                      "metric": "row-grouping plan of the 512-row Zipf batch, us per ops.bgmv_plan call", "value": ms * 1e3,
                       "unit": "us", "higher_is_better": False, "n_gpus": 1, "steps": steps, "warmup": warm,
                       "config": {"rows": ROWS_PER_GPU, "pool_slots": POOL_SLOTS}}), flush=True)
     B, Hq, Hkv, L, D, layers = 8, 32, 8, 256, 128, 32
