@@ -461,24 +461,12 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
       if (lane == 0) mbar_arrive(&sm.ufull[iq]);
       if (d.kind == kUnitEnd) break;
 
-      // The next unit's claim has returned by now; issue the one after it,
-      // and start loading the next unit's item record.
-      const int u_next = claim_read(pending);
-      pending = u_next < units ? claim_issue() : 0;
-      const Dec dn = decode(u_next);
-      const int4 itn = dn.kind != kUnitEnd ? pv.items[dn.item] : make_int4(0, 0, 0, 0);
-      const int rdn = MODE == kModeFused && dn.kind == kUnitExpand && lane == 0 ? ld_relaxed(ready_word(dn)) : 0;
-      int rown = 0;
-      bool rows_loaded = false;
-      auto load_next_rows = [&]() {  // once itn has arrived: after the first stage is issued
-        if (!rows_loaded) {
-          rows_loaded = true;
-          if (dn.kind != kUnitEnd && item_ok(itn) && lane < itn.z) rown = pv.perm[itn.y + lane];
-        }
-      };
-
       const int slot = it.x, c = it.z;
       const SplitProblem& pr = args.prob[d.prob];
+      // Fused expand unit: acquire the item's v and start its copy before the
+      // next unit's loads are issued, so the acquire fence waits for none of
+      // them (after them it held the copy, and the first stage's loads behind
+      // it, back by about 2 us per unit).
       if (MODE == kModeFused && d.kind == kUnitExpand) {
         int vok = 1;
         if (lane == 0) {
@@ -504,6 +492,22 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
         else
           dead = true;
       }
+      // The next unit's claim has returned by now; issue the one after it,
+      // and start loading the next unit's item record.
+      const int u_next = claim_read(pending);
+      pending = u_next < units ? claim_issue() : 0;
+      const Dec dn = decode(u_next);
+      const int4 itn = dn.kind != kUnitEnd ? pv.items[dn.item] : make_int4(0, 0, 0, 0);
+      const int rdn = MODE == kModeFused && dn.kind == kUnitExpand && lane == 0 ? ld_relaxed(ready_word(dn)) : 0;
+      int rown = 0;
+      bool rows_loaded = false;
+      auto load_next_rows = [&]() {  // once itn has arrived: after the first stage is issued
+        if (!rows_loaded) {
+          rows_loaded = true;
+          if (dn.kind != kUnitEnd && item_ok(itn) && lane < itn.z) rown = pv.perm[itn.y + lane];
+        }
+      };
+
       if (d.kind == kUnitShrink) {
         const uint16_t* x = static_cast<const uint16_t*>(pr.x);
         for (int k0 = d.lo; !dead && k0 < d.hi; k0 += C::kKC) {
