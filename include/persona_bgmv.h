@@ -199,8 +199,7 @@ int persona_sgmv_fused(const void* x, int64_t ldx, const void* a_pool, int64_t a
  *  - T <= PERSONA_NOALLOC_MAX_ROWS; a larger T returns
  *    PERSONA_ERR_NOALLOC_ROWS and enqueues nothing.
  *  - The first call on a device looks the array's device address up
- *    (cudaGetSymbolAddress, with that device current); make that first call
- *    before any stream capture begins.
+ *    (cudaGetSymbolAddress, with that device current) and keeps it.
  *  - Nothing in the array has to start at zero: each call rewrites the plan
  *    and resets the counters before the kernel reads them.  Calls of at most
  *    PERSONA_SMALL_MAX_ROWS rows run the decode-sized kernel and do not
