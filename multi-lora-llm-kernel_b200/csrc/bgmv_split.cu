@@ -91,6 +91,7 @@ struct SplitShared {
   ProbGeom geom[kMaxProblems];
   int sorder[kMaxProblems], eorder[kMaxProblems];  // problems in claim order (longest units first)
   int units_s, units;
+  int first[kGroups];  // each pipeline's first claimed unit
   uint32_t tmem;
   int abort;  // set by the first wait of the CTA that gives up
 };
@@ -155,62 +156,81 @@ __device__ __forceinline__ SplitSmem carve(uint8_t* raw, int grp) {
 
 // Slice counts for every problem: about units_per_cta units per pipeline in
 // total, shared between the problems by their stage counts and, within a
-// problem, between shrink and expand by theirs.  Run by one thread.
-__device__ void plan_units(SplitShared& sh, const SplitArgs& a, int n_items, int kc, int nb_rows, int pipes,
-                           bool shrink, bool expand) {
-  const int P = a.num_problems;
+// problem, between shrink and expand by theirs.  Run by one warp, lane p for
+// problem p (the divisions of all problems run side by side: done by one
+// thread they took 5 us at the start of every launch of seven problems).
+__device__ __noinline__ void plan_units(SplitShared& sh, int K, int N, int n_box, int P, int units_per_cta,
+                                        int n_items, int kc, int nb_rows, int pipes, bool shrink, bool expand,
+                                        int lane) {
   const int items = n_items > 0 ? n_items : 1;
   // Many items (large batches): small units, so the tail stays short.  Few
   // items (decode): fewer, larger units, so the latency chain shrink slice ->
   // finisher -> expand slice has fewer links per item.
-  const int upc = a.units_per_cta > 0 ? a.units_per_cta : n_items >= kManyItems ? kUnitsPerCtaMany : kUnitsPerCta;
-  int work = 0;
-  for (int p = 0; p < P; ++p) {
-    ProbGeom& g = sh.geom[p];
-    g.stage_rows = (nb_rows / a.prob[p].n_box) * a.prob[p].n_box;
-    g.kst = shrink ? (a.prob[p].K + kc - 1) / kc : 0;
-    g.nst = expand ? (a.prob[p].N + g.stage_rows - 1) / g.stage_rows : 0;
-    work += g.kst + g.nst;
+  const int upc = units_per_cta > 0 ? units_per_cta : n_items >= kManyItems ? kUnitsPerCtaMany : kUnitsPerCta;
+  const bool mine = lane < P;
+  int kst = 0, nst = 0, stage_rows = 0;
+  if (mine) {
+    stage_rows = (nb_rows / n_box) * n_box;
+    kst = shrink ? (K + kc - 1) / kc : 0;
+    nst = expand ? (N + stage_rows - 1) / stage_rows : 0;
   }
-  int s_units = 0, e_units = 0;
-  for (int p = 0; p < P; ++p) {
-    ProbGeom& g = sh.geom[p];
-    const long long budget = static_cast<long long>(upc) * pipes * (g.kst + g.nst) / (work > 0 ? work : 1);
+  int work = kst + nst;
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) work += __shfl_xor_sync(0xffffffffu, work, off);
+  int ks_st = 0, es_st = 0, nks = 0, nes = 0;
+  if (mine) {
+    const long long budget = static_cast<long long>(upc) * pipes * (kst + nst) / (work > 0 ? work : 1);
     const int per_item = max(1, static_cast<int>((budget + items - 1) / items));
-    int nks = 1, nes = 1;
+    int n1 = 1, n2 = 1;
     if (shrink && expand) {
-      nks = max(1, (per_item * g.kst + (g.kst + g.nst) / 2) / max(1, g.kst + g.nst));
-      nes = max(1, per_item - nks);
+      n1 = max(1, (per_item * kst + (kst + nst) / 2) / max(1, kst + nst));
+      n2 = max(1, per_item - n1);
     } else if (shrink) {
-      nks = per_item;
+      n1 = per_item;
     } else {
-      nes = per_item;
+      n2 = per_item;
     }
-    nks = min(min(nks, max(1, g.kst)), max(1, kPartSlots / (items * P)));
-    nes = min(nes, max(1, g.nst));
-    g.ks_st = shrink ? (g.kst + nks - 1) / nks : 0;
-    g.nks = shrink ? (g.kst + g.ks_st - 1) / g.ks_st : 0;
-    g.es_st = expand ? (g.nst + nes - 1) / nes : 0;
-    g.nes = expand ? (g.nst + g.es_st - 1) / g.es_st : 0;
+    n1 = min(min(n1, max(1, kst)), max(1, kPartSlots / (items * P)));
+    n2 = min(n2, max(1, nst));
+    ks_st = shrink ? (kst + n1 - 1) / n1 : 0;
+    nks = shrink ? (kst + ks_st - 1) / ks_st : 0;
+    es_st = expand ? (nst + n2 - 1) / n2 : 0;
+    nes = expand ? (nst + es_st - 1) / es_st : 0;
   }
   // Claim order inside each phase: problem by problem, the same order in
   // both phases, so an expand unit's item was shrunk long before (ordering
   // the phases by unit length instead made the first expand units wait for
-  // the last shrink units: 356 against 306 us per launch).
-  for (int q = 0; q < P; ++q) sh.sorder[q] = sh.eorder[q] = q;
-  for (int q = 0; q < P; ++q) {
-    ProbGeom& g = sh.geom[sh.sorder[q]];
-    g.s_base = s_units;
-    g.p_base = s_units;  // partial slots follow the shrink units one to one
-    s_units += n_items * g.nks;
+  // the last shrink units: 356 against 306 us per launch).  Unit bases are
+  // prefix sums over the lanes.
+  const int s_cnt = mine ? n_items * nks : 0, e_cnt = mine ? n_items * nes : 0;
+  int s_inc = s_cnt, e_inc = e_cnt;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const int ts = __shfl_up_sync(0xffffffffu, s_inc, off), te = __shfl_up_sync(0xffffffffu, e_inc, off);
+    if (lane >= off) {
+      s_inc += ts;
+      e_inc += te;
+    }
   }
-  for (int q = 0; q < P; ++q) {
-    ProbGeom& g = sh.geom[sh.eorder[q]];
-    g.e_base = s_units + e_units;
-    e_units += n_items * g.nes;
+  const int s_units = __shfl_sync(0xffffffffu, s_inc, 31), e_units = __shfl_sync(0xffffffffu, e_inc, 31);
+  if (mine) {
+    ProbGeom& g = sh.geom[lane];
+    g.kst = kst;
+    g.nst = nst;
+    g.stage_rows = stage_rows;
+    g.ks_st = ks_st;
+    g.nks = nks;
+    g.es_st = es_st;
+    g.nes = nes;
+    g.s_base = s_inc - s_cnt;
+    g.p_base = g.s_base;  // partial slots follow the shrink units one to one
+    g.e_base = s_units + e_inc - e_cnt;
+    sh.sorder[lane] = sh.eorder[lane] = lane;
   }
-  sh.units_s = s_units;
-  sh.units = s_units + e_units;
+  if (lane == 0) {
+    sh.units_s = s_units;
+    sh.units = s_units + e_units;
+  }
 }
 
 __device__ __forceinline__ void sts16(uint32_t addr, uint16_t v) {
@@ -332,14 +352,28 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
   const bool plan_ok = pv.hdr[kHdrMagic] == kPlanMagic && pv.hdr[kHdrT] == args.T && pv.hdr[kHdrS] == args.S &&
                        pv.hdr[kHdrRowsPerItem] == kRowsPerItem && n_items >= 0 && n_items <= tpad;
   const int epoch = wv.sync[kSyncEpoch];
-  if (threadIdx.x == 0) {
-    sh.abort = 0;
+  // Each producer's first claim goes out now; its round trip overlaps the
+  // unit geometry below.
+  if (plan_ok && warp == kConsumerWarps && lane == 0) sh.first[grp] = atomicAdd(&wv.sync[kSyncQueue], 1);
+  if (threadIdx.x < 32) {
     if (plan_ok) {
-      plan_units(sh, args, n_items, C::kKC, C::kNB, static_cast<int>(gridDim.x) * kGroups, kDoShrink, kDoExpand);
-    } else {
+      // lane p takes problem p's sizes (constant indices: no local copy of the arguments)
+      int pk = 0, pn = 0, pb = 1;
+#pragma unroll
+      for (int q = 0; q < kMaxProblems; ++q) {
+        if (static_cast<int>(threadIdx.x) == q && q < P) {
+          pk = args.prob[q].K;
+          pn = args.prob[q].N;
+          pb = args.prob[q].n_box;
+        }
+      }
+      plan_units(sh, pk, pn, pb, P, args.units_per_cta, n_items, C::kKC, C::kNB,
+                 static_cast<int>(gridDim.x) * kGroups, kDoShrink, kDoExpand, static_cast<int>(threadIdx.x));
+    } else if (threadIdx.x == 0) {
       sh.units_s = sh.units = 0;
       if (blockIdx.x == 0) raise_error(args.err, PERSONA_DEV_ERR_PLAN);
     }
+    if (threadIdx.x == 0) sh.abort = 0;
   }
   tc::fence_before_sync();
   __syncthreads();
@@ -418,7 +452,7 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
     auto item_ok = [&](const int4& q) {
       return q.x >= 0 && q.x < args.S && q.z >= 1 && q.z <= kRowsPerItem && q.y >= 0 && q.y <= args.T - q.z;
     };
-    int u = claim_read(claim_issue());
+    int u = sh.first[grp];
     int pending = u < units ? claim_issue() : 0;
     // The item record and rows of the next unit are loaded while the current
     // unit's stages are issued, so no unit waits on them.
