@@ -37,6 +37,8 @@
 // not wait for the count.
 #include <cuda_fp16.h>
 
+#include <atomic>
+
 #include "common.cuh"
 #include "nf4_args.h"
 #include "tcgen05.cuh"
@@ -616,20 +618,22 @@ static cudaError_t gemm_launch(const Nf4Maps& maps, const Nf4GemmArgs& args, cud
   auto kern = nf4_gemm_kernel<MT>;
   constexpr int smem = Nf4Cfg<MT>::kSmem;
   constexpr int kMaxDev = 64;
-  static int per_sm[kMaxDev] = {};
+  // CTAs per SM, per device; racing first calls compute the same value
+  static std::atomic<int> per_sm[kMaxDev];
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= kMaxDev) return cudaErrorInvalidDevice;
-  if (per_sm[dev] == 0) {
+  int occ = per_sm[dev].load(std::memory_order_acquire);
+  if (occ == 0) {
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
-    int occ = 0;
     e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kNf4Threads, smem);
     if (e != cudaSuccess) return e;
-    per_sm[dev] = occ > 0 ? occ : 1;
+    if (occ < 1) occ = 1;
+    per_sm[dev].store(occ, std::memory_order_release);
   }
-  const int ctas = per_sm[dev] * nf4_sm_count();
+  const int ctas = occ * nf4_sm_count();
   // never more CTAs than chunks, nor than the partial buffer was sized for
   int grid = ctas < args.max_ctas ? ctas : args.max_ctas;
   if (grid < 1) grid = 1;
