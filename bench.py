@@ -64,6 +64,8 @@ def parse_args():
     ap.add_argument("--batch", type=int, default=None,
                     help="e2e_decode: rows per GPU (default 8 on one GPU, 64 per replica on several); "
                          "nf4_decode: rows of x (default 8)")
+    ap.add_argument("--sgmv-rank", type=int, default=16, choices=[16, 32, 64],
+                    help="adapter rank of --workload sgmv_prefill on one GPU (16: the segmented prefill config)")
     ap.add_argument("--only", default=None,
                     help="restrict to one projection (e.g. gate_proj), for profiling a small case")
     return ap.parse_args()
@@ -585,8 +587,8 @@ def run_extra(args):
         return a, b
 
     if args.workload == "sgmv_prefill":
-        # 32 requests x 512 rows, rank 16, 32 adapters, bf16; gate/up/down.
-        req, rows, R, S = 32, 512, 16, 32
+        # 32 requests x 512 rows, rank 16 (or --sgmv-rank), 32 adapters, bf16; gate/up/down.
+        req, rows, R, S = 32, 512, args.sgmv_rank, 32
         T = req * rows
         rng = np.random.Generator(np.random.PCG64(SEED + 1))
         seg = rng.permutation(req).astype(np.int32)
@@ -638,7 +640,7 @@ def run_extra(args):
             "workload": "sgmv_prefill", "metric": "SGMV fused shrink+expand GB/s (algorithmic)",
             "value": tot_b / (ms * 1e-3) / 1e9, "unit": "GB/s", "n_gpus": 1, "steps": steps, "warmup": warm,
             "ms_per_step": ms, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "segmented prefill: 32 requests x 512 rows contiguous by adapter, rank 16, "
+            "config": {"workload": f"segmented prefill: 32 requests x 512 rows contiguous by adapter, rank {R}, "
                                    "32-slot pool, bf16", "projections": names,
                        "l2": "inputs larger than L2 (~2.9 GB per step)"},
             "per_projection": {n: {"ms": t, "GB/s": p["bytes"] / (t * 1e-3) / 1e9,

@@ -222,7 +222,7 @@ int persona_bgmv_fused_noalloc(const void* x, int64_t ldx, const void* a_pool, i
  * y of every other rank: peer_ys[0..num_peers) are those ranks' y buffers
  * mapped into this process (persona_ipc_import), same shape and ldy.  After
  * the launch and a cross-rank barrier (any collective on this stream) every
- * rank holds the full updated y.  Tensor-core shapes only: R in {16, 32},
+ * rank holds the full updated y.  Tensor-core shapes only: R in {16, 32, 64},
  * K % 64 == 0, N % 64 == 0, n0 and n1 multiples of 64; at most
  * PERSONA_MAX_TP_PEERS peers.  The ranks' y must hold the same values before
  * the call (rows outside every segment are not written).                   */

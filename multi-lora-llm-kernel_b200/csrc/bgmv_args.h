@@ -24,8 +24,9 @@ cudaError_t launch_sgmv_plan(const int32_t* indptr, const int32_t* seg_slots, in
                              int rows_per_item, int32_t* plan, int32_t* row_slots, int32_t* dev_err,
                              cudaStream_t stream, int32_t* item_state = nullptr, int item_state_stride = 0);
 constexpr int kSgmvMaxCtas = 160;  // CTAs of a tensor-core SGMV launch (pieces are sized for it)
-// Bytes of the pieces region of the SGMV workspace (two pieces of 128 x 32 fp32 per CTA).
-constexpr size_t kSgmvPieceBytes = static_cast<size_t>(2) * kSgmvMaxCtas * 128 * 32 * 4;
+// Bytes of the pieces region of the SGMV workspace (two pieces of 128 x R
+// fp32 per CTA, R <= 64).
+constexpr size_t kSgmvPieceBytes = static_cast<size_t>(2) * kSgmvMaxCtas * 128 * 64 * 4;
 int bgmv_stage_rows(int R);  // B rows one ring slot holds at rank R
 // Split kernels (bgmv_split.cu): every item of every problem cut into K / N
 // slices claimed by all CTAs; workspace = bgmv_ws_bytes(T, problems)

@@ -470,14 +470,14 @@ int sgmv_prepare(const int32_t* seg_indptr, const int32_t* seg_slots, int64_t ns
 }  // namespace
 
 namespace {
-// Tensor-core path: ranks 16 / 32, K and N multiples of 64.
+// Tensor-core path: ranks 16 / 32 / 64, K and N multiples of 64.
 // PERSONA_SGMV_TENSOR_CORES=0 selects the BGMV split path instead.
 bool sgmv_tc_eligible(int64_t R, int64_t K, int64_t N, bool need_k, bool need_n) {
   static const bool enabled = [] {
     const char* e = std::getenv("PERSONA_SGMV_TENSOR_CORES");
     return !(e != nullptr && e[0] == '0');
   }();
-  if (!enabled || !(R == 16 || R == 32)) return false;
+  if (!enabled || !(R == 16 || R == 32 || R == 64)) return false;
   if (need_k && (K % 64 != 0 || K <= 0)) return false;
   if (need_n && (N % 64 != 0 || N <= 0)) return false;
   return true;
@@ -567,7 +567,7 @@ int persona_sgmv_fused_tp(const void* x, int64_t ldx, const void* a_pool, int64_
                           int64_t S, int dtype, void* workspace, size_t workspace_bytes, int32_t* dev_err,
                           cudaStream_t stream) {
   if (dtype != PERSONA_DTYPE_F16 && dtype != PERSONA_DTYPE_BF16) return PERSONA_ERR_DTYPE;
-  if (!(R == 16 || R == 32)) return PERSONA_ERR_RANK;
+  if (!(R == 16 || R == 32 || R == 64)) return PERSONA_ERR_RANK;
   if (K <= 0 || K % 64 != 0 || N <= 0 || N % 64 != 0) return PERSONA_ERR_SHAPE;
   return sgmv_tc_run(persona::kModeFused, x, ldx, a_pool, a_slot_stride, a_row_stride, b_pool, b_slot_stride,
                      seg_indptr, seg_slots, num_segments, nullptr, nullptr, y, ldy, T, K, N, R, S, dtype, workspace,

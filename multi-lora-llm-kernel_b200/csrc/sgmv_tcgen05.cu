@@ -57,19 +57,23 @@ constexpr int kSmemPerBlock = 227 * 1024;  // opt-in maximum per block on sm_100
 // Sharing the ring keeps ~200 KB of loads in flight in either phase.
 template <int R>
 struct TcCfg {
-  static_assert(R == 16 || R == 32, "tensor-core SGMV ranks");
+  static_assert(R == 16 || R == 32 || R == 64, "tensor-core SGMV ranks");
   static constexpr int kBoxBytes = kTcRows * 128;      // one x / y box: 16 KB
   static constexpr int kTileBytes = kBoxes * kBoxBytes;
   static constexpr int kABox = R * 128;                // one A box
   static constexpr int kABytes = kBoxes * kABox;
   static constexpr int kBBytes = kTcNT * R * 2;
   static constexpr int kSlotBytes = kTileBytes + (kABytes > kBBytes ? kABytes : kBBytes);
-  static constexpr int kVBytes = kTcRows * 128;  // V' rows of 128 bytes (hi | lo | 0)
+  // V': rows of 128 bytes [hi | lo | 0] up to rank 32; at rank 64 one
+  // 128-byte-row block of hi, then one of lo.
+  static constexpr int kVBytes = kTcRows * 128 * (R <= 32 ? 1 : 2);
+  // byte offset of K step ks of the lo half inside V'
+  __host__ __device__ static constexpr uint32_t lo_off(int ks) { return R <= 32 ? (R / 16 + ks) * 32 : kTcRows * 128 + ks * 32; }
   static constexpr int kSlots = (kSmemPerBlock - 2048 - kVBytes) / kSlotBytes < kMaxSlots
                                     ? (kSmemPerBlock - 2048 - kVBytes) / kSlotBytes
                                     : kMaxSlots;
   static constexpr int kSmem = kSlots * kSlotBytes + kVBytes;
-  static constexpr uint32_t kBLayout = R == 16 ? tc::kLayoutSw32 : tc::kLayoutSw64;
+  static constexpr uint32_t kBLayout = R == 16 ? tc::kLayoutSw32 : R == 32 ? tc::kLayoutSw64 : tc::kLayoutSw128;
   static constexpr uint32_t kBSbo = 8 * 2 * R;  // 8 rows of 2R bytes
   static_assert(kSlotBytes % 1024 == 0, "slot alignment");
   static_assert(kSlots >= 4, "ring depth");
@@ -348,7 +352,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           for (int ks = 0; ks < R / 16; ++ks) {
             const uint64_t b = tc::smem_desc(sb + ks * 32, C::kBSbo, C::kBLayout);
             tc::mma_f16(d_y, tc::smem_desc(sv + ks * 32, 1024, tc::kLayoutSw128), b, kIdescY, ks > 0 ? 1u : 0u);
-            tc::mma_f16(d_y, tc::smem_desc(sv + (R / 16 + ks) * 32, 1024, tc::kLayoutSw128), b, kIdescY, 1u);
+            tc::mma_f16(d_y, tc::smem_desc(sv + C::lo_off(ks), 1024, tc::kLayoutSw128), b, kIdescY, 1u);
           }
           tc::commit(&bars.acc_full[buf]);  // the epilogue releases the slot (it also holds the y tile)
         }
@@ -486,23 +490,40 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         scale_down = __uint_as_float(static_cast<uint32_t>(127 - e2) << 23);
         scale_up = __uint_as_float(static_cast<uint32_t>(127 + e2) << 23);
       }
-      // V' row: [hi(R) | lo(R) | zeros] as 16-bit, 128-byte swizzled rows.
-      uint32_t w[32];
+      // V' as 16-bit, 128-byte swizzled rows: [hi(R) | lo(R) | zeros] up to
+      // rank 32; at rank 64 a block of hi rows, then a block of lo rows.
+      auto store_row = [&](uint32_t vrow, const uint32_t* w) {
 #pragma unroll
-      for (int i = 0; i < R; i += 2) {
-        const float a = v[i] * scale_down, b = v[i + 1] * scale_down;
-        const float ha = Mma<DT>::round_trip(a), hb = Mma<DT>::round_trip(b);
-        w[i / 2] = Mma<DT>::pack(ha, hb);
-        w[R / 2 + i / 2] = Mma<DT>::pack(a - ha, b - hb);
+        for (int c = 0; c < 8; ++c)
+          asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(vrow + ((c ^ (row & 7)) << 4)),
+                       "r"(w[4 * c]), "r"(w[4 * c + 1]), "r"(w[4 * c + 2]), "r"(w[4 * c + 3])
+                       : "memory");
+      };
+      if constexpr (R <= 32) {
+        uint32_t w[32];
+#pragma unroll
+        for (int i = 0; i < R; i += 2) {
+          const float a = v[i] * scale_down, b = v[i + 1] * scale_down;
+          const float ha = Mma<DT>::round_trip(a), hb = Mma<DT>::round_trip(b);
+          w[i / 2] = Mma<DT>::pack(ha, hb);
+          w[R / 2 + i / 2] = Mma<DT>::pack(a - ha, b - hb);
+        }
+#pragma unroll
+        for (int i = R; i < 32; ++i) w[i] = 0u;
+        store_row(smem_u32(vsm) + row * 128, w);
+      } else {
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          uint32_t w[32];
+#pragma unroll
+          for (int i = 0; i < R; i += 2) {
+            const float a = v[i] * scale_down, b = v[i + 1] * scale_down;
+            const float ha = Mma<DT>::round_trip(a), hb = Mma<DT>::round_trip(b);
+            w[i / 2] = half == 0 ? Mma<DT>::pack(ha, hb) : Mma<DT>::pack(a - ha, b - hb);
+          }
+          store_row(smem_u32(vsm) + half * (kTcRows * 128) + row * 128, w);
+        }
       }
-#pragma unroll
-      for (int i = R; i < 32; ++i) w[i] = 0u;
-      const uint32_t vrow = smem_u32(vsm) + row * 128;
-#pragma unroll
-      for (int c = 0; c < 8; ++c)
-        asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(vrow + ((c ^ (row & 7)) << 4)),
-                     "r"(w[4 * c]), "r"(w[4 * c + 1]), "r"(w[4 * c + 2]), "r"(w[4 * c + 3])
-                     : "memory");
       tc::fence_proxy_async();
       named_sync(kEpiBar, 128);
       if (ew == 0 && lane == 0) mbar_arrive(&bars.vsm_ready);
@@ -686,8 +707,9 @@ static cudaError_t tc_launch(const CUtensorMap& tx, const CUtensorMap& ta, const
 template <typename DT, int MODE>
 static cudaError_t tc_rank(int R, const CUtensorMap& tx, const CUtensorMap& ta, const CUtensorMap& tb,
                            const CUtensorMap& ty, const SgmvTcArgs& a, int max_items, cudaStream_t st) {
-  return R == 16 ? tc_launch<DT, 16, MODE>(tx, ta, tb, ty, a, max_items, st)
-                 : tc_launch<DT, 32, MODE>(tx, ta, tb, ty, a, max_items, st);
+  return R == 16   ? tc_launch<DT, 16, MODE>(tx, ta, tb, ty, a, max_items, st)
+         : R == 32 ? tc_launch<DT, 32, MODE>(tx, ta, tb, ty, a, max_items, st)
+                   : tc_launch<DT, 64, MODE>(tx, ta, tb, ty, a, max_items, st);
 }
 
 cudaError_t launch_sgmv_tc(int mode, int dtype, int R, const CUtensorMap& tx, const CUtensorMap& ta,

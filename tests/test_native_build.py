@@ -65,7 +65,7 @@ def test_workspace_size_matches_layout(built):
         assert lib.persona_bgmv_workspace_size(T) == total(1)
         # + per-row slots, then the tensor-core kernel's partial-v pieces:
         # two of 128 x 32 fp32 for each of at most 160 CTAs
-        assert lib.persona_sgmv_workspace_size(T) == a256(total(1) + 4 * tp) + 2 * 160 * 128 * 32 * 4
+        assert lib.persona_sgmv_workspace_size(T) == a256(total(1) + 4 * tp) + 2 * 160 * 128 * 64 * 4
         for p in (1, 3, 8):
             assert lib.persona_bgmv_multi_workspace_size(T, p) == total(p)
         assert lib.persona_bgmv_multi_workspace_size(T, 9) == 0

@@ -1,4 +1,4 @@
-"""SGMV on the tensor-core path (ranks 16 / 32, K % 64 == 0, N % 64 == 0)
+"""SGMV on the tensor-core path (ranks 16 / 32 / 64, K % 64 == 0, N % 64 == 0)
 against the oracle: ragged segments that straddle the 128-row items, holes,
 slot -1 segments, both 16-bit types, strided y, and the C ABI."""
 
@@ -75,7 +75,7 @@ CASES = [
 
 
 @pytest.mark.parametrize("dtype", ["bf16", "f16"])
-@pytest.mark.parametrize("R", [16, 32])
+@pytest.mark.parametrize("R", [16, 32, 64])
 @pytest.mark.parametrize("ci", range(len(CASES)))
 def test_sgmv_tensor_core_matches_oracle(dtype, R, ci):
     lens, K, N = CASES[ci]
@@ -105,10 +105,11 @@ def test_sgmv_tensor_core_matches_oracle(dtype, R, ci):
     no_device_error()
 
 
-def test_sgmv_tensor_core_f16_large_intermediate():
+@pytest.mark.parametrize("R", [16, 64])
+def test_sgmv_tensor_core_f16_large_intermediate(R):
     """|v| far above the f16 range: the per-row power-of-two scale keeps the
     16-bit halves of v finite; y stays within f16."""
-    dtype, R, K, N, S = "f16", 16, 256, 256, 3
+    dtype, K, N, S = "f16", 256, 256, 3
     indptr, seg, x, a, b, y0 = ragged_case(5, [200, 60], K, N, R, S, dtype, x_scale=4000.0)
     a = O.from_f32(f32(a, dtype) * 32.0, dtype)
     b = O.from_f32(f32(b, dtype) * 1e-3, dtype)

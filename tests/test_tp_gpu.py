@@ -83,7 +83,7 @@ def _worker(rank, world, port, dtype_name, R):
 
 
 @pytest.mark.parametrize("world", [2, 4, 8])
-@pytest.mark.parametrize("dtype_name,R", [("bf16", 16), ("f16", 32)])
+@pytest.mark.parametrize("dtype_name,R", [("bf16", 16), ("f16", 32), ("bf16", 64)])
 def test_tensor_parallel_sgmv(world, dtype_name, R):
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
