@@ -109,7 +109,7 @@ def sgmv_fused_tp_nvlink(x: torch.Tensor, a_pool: torch.Tensor, b_pool: torch.Te
                          group: Optional[dist.ProcessGroup] = None) -> torch.Tensor:
     """Same result as ``sgmv_fused_tp``, with the all-gather fused into the
     kernel (NVLink stores of each finished tile into the other ranks' y).
-    Tensor-core shapes only (rank 16 / 32, K % 64 == 0, N % 64 == 0)."""
+    Tensor-core shapes only (rank 16 / 32 / 64, K % 64 == 0, N % 64 == 0)."""
     from persona import ops
 
     ext = ops._load()
