@@ -198,8 +198,10 @@ int persona_sgmv_fused(const void* x, int64_t ldx, const void* a_pool, int64_t a
  * Limits and rules:
  *  - T <= PERSONA_NOALLOC_MAX_ROWS; a larger T returns
  *    PERSONA_ERR_NOALLOC_ROWS and enqueues nothing.
- *  - The first call on a device looks the array's device address up
- *    (cudaGetSymbolAddress, with that device current) and keeps it.
+ *  - The first call on a device does a one-time set-up: it looks the
+ *    array's device address up (cudaGetSymbolAddress, with that device
+ *    current) and keeps it.  Make that first call on each device before any
+ *    stream capture begins.
  *  - Nothing in the array has to start at zero: each call rewrites the plan
  *    and resets the counters before the kernel reads them.  Calls of at most
  *    PERSONA_SMALL_MAX_ROWS rows run the decode-sized kernel and do not

@@ -3,7 +3,9 @@
 //
 // The array is a file-scope __device__ variable, one copy per device, loaded
 // with the library's device code.  Its device address is looked up once per
-// device (cudaGetSymbolAddress with that device current) and then handed to
+// device, by the first call on that device (cudaGetSymbolAddress with that
+// device current; make that first call before any stream capture begins),
+// and then handed to
 // the fused op as its workspace: above PERSONA_SMALL_MAX_ROWS rows the plan
 // kernel writes the row grouping there and the split kernel keeps its
 // partial sums and counters there.  At up to PERSONA_SMALL_MAX_ROWS rows
