@@ -5,10 +5,9 @@
 // with the library's device code.  Its device address is looked up once per
 // device, by the first call on that device (cudaGetSymbolAddress with that
 // device current; make that first call before any stream capture begins),
-// and then handed to
-// the fused op as its workspace: above PERSONA_SMALL_MAX_ROWS rows the plan
-// kernel writes the row grouping there and the split kernel keeps its
-// partial sums and counters there.  At up to PERSONA_SMALL_MAX_ROWS rows
+// and then handed to the fused op as its workspace: above
+// PERSONA_SMALL_MAX_ROWS rows the plan kernel writes the row grouping there
+// and the split kernel keeps its partial sums and counters there.  At up to PERSONA_SMALL_MAX_ROWS rows
 // the decode-sized kernel runs, which needs no plan, so such calls neither
 // read nor write the array.  Nothing here calls cudaMalloc / cudaFree or any
 // allocating routine.
