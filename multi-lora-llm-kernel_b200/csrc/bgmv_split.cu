@@ -9,10 +9,11 @@
 // nes N-slices; the unit list is [all shrink slices, problem by problem,
 // item by item] then [all expand slices, same order].  Slice counts are
 // chosen on the device from the item count so that each pipeline gets 8
-// (few items) to 24 (many items) units: a decode batch of 8 adapters
-// spreads over the whole GPU, a batch of ~150 adapters leaves no pipeline
-// streaming a second whole adapter while others idle, and the seven
-// projections of a layer fill each other's tails.
+// (few items) to 24 (many items) units, none of them shorter than about
+// kMinUnitStages (one problem: kMinUnitStagesOne) stages on average: a
+// decode batch of 8 adapters spreads over the whole GPU, a batch of ~150
+// adapters leaves no pipeline streaming a second whole adapter while others
+// idle, and the seven projections of a layer fill each other's tails.
 //
 // Scheduling.  Persistent pipelines claim units in list order from a
 // device-wide counter.  Every shrink unit precedes every expand unit in claim
@@ -55,6 +56,19 @@ constexpr int kUnitRing = 4;
 constexpr int kUnitsPerCta = 8;       // units per pipeline, few items
 constexpr int kUnitsPerCtaMany = 24;  // units per pipeline, kManyItems items or more
 constexpr int kManyItems = 64;
+// An item's units average at least this many stages (launches of several
+// problems / of one problem).  Without a floor a launch with few items per
+// pipeline (one projection of a 512-row batch: 139 items for 296 pipelines)
+// cut gate's expand into 4-stage units, each paying a unit's start.
+// Measured on that batch: the 7-projection launch takes 286.0 us with a
+// floor of 16 (288.5 with 8 or none); the seven projections launched one at
+// a time take 498.7 us in all with 8, 519.5 with 16, 565.5 with none.  A
+// launch of several problems drops the floor when it would leave fewer than
+// kMinUnitsPerPipe units per pipeline: the shard of one of 8 GPUs (about 70
+// items) took 158.8 us with the floor, 150.7 without it.
+constexpr int kMinUnitStages = 16;
+constexpr int kMinUnitStagesOne = 8;
+constexpr int kMinUnitsPerPipe = 10;
 enum : int { kUnitEnd = 0, kUnitShrink = 1, kUnitExpand = 2 };
 
 constexpr int kGroups = 2;
@@ -178,9 +192,19 @@ __device__ __noinline__ void plan_units(SplitShared& sh, int K, int N, int n_box
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) work += __shfl_xor_sync(0xffffffffu, work, off);
   int ks_st = 0, es_st = 0, nks = 0, nes = 0;
+  int per_item = 1, per_floor = 1;
   if (mine) {
     const long long budget = static_cast<long long>(upc) * pipes * (kst + nst) / (work > 0 ? work : 1);
-    const int per_item = max(1, static_cast<int>((budget + items - 1) / items));
+    const int min_st = P > 1 ? kMinUnitStages : kMinUnitStagesOne;
+    per_item = max(1, static_cast<int>((budget + items - 1) / items));
+    per_floor = max(1, min(per_item, (kst + nst) / min_st));
+  }
+  // units the floor would leave, over all problems
+  long long u_floor = mine ? static_cast<long long>(n_items) * per_floor : 0;
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) u_floor += __shfl_xor_sync(0xffffffffu, u_floor, off);
+  if (P == 1 || u_floor >= static_cast<long long>(kMinUnitsPerPipe) * pipes) per_item = per_floor;
+  if (mine) {
     int n1 = 1, n2 = 1;
     if (shrink && expand) {
       n1 = max(1, (per_item * kst + (kst + nst) / 2) / max(1, kst + nst));
