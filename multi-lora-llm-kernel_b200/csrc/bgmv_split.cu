@@ -64,11 +64,13 @@ constexpr int kManyItems = 64;
 // floor of 16 (288.5 with 8 or none); the seven projections launched one at
 // a time take 498.7 us in all with 8, 519.5 with 16, 565.5 with none.  A
 // launch of several problems drops the floor when it would leave fewer than
-// kMinUnitsPerPipe units per pipeline: the shard of one of 8 GPUs (about 70
-// items) took 158.8 us with the floor, 150.7 without it.
+// kMinUnitsPerPipe units per pipeline: the shard of one of 8 GPUs (51 items,
+// already sliced coarsely) took 158.8 us with the floor and 150.7 without
+// it, while a shard of one of 4 GPUs (70 items) took 173.3 with it and 179.0
+// without.
 constexpr int kMinUnitStages = 16;
 constexpr int kMinUnitStagesOne = 8;
-constexpr int kMinUnitsPerPipe = 10;
+constexpr int kMinUnitsPerPipe = 8;
 enum : int { kUnitEnd = 0, kUnitShrink = 1, kUnitExpand = 2 };
 
 constexpr int kGroups = 2;
