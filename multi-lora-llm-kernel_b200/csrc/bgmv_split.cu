@@ -9,7 +9,7 @@
 // nes N-slices; the unit list is [all shrink slices, problem by problem,
 // item by item] then [all expand slices, same order].  Slice counts are
 // chosen on the device from the item count so that each pipeline gets 8
-// (few items) to 24 (many items) units, none of them shorter than about
+// (few items) to 24 (many items: items / 4) units, none shorter than about
 // kMinUnitStages (one problem: kMinUnitStagesOne) stages on average: a
 // decode batch of 8 adapters spreads over the whole GPU, a batch of ~150
 // adapters leaves no pipeline streaming a second whole adapter while others
@@ -53,9 +53,13 @@ namespace persona {
 namespace {
 
 constexpr int kUnitRing = 4;
+// Units per pipeline: items / kItemsPerUnitStep, between these bounds.
+// Measured on 7-projection launches: 128 rows over 8 adapters 65.8 us at 8
+// units (67.0 at 12); an 8-GPU rank's 51 items 146.5 us at 12 (150.5 at 8);
+// the 1-GPU batch's 139 items best at 24.
 constexpr int kUnitsPerCta = 8;       // units per pipeline, few items
-constexpr int kUnitsPerCtaMany = 24;  // units per pipeline, kManyItems items or more
-constexpr int kManyItems = 64;
+constexpr int kUnitsPerCtaMany = 24;  // units per pipeline, many items
+constexpr int kItemsPerUnitStep = 4;
 // An item's units average at least this many stages (launches of several
 // problems / of one problem).  Without a floor a launch with few items per
 // pipeline (one projection of a 512-row batch: 139 items for 296 pipelines)
@@ -182,7 +186,8 @@ __device__ __noinline__ void plan_units(SplitShared& sh, int K, int N, int n_box
   // Many items (large batches): small units, so the tail stays short.  Few
   // items (decode): fewer, larger units, so the latency chain shrink slice ->
   // finisher -> expand slice has fewer links per item.
-  const int upc = units_per_cta > 0 ? units_per_cta : n_items >= kManyItems ? kUnitsPerCtaMany : kUnitsPerCta;
+  const int upc = units_per_cta > 0 ? units_per_cta
+                                    : min(kUnitsPerCtaMany, max(kUnitsPerCta, n_items / kItemsPerUnitStep));
   const bool mine = lane < P;
   int kst = 0, nst = 0, stage_rows = 0;
   if (mine) {
