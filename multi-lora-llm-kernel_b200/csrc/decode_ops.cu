@@ -210,35 +210,6 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attention_kernel(
   asm volatile("griddepcontrol.launch_dependents;");
   const int b = blockIdx.x, kh = blockIdx.y, tid = threadIdx.x;
   const int G = Hq / Hkv;
-  if (rope.pos != nullptr && rank == 0) {
-    const int pos = *rope.pos;
-    if (pos >= 0 && pos < L) {
-      const int j = tid & 63;
-      const float inv_freq = exp2f(-rope.log2_theta * static_cast<float>(2 * j) / static_cast<float>(D));
-      float sn, cs;
-      sincosf(static_cast<float>(pos) * inv_freq, &sn, &cs);
-      const __half c = __float2half_rn(cs), s = __float2half_rn(sn);
-      // heads 0 .. G - 1: this kv head's query heads; head G: its k
-      for (int hh = tid >> 6; hh <= G; hh += kAttnThreads / 64) {
-        __half o1, o2;
-        if (hh < G) {
-          rope_pair(rope.q + (static_cast<int64_t>(b) * Hq + kh * G + hh) * D, j, c, s, o1, o2);
-        } else {
-          rope_pair(rope.k + (static_cast<int64_t>(b) * Hkv + kh) * D, j, c, s, o1, o2);
-          const int64_t dst = ((static_cast<int64_t>(b) * Hkv + kh) * L + pos) * D;
-          const __half* vr = rope.v + (static_cast<int64_t>(b) * Hkv + kh) * D;
-          rope.kc[dst + j] = o1;
-          rope.kc[dst + j + 64] = o2;
-          rope.vc[dst + j] = vr[j];
-          rope.vc[dst + j + 64] = vr[j + 64];
-        }
-      }
-    }
-    __threadfence();
-  }
-  // the rotated q and the new cache row, written by rank 0, are read below
-  // by every CTA of the cluster (release / acquire at cluster scope)
-  if (rope.pos != nullptr) cluster.sync();
   const int len = min(*len_ptr, L);
   const int chunk = (len + P - 1) / P;
   const int p0 = min(len, rank * chunk), p1 = min(len, p0 + chunk);
@@ -248,8 +219,45 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attention_kernel(
   float* qs = part + 8 * G * D;   // [G][D]
   float* accs = qs + G * D;       // [G][D] this range's unnormalised P V
   __shared__ float s_m[8], s_l[8];
-  for (int i = tid; i < G * D; i += kAttnThreads)
-    qs[i] = __half2float(q[(static_cast<int64_t>(b) * Hq + kh * G) * D + i]);
+  // With a position: every CTA rotates this kv head's query heads itself
+  // (the rotary kernel's half arithmetic), and the CTA whose range holds the
+  // position (rank 0 if none does) rotates k and writes the new cache row,
+  // which only that CTA reads back.  So no CTA waits for another before
+  // scoring; rank 0 writes the rotated q back once every CTA of the cluster
+  // has read the original (after the cluster barrier below).
+  const int pos = rope.pos != nullptr ? *rope.pos : -1;
+  const bool rot = rope.pos != nullptr && pos >= 0 && pos < L;
+  const int owner = !rot ? -1 : pos < len ? pos / chunk : 0;
+  const __half* qg = q + (static_cast<int64_t>(b) * Hq + kh * G) * D;
+  if (rot) {
+    for (int i = tid; i < G * 64; i += kAttnThreads) {
+      const int h = i >> 6, j = i & 63;
+      const float inv_freq = exp2f(-rope.log2_theta * static_cast<float>(2 * j) / static_cast<float>(D));
+      float sn, cs;
+      sincosf(static_cast<float>(pos) * inv_freq, &sn, &cs);
+      const __half c = __float2half_rn(cs), sv = __float2half_rn(sn);
+      const __half x1 = qg[h * D + j], x2 = qg[h * D + j + 64];
+      qs[h * D + j] = __half2float(__hsub(__hmul(x1, c), __hmul(x2, sv)));
+      qs[h * D + j + 64] = __half2float(__hadd(__hmul(x2, c), __hmul(x1, sv)));
+    }
+    if (rank == owner && tid < 64) {
+      const int j = tid;
+      const float inv_freq = exp2f(-rope.log2_theta * static_cast<float>(2 * j) / static_cast<float>(D));
+      float sn, cs;
+      sincosf(static_cast<float>(pos) * inv_freq, &sn, &cs);
+      const __half c = __float2half_rn(cs), sv = __float2half_rn(sn);
+      __half o1, o2;
+      rope_pair(rope.k + (static_cast<int64_t>(b) * Hkv + kh) * D, j, c, sv, o1, o2);
+      const int64_t dst = ((static_cast<int64_t>(b) * Hkv + kh) * L + pos) * D;
+      const __half* vr = rope.v + (static_cast<int64_t>(b) * Hkv + kh) * D;
+      rope.kc[dst + j] = o1;
+      rope.kc[dst + j + 64] = o2;
+      rope.vc[dst + j] = vr[j];
+      rope.vc[dst + j + 64] = vr[j + 64];
+    }
+  } else {
+    for (int i = tid; i < G * D; i += kAttnThreads) qs[i] = __half2float(qg[i]);
+  }
   __syncthreads();
   const __half* kb = kc + (static_cast<int64_t>(b) * Hkv + kh) * L * D;
   const __half* vb = vc + (static_cast<int64_t>(b) * Hkv + kh) * L * D;
@@ -344,8 +352,12 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attention_kernel(
     for (int g = 0; g < 8; ++g) sum += part[g * G * D + i];
     accs[i] = sum;
   }
-  // every range's statistics and P V are in its CTA's shared memory
+  // every range's statistics and P V are in its CTA's shared memory, and
+  // every CTA has read the original q
   cluster.sync();
+  if (rot && rank == 0)
+    for (int i = tid; i < G * D; i += kAttnThreads)
+      rope.q[(static_cast<int64_t>(b) * Hq + kh * G) * D + i] = __float2half_rn(qs[i]);
   // combine the ranges, in rank order: this CTA writes outputs
   // [rank * G * D / P, (rank + 1) * G * D / P)
   const int o0 = rank * G * D / P, o1 = (rank + 1) * G * D / P;
