@@ -111,8 +111,12 @@ __global__ void __launch_bounds__(kSmallThreads) bgmv_small_kernel(const SmallAr
     for (int c = 0; c < kSmallCluster; ++c) v += cluster.map_shared_rank(v_part, c)[tid];
     v_all[tid] = v;
   }
-  // no CTA may leave (and drop its shared memory) while another still reads it
-  cluster.sync();
+  // This CTA is done with the other CTAs' partials: it says so now and waits
+  // for the others only before it exits (no CTA may leave, dropping its
+  // shared memory, while another still reads it), so the expand below runs
+  // inside that barrier instead of after it.
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+  __syncthreads();  // v_all complete for every thread of the CTA
   float v[R];
 #pragma unroll
   for (int r = 0; r < R; ++r) v[r] = v_all[r];
@@ -142,6 +146,7 @@ __global__ void __launch_bounds__(kSmallThreads) bgmv_small_kernel(const SmallAr
     else
       yr[n] = Cvt<DT>::from1(Cvt<DT>::to1(yo) + acc);
   }
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
 template <typename DT, int R>
