@@ -798,12 +798,13 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
           float* part = wv.parts + static_cast<int64_t>(gg.p_base + item * gg.nks + slice) * kPartFloats;
           for (int e = tid; e < E; e += kConsumers) part[e] = sm.pv[e];
           named_sync(bar_cons, kConsumers);
-          // One cumulative fence after the barrier orders every consumer's
-          // partial stores before the count.
+          // One acquire-release count after the barrier: its release side
+          // (cumulative) orders every consumer's partial stores before it, its
+          // acquire side the other slices' partials before the finisher's reads.
           if (tid == 0) {
-            __threadfence();
-            *sm.flag = atomicAdd(s_cnt, 1) == gg.nks - 1;
-            if (*sm.flag) __threadfence();  // acquire side: the other slices' partials
+            int old;
+            asm volatile("atom.add.acq_rel.gpu.global.s32 %0, [%1], 1;" : "=r"(old) : "l"(s_cnt) : "memory");
+            *sm.flag = old == gg.nks - 1;
           }
           named_sync(bar_cons, kConsumers);
           finisher = *sm.flag != 0;
@@ -839,7 +840,7 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
           named_sync(bar_cons, kConsumers);
           if (tid == 0) {
             if (gg.nks > 1) *s_cnt = 0;  // every slice has counted: ready for the next launch
-            __threadfence();
+            // the release store orders the CTA's v stores (cumulative over the barrier)
             if (MODE != kModeShrink) st_release(wv.ready + prob * tpad + item, epoch);
           }
         }
